@@ -1,0 +1,278 @@
+// ref_harness.cpp - test/benchmark driver for the REFERENCE ggml CPU backend.
+//
+// TEST INFRASTRUCTURE ONLY.  This file is linked (by oracle/Makefile) against the
+// reference's own ggml sources compiled from the reference tree (vendored llama.cpp
+// ggml 1b70350c9).  It builds the same ggml graphs QuestWend builds for the MoE hot path
+// and runs them on the ggml CPU backend, so the tests can compare the CUDA path with
+// the reference's own arithmetic and bench.py can time the reference CPU path.
+// Nothing in the product links this file.
+//
+// Graphs mirrored (reference core/runtime.cpp):
+//   * route_experts        runtime.cpp:2693-2734  softmax -> argsort_top_k -> get_rows ->
+//                                                sum_rows -> clamp(6.1035e-5) -> div
+//   * build_moe            runtime.cpp:2743-2816  router mul_mat, 3x mul_mat_id,
+//                                                swiglu_split, weighted reduce
+//                                                (T=1: mul_mat(cont(transpose)), T>1: mul + adds)
+//   * in-graph slot remap  runtime.cpp:2769-2778  get_rows(g2s I32 table, selected)
+// Ops exercised: ggml_mul_mat_id (ggml.c:3413), ggml_get_rows (ggml.c:3975),
+// ggml_argsort_top_k (ggml.c:5462), ggml_swiglu_split (ggml.c:3082).
+#include "ggml.h"
+#include "ggml-alloc.h"
+#include "ggml-backend.h"
+#include "ggml-cpu.h"
+
+#include <chrono>
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+namespace {
+
+ggml_backend_t g_cpu = nullptr;
+int g_threads = 1;
+
+ggml_backend_t cpu() {
+    if (!g_cpu) {
+        g_cpu = ggml_backend_cpu_init();
+        ggml_backend_cpu_set_n_threads(g_cpu, g_threads);
+    }
+    return g_cpu;
+}
+
+struct Graph {
+    ggml_context * ctx = nullptr;
+    ggml_backend_buffer_t buf = nullptr;
+    std::vector<ggml_backend_buffer_t> user_bufs;
+    ggml_cgraph * gf = nullptr;
+
+    explicit Graph(size_t n_tensors = 512) {
+        ggml_init_params p = { ggml_tensor_overhead() * n_tensors + ggml_graph_overhead_custom(4096, false), nullptr, true };
+        ctx = ggml_init(p);
+        gf = ggml_new_graph_custom(ctx, 4096, false);
+    }
+    ~Graph() {
+        if (buf) ggml_backend_buffer_free(buf);
+        for (auto b : user_bufs) ggml_backend_buffer_free(b);
+        if (ctx) ggml_free(ctx);
+    }
+    // wrap caller memory (weights) without copying when it meets ggml's 32-byte tensor
+    // alignment; otherwise the tensor is allocated with the rest and copied in
+    std::vector<std::pair<ggml_tensor *, const void *>> copies;
+    void bind(ggml_tensor * t, const void * ptr) {
+        if (((uintptr_t) ptr) % 32 != 0) { copies.emplace_back(t, ptr); return; }
+        ggml_backend_buffer_t b = ggml_backend_cpu_buffer_from_ptr(const_cast<void *>(ptr), ggml_nbytes(t));
+        ggml_backend_tensor_alloc(b, t, const_cast<void *>(ptr));
+        user_bufs.push_back(b);
+    }
+    void alloc_rest() {
+        buf = ggml_backend_alloc_ctx_tensors(ctx, cpu());
+        for (auto & c : copies) ggml_backend_tensor_set(c.first, c.second, 0, ggml_nbytes(c.first));
+    }
+    double compute(int iters) {
+        ggml_backend_graph_compute(cpu(), gf);  // warm-up (also the result for iters==0)
+        if (iters <= 0) return 0.0;
+        auto t0 = std::chrono::steady_clock::now();
+        for (int i = 0; i < iters; ++i) ggml_backend_graph_compute(cpu(), gf);
+        auto t1 = std::chrono::steady_clock::now();
+        return std::chrono::duration<double, std::milli>(t1 - t0).count() / iters;
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+void qref_set_threads(int n) {
+    g_threads = n > 0 ? n : 1;
+    if (g_cpu) ggml_backend_cpu_set_n_threads(g_cpu, g_threads);
+}
+
+size_t qref_row_size(int type, int64_t n) { return ggml_row_size((ggml_type) type, n); }
+
+// Weight creation exactly as a GGUF converter would: ggml_quantize_chunk (ggml.c:8079),
+// no importance matrix (=> the *_ref quantizers).
+size_t qref_quantize(int type, const float * src, void * dst, int64_t nrow, int64_t n_per_row) {
+    ggml_quantize_init((ggml_type) type);
+    return ggml_quantize_chunk((ggml_type) type, src, dst, 0, nrow, n_per_row, nullptr);
+}
+
+// The CPU backend's activation quantizer: type_traits_cpu[vec_dot_type].from_float
+// (ggml-cpu.c:1609-1644 calls it on src1 rows).  Q8_K -> quantize_row_q8_K,
+// Q8_0 -> the x86 SIMD quantize_row_q8_0 (arch/x86/quants.c:302).
+int qref_from_float(int type, const float * x, void * y, int64_t nrow, int64_t k) {
+    const ggml_type_traits_cpu * tr = ggml_get_type_traits_cpu((ggml_type) type);
+    if (!tr || !tr->from_float) return -1;
+    const size_t rs = ggml_row_size((ggml_type) type, k);
+    for (int64_t r = 0; r < nrow; ++r) tr->from_float(x + r * k, (char *) y + r * rs, k);
+    return 0;
+}
+
+// Plain dequantize (ggml_get_type_traits(type)->to_float).
+int qref_to_float(int type, const void * x, float * y, int64_t nrow, int64_t k) {
+    const ggml_type_traits * tr = ggml_get_type_traits((ggml_type) type);
+    if (!tr || !tr->to_float) return -1;
+    const size_t rs = ggml_row_size((ggml_type) type, k);
+    for (int64_t r = 0; r < nrow; ++r) tr->to_float((const char *) x + r * rs, y + r * k, k);
+    return 0;
+}
+
+// dst[M, n_used, T] = mul_mat_id(as[K, M, n_as], b[K, n_b, T], ids[n_used, T])
+// ids_stride: elements between consecutive tokens in ids (>= n_used; a strided view
+// like argsort_top_k's when > n_used).
+double qref_mul_mat_id(int type, const void * as, int64_t K, int64_t M, int64_t n_as,
+                       const float * b, int64_t n_b, int64_t T,
+                       const int32_t * ids, int64_t n_used, int64_t ids_stride,
+                       float * dst, int iters) {
+    Graph g;
+    ggml_tensor * tas  = ggml_new_tensor_3d(g.ctx, (ggml_type) type, K, M, n_as);
+    ggml_tensor * tb   = ggml_new_tensor_3d(g.ctx, GGML_TYPE_F32, K, n_b, T);
+    ggml_tensor * tidf = ggml_new_tensor_2d(g.ctx, GGML_TYPE_I32, ids_stride, T);
+    ggml_tensor * tid  = ggml_view_2d(g.ctx, tidf, n_used, T, tidf->nb[1], 0);
+    ggml_tensor * out  = ggml_mul_mat_id(g.ctx, tas, tb, tid);
+    ggml_build_forward_expand(g.gf, out);
+    g.bind(tas, as);
+    g.alloc_rest();
+    ggml_backend_tensor_set(tb, b, 0, ggml_nbytes(tb));
+    ggml_backend_tensor_set(tidf, ids, 0, ggml_nbytes(tidf));
+    double ms = g.compute(iters);
+    ggml_backend_tensor_get(out, dst, 0, ggml_nbytes(out));
+    return ms;
+}
+
+// dst[ne0, n] = get_rows(src[ne0, nrows] of `type`, idx[n]); dst type F32 (or I32 for I32 src)
+double qref_get_rows(int type, const void * src, int64_t ne0, int64_t nrows,
+                     const int32_t * idx, int64_t n, void * dst, int iters) {
+    Graph g;
+    ggml_tensor * ts = ggml_new_tensor_2d(g.ctx, (ggml_type) type, ne0, nrows);
+    ggml_tensor * ti = ggml_new_tensor_1d(g.ctx, GGML_TYPE_I32, n);
+    ggml_tensor * out = ggml_get_rows(g.ctx, ts, ti);
+    ggml_build_forward_expand(g.gf, out);
+    g.bind(ts, src);
+    g.alloc_rest();
+    ggml_backend_tensor_set(ti, idx, 0, ggml_nbytes(ti));
+    double ms = g.compute(iters);
+    ggml_backend_tensor_get(out, dst, 0, ggml_nbytes(out));
+    return ms;
+}
+
+// route_experts (runtime.cpp:2693-2734) on given logits [E, T]:
+// selected[n_used, T] i32, weights[n_used, T] f32 (renormalised when norm != 0).
+double qref_route(const float * logits, int64_t E, int64_t T, int64_t n_used, int norm,
+                  float scale, const float * mask, int32_t * selected, float * weights, int iters) {
+    Graph g;
+    ggml_tensor * tl = ggml_new_tensor_2d(g.ctx, GGML_TYPE_F32, E, T);
+    ggml_tensor * tm = mask ? ggml_new_tensor_2d(g.ctx, GGML_TYPE_F32, E, T) : nullptr;
+    ggml_tensor * lg = tm ? ggml_add(g.ctx, tl, tm) : tl;
+    ggml_tensor * probs = ggml_soft_max(g.ctx, lg);
+    ggml_tensor * sel = ggml_argsort_top_k(g.ctx, probs, n_used);
+    ggml_tensor * p3 = ggml_reshape_3d(g.ctx, probs, 1, E, T);
+    ggml_tensor * w = ggml_get_rows(g.ctx, p3, sel);
+    if (norm) {
+        w = ggml_reshape_2d(g.ctx, w, n_used, T);
+        ggml_tensor * ws = ggml_sum_rows(g.ctx, w);
+        ws = ggml_clamp(g.ctx, ws, 6.103515625e-5f, INFINITY);
+        w = ggml_div(g.ctx, w, ws);
+        w = ggml_reshape_3d(g.ctx, w, 1, n_used, T);
+    }
+    if (scale != 0.0f && scale != 1.0f) w = ggml_scale(g.ctx, w, scale);
+    ggml_tensor * selc = ggml_cont(g.ctx, sel);
+    ggml_build_forward_expand(g.gf, w);
+    ggml_build_forward_expand(g.gf, selc);
+    g.alloc_rest();
+    ggml_backend_tensor_set(tl, logits, 0, ggml_nbytes(tl));
+    if (tm) ggml_backend_tensor_set(tm, mask, 0, ggml_nbytes(tm));
+    double ms = g.compute(iters);
+    ggml_backend_tensor_get(selc, selected, 0, ggml_nbytes(selc));
+    ggml_backend_tensor_get(w, weights, 0, ggml_nbytes(w));
+    return ms;
+}
+
+// One MoE FFN layer as build_moe emits it (runtime.cpp:2743-2816), resident branch
+// (expert ids used directly) or, when g2s != NULL, the slot-remap branch where each of
+// gate/up/down gathers its slot ids through an I32 [1, E] table (runtime.cpp:2769-2778)
+// and the expert tensors are slot pools [.., .., n_slots].
+//   x        [H, T] f32            router_w [H, E] f32
+//   gate/up  [H, F, n_mat] (type_gu)   down [F, H, n_mat] (type_d)
+//   g2s      3 x E int32 (gate, up, down tables) or NULL
+// outputs: out [H, T], selected [n_used, T], weights [n_used, T]; optional act [F, n_used, T].
+double qref_moe_layer(const float * x, int64_t H, int64_t T,
+                      const float * router_w, int64_t E, int64_t n_used,
+                      int type_gu, const void * gate, const void * up,
+                      int type_d, const void * down, int64_t F, int64_t n_mat,
+                      const int32_t * g2s, const float * mask,
+                      float * out, int32_t * selected, float * weights, float * act_out,
+                      int iters) {
+    Graph g(1024);
+    ggml_context * ctx = g.ctx;
+    ggml_tensor * tx  = ggml_new_tensor_2d(ctx, GGML_TYPE_F32, H, T);
+    ggml_tensor * trw = ggml_new_tensor_2d(ctx, GGML_TYPE_F32, H, E);
+    ggml_tensor * tg  = ggml_new_tensor_3d(ctx, (ggml_type) type_gu, H, F, n_mat);
+    ggml_tensor * tu  = ggml_new_tensor_3d(ctx, (ggml_type) type_gu, H, F, n_mat);
+    ggml_tensor * td  = ggml_new_tensor_3d(ctx, (ggml_type) type_d, F, H, n_mat);
+    ggml_tensor * tm  = mask ? ggml_new_tensor_2d(ctx, GGML_TYPE_F32, E, T) : nullptr;
+    ggml_tensor * tg2s = g2s ? ggml_new_tensor_3d(ctx, GGML_TYPE_I32, 1, E, 3) : nullptr;
+
+    ggml_tensor * logits = ggml_mul_mat(ctx, trw, tx);  // [E, T]
+    if (tm) logits = ggml_add(ctx, logits, tm);
+    ggml_tensor * probs = ggml_soft_max(ctx, logits);
+    ggml_tensor * sel = ggml_argsort_top_k(ctx, probs, n_used);
+    ggml_tensor * p3 = ggml_reshape_3d(ctx, probs, 1, E, T);
+    ggml_tensor * w = ggml_get_rows(ctx, p3, sel);
+    w = ggml_reshape_2d(ctx, w, n_used, T);
+    ggml_tensor * ws = ggml_sum_rows(ctx, w);
+    ws = ggml_clamp(ctx, ws, 6.103515625e-5f, INFINITY);
+    w = ggml_div(ctx, w, ws);
+    w = ggml_reshape_3d(ctx, w, 1, n_used, T);
+    ggml_build_forward_expand(g.gf, w);
+
+    ggml_tensor *ids_g = sel, *ids_u = sel, *ids_d = sel;
+    if (tg2s) {
+        auto remap = [&](int role) {
+            ggml_tensor * tab = ggml_view_2d(ctx, tg2s, 1, E, tg2s->nb[1], (size_t) role * tg2s->nb[2]);
+            ggml_tensor * s = ggml_get_rows(ctx, tab, sel);  // [1, n_used, T] i32
+            return ggml_reshape_2d(ctx, s, n_used, T);
+        };
+        ids_g = remap(0); ids_u = remap(1); ids_d = remap(2);
+    }
+    ggml_tensor * x3 = ggml_reshape_3d(ctx, tx, H, 1, T);
+    ggml_tensor * tup   = ggml_mul_mat_id(ctx, tu, x3, ids_u);
+    ggml_tensor * tgate = ggml_mul_mat_id(ctx, tg, x3, ids_g);
+    ggml_tensor * act = ggml_swiglu_split(ctx, tgate, tup);  // [F, n_used, T]
+    ggml_tensor * experts = ggml_mul_mat_id(ctx, td, act, ids_d);  // [H, n_used, T]
+    ggml_tensor * moe;
+    if (T == 1) {
+        ggml_tensor * et = ggml_cont(ctx, ggml_transpose(ctx, ggml_reshape_2d(ctx, experts, H, n_used)));
+        ggml_tensor * w2 = ggml_reshape_2d(ctx, w, n_used, 1);
+        moe = ggml_mul_mat(ctx, et, w2);
+    } else {
+        experts = ggml_mul(ctx, experts, w);
+        ggml_build_forward_expand(g.gf, experts);
+        moe = ggml_view_2d(ctx, experts, H, T, experts->nb[2], 0);
+        for (int64_t i = 1; i < n_used; ++i) {
+            ggml_tensor * v = ggml_view_2d(ctx, experts, H, T, experts->nb[2], (size_t) i * experts->nb[1]);
+            moe = ggml_add(ctx, moe, v);
+        }
+        if (n_used == 1) moe = ggml_cont(ctx, moe);
+    }
+    ggml_tensor * selc = ggml_cont(ctx, sel);
+    ggml_build_forward_expand(g.gf, moe);
+    ggml_build_forward_expand(g.gf, selc);
+    if (act_out) ggml_build_forward_expand(g.gf, act);
+
+    g.bind(tg, gate); g.bind(tu, up); g.bind(td, down);
+    g.alloc_rest();
+    ggml_backend_tensor_set(tx, x, 0, ggml_nbytes(tx));
+    ggml_backend_tensor_set(trw, router_w, 0, ggml_nbytes(trw));
+    if (tm) ggml_backend_tensor_set(tm, mask, 0, ggml_nbytes(tm));
+    if (tg2s) ggml_backend_tensor_set(tg2s, g2s, 0, ggml_nbytes(tg2s));
+    double ms = g.compute(iters);
+    ggml_backend_tensor_get(moe, out, 0, ggml_nbytes(moe));
+    if (selected) ggml_backend_tensor_get(selc, selected, 0, ggml_nbytes(selc));
+    if (weights) ggml_backend_tensor_get(w, weights, 0, ggml_nbytes(w));
+    if (act_out) ggml_backend_tensor_get(act, act_out, 0, ggml_nbytes(act));
+    return ms;
+}
+
+}  // extern "C"
