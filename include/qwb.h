@@ -1,0 +1,213 @@
+/* qwb.h - C ABI of the B200 (sm_100a) kernel library for QuestWend's quantized MoE
+ * expert hot path.
+ *
+ * What this library replaces.  QuestWend builds ggml graphs whose MoE nodes are
+ * GGML_OP_MUL_MAT_ID (ggml.c:3401-3437 op contract) on Q4_K / Q6_K / Q8_0 expert weights
+ * and GGML_OP_GET_ROWS (ggml.c:3975-3996), and hands them to a ggml backend through the
+ * backend C ABI (ggml-backend-impl.h:122-247).  The entry points below are what a ggml
+ * backend for B200 binds from its graph_compute: each names the reference function whose
+ * result it reproduces (paths relative to the reference's third_party/ggml/src unless
+ * they start with core/).  The ggml backend shim that registers these with ggml is
+ * include/qwb_ggml_backend.h.
+ *
+ * Conventions
+ *   - Plain pointers and sizes; tensors are described by qwb_tensor, a copy of the
+ *     fields of struct ggml_tensor the kernels need (type, ne[4], nb[4] in bytes, data).
+ *     Type ids are ggml's enum ggml_type values.
+ *   - Every call is asynchronous on the given cudaStream_t (pass 0 for the legacy
+ *     default stream), performs no host synchronisation, no device allocation and no
+ *     host read-back of device data, so it can be captured in a CUDA graph.
+ *   - Scratch memory is caller-owned ("workspace"); sizes come from the *_workspace_size
+ *     queries.  Workspaces must be 256-byte aligned.
+ *   - Host-detectable errors (bad type, shape, stride, alignment, workspace) return a
+ *     qwb_status and launch nothing.  Data-dependent errors found on the device (an
+ *     expert / row id out of range) never fault: the kernel skips the access, writes
+ *     zeros for the affected outputs and records the error in an optional device-side
+ *     qwb_status_block, read back with qwb_status_block_read.  (The reference's CPU
+ *     backend aborts on such ids, ggml-cpu.c:1659 / ops.cpp get_rows asserts.)
+ */
+#ifndef QWB_H
+#define QWB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define QWB_API __declspec(dllexport)
+#else
+#define QWB_API __attribute__((visibility("default")))
+#endif
+
+typedef struct CUstream_st *qwb_stream_t; /* == cudaStream_t */
+
+#define QWB_ABI_VERSION 1
+
+typedef enum qwb_status {
+    QWB_OK = 0,
+    QWB_ERR_INVALID_ARG = 1,      /* null pointer, negative size */
+    QWB_ERR_UNSUPPORTED_TYPE = 2, /* tensor type not handled by this entry point */
+    QWB_ERR_SHAPE = 3,            /* shapes inconsistent with the op contract */
+    QWB_ERR_LAYOUT = 4,           /* unsupported strides (permuted / non-contiguous rows) */
+    QWB_ERR_ALIGNMENT = 5,        /* pointer or row stride not aligned as required */
+    QWB_ERR_WORKSPACE = 6,        /* workspace missing or smaller than required */
+    QWB_ERR_CUDA = 7,             /* a CUDA runtime call failed (launch, attribute) */
+    QWB_ERR_DEVICE = 8,           /* device not sm_100 */
+    QWB_ERR_LIMIT = 9,            /* size beyond a documented maximum */
+} qwb_status;
+
+/* ggml_type values used on this path */
+enum {
+    QWB_TYPE_F32 = 0, QWB_TYPE_F16 = 1, QWB_TYPE_Q8_0 = 8, QWB_TYPE_Q4_K = 12,
+    QWB_TYPE_Q6_K = 14, QWB_TYPE_Q8_K = 15, QWB_TYPE_I32 = 26,
+};
+
+/* A tensor view with ggml semantics: ne[] element counts, nb[] byte strides. */
+typedef struct qwb_tensor {
+    void *data;
+    int32_t type;
+    int32_t reserved;
+    int64_t ne[4];
+    size_t nb[4];
+} qwb_tensor;
+
+/* Device-resident error record.  Allocate it zeroed in device memory; kernels OR flags
+ * into it and keep the first offending value.  It is sticky until reset. */
+typedef struct qwb_status_block {
+    uint32_t flags;       /* QWB_DEVERR_* bits */
+    int32_t bad_value;    /* first offending id / row index seen */
+    uint32_t count;       /* number of offending accesses */
+    uint32_t reserved;
+} qwb_status_block;
+
+#define QWB_DEVERR_ID_RANGE 0x1u      /* mul_mat_id expert/slot id outside [0, n_as) */
+#define QWB_DEVERR_ROW_RANGE 0x2u     /* get_rows index outside [0, nrows) */
+#define QWB_DEVERR_TIMEOUT 0x4u       /* a bounded device wait gave up (copy never landed) */
+
+QWB_API int qwb_abi_version(void);
+QWB_API const char *qwb_status_string(qwb_status s);
+
+/* Synchronises `stream`, copies the block to *out and, when reset != 0, zeroes it. */
+QWB_API qwb_status qwb_status_block_read(qwb_status_block *d_block, qwb_status_block *out,
+                                         int reset, qwb_stream_t stream);
+
+/* ---------------------------------------------------------------- quantizers
+ * Activation quantizers, bit-exact with the reference CPU backend's from_float for the
+ * weight type's vec_dot_type (ggml-cpu.c:1609-1644 applies them to src1 rows).
+ * x: n_rows rows of k floats, row r at x + r*x_row_stride (elements).  y: packed ggml
+ * blocks, row r at y + r*row_size(k).  k % 256 == 0 (Q8_K) / k % 32 == 0 (Q8_0). */
+
+/* replaces quantize_row_q8_K (ggml-cpu/arch/x86/quants.c:505 -> ggml-quants.c:2769-2806) */
+QWB_API qwb_status qwb_quantize_row_q8_K(const float *x, void *y, int64_t n_rows, int64_t k,
+                                         int64_t x_row_stride, qwb_stream_t stream);
+
+#define QWB_Q8_0_CPU 0 /* ggml-cpu/arch/x86/quants.c:302-360: id = 127/amax, round-half-even */
+#define QWB_Q8_0_REF 1 /* ggml-quants.c:276-300 quantize_row_q8_0_ref: id = 1/d, roundf     */
+/* replaces quantize_row_q8_0 (x86 CPU backend) or quantize_row_q8_0_ref */
+QWB_API qwb_status qwb_quantize_row_q8_0(const float *x, void *y, int64_t n_rows, int64_t k,
+                                         int64_t x_row_stride, int variant, qwb_stream_t stream);
+
+/* ----------------------------------------------------------------- GET_ROWS
+ * replaces ggml_compute_forward_get_rows (ggml-cpu/ops.cpp:5371) incl. get_rows_q
+ * (ops.cpp:5204-5240); op contract ggml.c:3975-3996.
+ * src0 [ne0, ne01, ne02, ne03] of Q4_K | Q6_K | Q8_0 | F16 | F32 | I32;
+ * idx  [n, ne11, ne12] I32 (row ids into src0's ne01, broadcast over ne02 like ggml);
+ * dst  [ne0, n, ne11, ne12] F32 (I32 when src0 is I32).  Quantized and F16 rows are
+ * dequantized bit-exactly; F32/I32 rows are copied bit-for-bit. */
+QWB_API qwb_status qwb_get_rows(const qwb_tensor *src0, const qwb_tensor *idx,
+                                const qwb_tensor *dst, qwb_status_block *d_status,
+                                qwb_stream_t stream);
+
+/* --------------------------------------------------------------- MUL_MAT_ID
+ * replaces ggml_compute_forward_mul_mat_id (ggml-cpu/ggml-cpu.c:1554-1736); op contract
+ * ggml.c:3401-3437:
+ *   as  [K, M, n_as]      Q4_K | Q6_K | Q8_0 (n_as may be a slot-pool size, ids slot ids)
+ *   b   [K, n_b, T]       F32, n_used % n_b == 0 (n_b == 1 broadcasts one row per token)
+ *   ids [n_used, T]       I32, may be a strided view (nb[1] != n_used*4)
+ *   dst [M, n_used, T]    F32
+ * dst[:, j, t] = as[:, :, ids[j, t]] . b[:, j % n_b, t], with b quantized exactly as the
+ * CPU backend does (Q8_K for K-quants, Q8_0 CPU variant for Q8_0). */
+QWB_API size_t qwb_mul_mat_id_workspace_size(const qwb_tensor *as, const qwb_tensor *b,
+                                             const qwb_tensor *ids);
+QWB_API qwb_status qwb_mul_mat_id(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor *ids,
+                                  const qwb_tensor *dst, void *workspace, size_t workspace_bytes,
+                                  qwb_status_block *d_status, qwb_stream_t stream);
+
+/* ------------------------------------------------------------ small MoE ops */
+/* replaces the route_experts subgraph (core/runtime.cpp:2693-2734): soft_max
+ * (ops.cpp:5813) -> argsort_top_k (ggml.c:5462) -> get_rows of probs -> sum_rows ->
+ * clamp(6.103515625e-5) -> div -> optional scale.  logits [E, T] f32 rows contiguous;
+ * mask [E, T] f32 or NULL (added to logits first); selected [n_used, T] i32 and
+ * weights [n_used, T] f32, both contiguous.  E <= 512, n_used <= 32. */
+QWB_API qwb_status qwb_moe_route(const float *logits, const float *mask, int64_t E, int64_t T,
+                                 int64_t n_used, int norm, float scale, int32_t *selected,
+                                 float *weights, qwb_stream_t stream);
+
+/* replaces ggml_swiglu_split (ggml.c:3082; ops.cpp:3331-3389): act = silu(gate) * up,
+ * n contiguous floats. */
+QWB_API qwb_status qwb_swiglu(const float *gate, const float *up, float *act, int64_t n,
+                              qwb_stream_t stream);
+
+/* replaces the weighted expert reduction (core/runtime.cpp:2796-2816:
+ * T=1 mul_mat(cont(transpose(experts)), w), T>1 mul + (n_used-1) add):
+ * out[:, t] = sum_j w[j, t] * experts[:, j, t]; experts [H, n_used, T] contiguous. */
+QWB_API qwb_status qwb_moe_weighted_sum(const float *experts, const float *weights, float *out,
+                                        int64_t H, int64_t n_used, int64_t T,
+                                        qwb_stream_t stream);
+
+/* ---------------------------------------------------------- fused MoE layer
+ * replaces the whole build_moe subgraph (core/runtime.cpp:2743-2816, and the cached
+ * fast path's slot remap :2769-2778):
+ *   logits = router_w . x            (F32 mul_mat, :2750)
+ *   selected, weights = route(...)   (as qwb_moe_route, norm on)
+ *   slot_r = g2s[r][selected]        (r = gate, up, down; skipped when g2s == NULL)
+ *   act    = swiglu(gate . x, up . x)  (mul_mat_id on the pools, Q8_K/Q8_0 activations)
+ *   out    = sum_j w_j * (down . act_j) [+ residual]
+ * Weight tensors may be slot pools [K, M, n_slots]. */
+typedef struct qwb_moe_ffn_desc {
+    const float *x;          /* [H, T] f32, contiguous rows */
+    const float *router_w;   /* [H, E] f32 (ggml: ffn_gate_inp), contiguous */
+    const float *mask;       /* [E, T] f32 added to logits, or NULL */
+    const int32_t *g2s;      /* [3][E] i32 expert -> slot tables (gate, up, down), or NULL */
+    qwb_tensor gate;         /* [H, F, n_mat] */
+    qwb_tensor up;           /* [H, F, n_mat] */
+    qwb_tensor down;         /* [F, H, n_mat] */
+    int64_t H, F, E, n_used, T;
+    const float *residual;   /* [H, T] added to out, or NULL */
+    float *out;              /* [H, T] */
+    int32_t *selected;       /* [n_used, T] out (logical expert ids), or NULL */
+    float *weights;          /* [n_used, T] out, or NULL */
+    float *act;              /* [F, n_used, T] out: swiglu(gate, up), the down projection's
+                                input (ggml's "act" node), or NULL */
+} qwb_moe_ffn_desc;
+
+QWB_API size_t qwb_moe_ffn_workspace_size(const qwb_moe_ffn_desc *desc);
+QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *desc, void *workspace, size_t workspace_bytes,
+                               qwb_status_block *d_status, qwb_stream_t stream);
+
+/* ------------------------------------------------------------- profiling hook
+ * Optional per-kernel timing for benchmarks (no counterpart in the reference, whose
+ * QWEN_PROF timers are host wall-clock, core/runtime.cpp:3720).  While enabled,
+ * qwb_moe_ffn records a CUDA event on its stream before its first kernel ("mark" with
+ * tag 0) and after each kernel (tag = QWB_KERNEL_*).  Event records are stream-capture
+ * safe: inside a captured CUDA graph they become event-record nodes and are re-recorded
+ * on every replay, so after a replay qwb_profile_read returns that replay's durations.
+ * Not thread-safe; one profiling session per process. */
+#define QWB_KERNEL_ROUTER 1
+#define QWB_KERNEL_GATE_UP 2
+#define QWB_KERNEL_DOWN 3
+#define QWB_KERNEL_OTHER 4
+QWB_API qwb_status qwb_profile_enable(int max_marks); /* creates the events; 0 disables */
+QWB_API qwb_status qwb_profile_reset(void);           /* next mark is mark 0 */
+QWB_API int qwb_profile_count(void);                  /* marks recorded since reset */
+/* ms[i] = time between mark i and mark i+1, tags[i] = tag of mark i+1, i < n <= count-1.
+ * Synchronises on the last mark. */
+QWB_API qwb_status qwb_profile_read(float *ms, int32_t *tags, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QWB_H */

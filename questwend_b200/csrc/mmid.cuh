@@ -1,0 +1,51 @@
+// mmid.cuh - shared declarations of the MUL_MAT_ID building blocks.
+#pragma once
+
+#include "common.cuh"
+
+namespace qwb {
+
+// Expert-sorted work description written by the index kernel into the workspace.
+struct MmidIndex {
+    int *n_tiles;  // device scalar
+    int *pairs;    // [P] pair ids p = t*n_used + j, grouped by expert
+    int4 *tiles;   // [max_tiles] (expert, first pair, pair count, 0)
+    int max_tiles; // host-side upper bound
+};
+
+struct GemvArgs {
+    const uint8_t *W;        // expert weights [K, M, n_as] (gate when GLU)
+    size_t nb1, nb2;
+    const uint8_t *W2;       // up weights (GLU only)
+    size_t nb1_2, nb2_2;
+    size_t row_bytes;
+    int64_t M, K;
+    Q8Planes act;            // quantized activation rows
+    int act_dstride, act_bstride, act_d_off, act_b_off, act_stride;
+    const int4 *tiles;
+    const int *n_tiles;
+    const int *pairs;
+    int n_used, n_b;
+    float *dst;              // dst[m, j, t] at dst + j*dnb1 + t*dnb2 (bytes) + 4m
+    size_t dnb1, dnb2;
+    int R, n_rb, wstage, stage_bytes;
+    // optional expert -> slot remap (the in-graph get_rows of an I32 [1, E] table,
+    // core/runtime.cpp:2769-2778); slot ids must lie in [0, n_slots)
+    const int32_t *remap, *remap2;
+    int64_t n_slots;
+    qwb_status_block *st;
+};
+
+void gemv_geometry(GemvArgs &a, int NT, bool glu);
+cudaError_t launch_gemv(int type, bool glu, GemvArgs a, int NT, int max_tiles, cudaStream_t s);
+int pick_nt(int64_t pairs, int64_t n_as);
+size_t mmid_index_bytes(int64_t P, int64_t n_as, int NT);
+MmidIndex mmid_index_at(void *base, int64_t P, int64_t n_as, int NT);
+cudaError_t launch_index(const int32_t *ids, int64_t s0, int64_t s1, int n_used, int T, int n_as, int NT,
+                         MmidIndex ix, float *dst, size_t dnb1, size_t dnb2, int64_t M, qwb_status_block *st,
+                         cudaStream_t s);
+
+qwb_status mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor *ids, const qwb_tensor *dst,
+                           void *ws, size_t ws_bytes, qwb_status_block *st, cudaStream_t s);
+
+}  // namespace qwb

@@ -1,0 +1,351 @@
+// moe_ffn.cu - the fused MoE FFN layer (QuestWend's build_moe subgraph) on B200.
+//
+// Reference: core/runtime.cpp:2743-2816 (build_moe), :2769-2778 (in-graph slot remap),
+// :2693-2734 (route_experts).  The chain router mul_mat -> softmax/top-k/renorm ->
+// get_rows(g2s) -> 3x mul_mat_id -> swiglu -> weighted reduce runs as
+//   decode (T == 1), 3 kernels:
+//     router_fused   logits GEMV + x -> Q8 + top-k (last CTA) + GEMV tile list
+//     gemv<GLU>      gate and up rows of each selected expert slot, SwiGLU epilogue
+//     down_decode    act -> Q8 in the prologue (overlapping the weight copies), down
+//                    rows of all selected slots per output row, weighted sum + residual
+//   batched (T > 1): router (+ quantize x), index build, gemv<GLU>, act -> Q8,
+//                    gemv (down, n_b = n_used), weighted sum + residual.
+// Numerics are the reference CPU backend's: Q8_K (or Q8_0-cpu) activations bit-exact,
+// integer sub-block dots exact, fp32 combine (see dot.cuh).
+#include <algorithm>
+
+#include "common.cuh"
+#include "dot.cuh"
+#include "kernels.cuh"
+#include "mmid.cuh"
+#include "quant_dev.cuh"
+#include "route.cuh"
+
+namespace qwb {
+
+struct DownArgs {
+    const uint8_t *W;
+    size_t nb1, nb2, row_bytes;
+    int64_t n_slots, E;
+    const int32_t *remap;      // g2s down table [E] or null
+    const int32_t *selected;   // [n_used] logical expert ids
+    const float *weights;      // [n_used]
+    int n_used;
+    const float *act;          // [n_used][F] f32
+    int64_t F, H;
+    float *out;
+    const float *residual;
+    int kq;
+    int R, n_rb, wspan, act_stride, act_d_off, act_b_off, smem_act;
+    qwb_status_block *st;
+};
+
+template <int TYPE>
+__global__ void __launch_bounds__(128) moe_down_decode_kernel(const DownArgs d) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *bar = (uint64_t *) smem;
+    __shared__ int64_t s_slot[kMaxUsed];
+    __shared__ float s_w[kMaxUsed];
+    uint8_t *act = smem + 128;
+    uint8_t *wbuf = act + d.smem_act;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t per = ceil_div((int64_t) d.n_rb, (int64_t) gridDim.x);
+    const int64_t i0 = (int64_t) blockIdx.x * per, i1 = min((int64_t) d.n_rb, i0 + per);
+    if (i0 >= i1) return;
+
+    if (tid < d.n_used) {
+        const int e = d.selected[tid];
+        int64_t sl = -1;
+        if (e >= 0 && e < d.E) sl = d.remap ? (int64_t) d.remap[e] : e;
+        if (sl < 0 || sl >= d.n_slots) {
+            if (blockIdx.x == 0) report(d.st, QWB_DEVERR_ID_RANGE, e);
+            sl = -1;
+        }
+        s_slot[tid] = sl;
+        s_w[tid] = d.weights[tid];
+    }
+    if (tid == 0) {
+        mbar_init(&bar[0], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    auto issue = [&](int64_t it) {
+        const int64_t r0 = it * d.R;
+        const int nr = (int) min((int64_t) d.R, d.H - r0);
+        const size_t span = (size_t) (nr - 1) * d.nb1 + d.row_bytes;
+        uint32_t bytes = 0;
+        for (int j = 0; j < d.n_used; ++j)
+            if (s_slot[j] >= 0) bytes += bulk_span_bytes(d.W + (size_t) s_slot[j] * d.nb2 + (size_t) r0 * d.nb1, span);
+        mbar_arrive_expect_tx(&bar[0], bytes);
+        for (int j = 0; j < d.n_used; ++j)
+            if (s_slot[j] >= 0)
+                bulk_span_issue(wbuf + j * d.wspan, d.W + (size_t) s_slot[j] * d.nb2 + (size_t) r0 * d.nb1, span,
+                                &bar[0]);
+    };
+    if (tid == 0) issue(i0);
+
+    // prologue (overlaps the first copy): quantize the n_used act rows into shared memory
+    {
+        const int64_t nck = d.F / 256;
+        for (int64_t c = warp; c < d.n_used * nck; c += 4) {
+            const int j = (int) (c / nck);
+            const int64_t cc = c - j * nck;
+            uint8_t *tok = act + j * d.act_stride;
+            const float *x = d.act + (int64_t) j * d.F + cc * 256;
+            if (d.kq)
+                q8K_block_warp(x, nullptr, (int8_t *) tok + cc * 256, (float *) (tok + d.act_d_off) + cc,
+                               (int16_t *) (tok + d.act_b_off) + cc * 16);
+            else
+                q80_8blocks_warp(x, QWB_Q8_0_CPU, nullptr, (int8_t *) tok + cc * 256,
+                                 (float *) (tok + d.act_d_off) + cc * 8);
+        }
+    }
+    __syncthreads();
+
+    const int units = (int) (d.F / 32);
+    for (int64_t it = i0; it < i1; ++it) {
+        const uint32_t ph = (uint32_t) ((it - i0) & 1);
+        bool ok = mbar_wait(&bar[0], ph);
+        ok = __syncthreads_and(ok);
+        if (!ok) {
+            if (tid == 0) {
+                report(d.st, QWB_DEVERR_TIMEOUT, (int32_t) it);
+                mbar_wait(&bar[0], ph);
+            }
+            return;
+        }
+        const int64_t r0 = it * d.R;
+        const int nr = (int) min((int64_t) d.R, d.H - r0);
+        for (int r = warp; r < nr; r += 4) {
+            float acc = 0.f;
+            for (int j = 0; j < d.n_used; ++j) {
+                if (s_slot[j] < 0) continue;
+                const uint8_t *row = wbuf + j * d.wspan +
+                                     ((uintptr_t) (d.W + (size_t) s_slot[j] * d.nb2 + (size_t) r0 * d.nb1) & 15) +
+                                     (size_t) r * d.nb1;
+                ActSmem A{act + j * d.act_stride, d.act_stride, d.act_d_off, d.act_b_off};
+                float pj = 0.f;
+                for (int u = lane; u < units; u += 32) unit_dot<TYPE, 1>(row, u, A, 1, &pj);
+                acc = fmaf(s_w[j], pj, acc);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) {
+                const int64_t h = r0 + r;
+                d.out[h] = d.residual ? acc + d.residual[h] : acc;
+            }
+        }
+        __syncthreads();
+        if (tid == 0 && it + 1 < i1) {
+            fence_proxy_async_smem();
+            issue(it + 1);
+        }
+    }
+}
+
+template <int TYPE>
+static cudaError_t launch_down_t(DownArgs d, cudaStream_t s) {
+    auto kern = moe_down_decode_kernel<TYPE>;
+    const size_t smem = 128 + (size_t) d.smem_act + (size_t) d.n_used * d.wspan;
+    static size_t configured = 0;
+    if (smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        if (e != cudaSuccess) return e;
+        configured = smem;
+    }
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    const int grid = std::max(1, std::min(d.n_rb, per_sm * num_sms()));
+    kern<<<grid, 128, smem, s>>>(d);
+    return cudaGetLastError();
+}
+
+static cudaError_t launch_down(int type, DownArgs d, cudaStream_t s) {
+    const bool kq = type != QWB_TYPE_Q8_0;
+    const int dstride = (int) plane_d_stride(d.F, kq ? QK_K : QK8_0);
+    const int bstride = kq ? (int) plane_bsum_stride(d.F) : 0;
+    d.kq = kq;
+    d.act_d_off = (int) d.F;
+    d.act_b_off = (int) (d.F + dstride * 4);
+    d.act_stride = (int) align_up((size_t) (d.F + dstride * 4 + bstride * 2), 16);
+    d.smem_act = (int) align_up((size_t) d.n_used * d.act_stride, 128);
+    // rows per item: keep the n_used weight spans within ~96 KB
+    int R = 32;
+    while (R > 1 && (size_t) d.n_used * align_up((size_t) R * d.nb1 + 32, 16) + d.smem_act > 96 * 1024) R >>= 1;
+    d.R = R;
+    d.wspan = (int) align_up((size_t) R * d.nb1 + 32, 16);
+    d.n_rb = (int) ceil_div(d.H, R);
+    switch (type) {
+        case QWB_TYPE_Q4_K: return launch_down_t<QWB_TYPE_Q4_K>(d, s);
+        case QWB_TYPE_Q6_K: return launch_down_t<QWB_TYPE_Q6_K>(d, s);
+        default: return launch_down_t<QWB_TYPE_Q8_0>(d, s);
+    }
+}
+
+// ------------------------------------------------------------ workspace plan
+struct FfnPlan {
+    bool kq_gu, kq_d;
+    int NT;
+    int64_t P;
+    size_t off_logits, off_sel, off_w, off_xq, off_index, off_act, off_actq, off_experts, total;
+};
+
+static qwb_status plan_ffn(const qwb_moe_ffn_desc *d, FfnPlan &p) {
+    if (!d) return QWB_ERR_INVALID_ARG;
+    if (d->H <= 0 || d->F <= 0 || d->E <= 0 || d->n_used <= 0 || d->T < 0) return QWB_ERR_INVALID_ARG;
+    const int tg = d->gate.type, tu = d->up.type, td = d->down.type;
+    auto ok_t = [](int t) { return t == QWB_TYPE_Q4_K || t == QWB_TYPE_Q6_K || t == QWB_TYPE_Q8_0; };
+    if (!ok_t(tg) || !ok_t(td) || tu != tg) return QWB_ERR_UNSUPPORTED_TYPE;
+    if (d->n_used > kMaxUsed || d->E > kMaxExperts || d->n_used > d->E) return QWB_ERR_LIMIT;
+    if (d->H % 1024 || d->F % 256) return QWB_ERR_SHAPE;
+    const int64_t n_mat = d->gate.ne[2];
+    if (d->gate.ne[0] != d->H || d->gate.ne[1] != d->F || d->up.ne[0] != d->H || d->up.ne[1] != d->F ||
+        d->up.ne[2] != n_mat || d->down.ne[0] != d->F || d->down.ne[1] != d->H || d->down.ne[2] != n_mat)
+        return QWB_ERR_SHAPE;
+    if (!d->g2s && n_mat != d->E) return QWB_ERR_SHAPE;
+    p.kq_gu = tg != QWB_TYPE_Q8_0;
+    p.kq_d = td != QWB_TYPE_Q8_0;
+    p.P = d->n_used * d->T;
+    p.NT = pick_nt(p.P, d->E);
+    size_t o = kCtrlBytes;
+    p.off_logits = o; o += align_up((size_t) (d->T * d->E) * 4, 256);
+    p.off_sel = o; o += align_up((size_t) p.P * 4, 256);
+    p.off_w = o; o += align_up((size_t) p.P * 4, 256);
+    p.off_xq = o; o += planes_bytes(d->T, d->H, p.kq_gu);
+    p.off_index = o; o += mmid_index_bytes(std::max<int64_t>(p.P, 1), d->E, p.NT);
+    p.off_act = o; o += align_up((size_t) p.P * d->F * 4, 256);
+    p.off_actq = o;
+    p.off_experts = o;
+    if (d->T > 1) {
+        o += planes_bytes(p.P, d->F, p.kq_d);
+        p.off_experts = o;
+        o += align_up((size_t) p.P * d->H * 4, 256);
+    }
+    p.total = o;
+    return QWB_OK;
+}
+
+}  // namespace qwb
+
+using namespace qwb;
+
+extern "C" QWB_API size_t qwb_moe_ffn_workspace_size(const qwb_moe_ffn_desc *desc) {
+    FfnPlan p;
+    if (plan_ffn(desc, p) != QWB_OK) return 0;
+    return p.total;
+}
+
+extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, size_t ws_bytes,
+                                          qwb_status_block *st, qwb_stream_t stream) {
+    FfnPlan p;
+    qwb_status rc = plan_ffn(d, p);
+    if (rc != QWB_OK) return rc;
+    if (d->T == 0) return QWB_OK;
+    if (!d->x || !d->router_w || !d->out || !d->gate.data || !d->up.data || !d->down.data) return QWB_ERR_INVALID_ARG;
+    if (!ws || ws_bytes < p.total) return QWB_ERR_WORKSPACE;
+    if ((uintptr_t) ws % 256) return QWB_ERR_ALIGNMENT;
+    if (((uintptr_t) d->x | (uintptr_t) d->router_w | (uintptr_t) d->out | (uintptr_t) d->act) % 16)
+        return QWB_ERR_ALIGNMENT;
+    for (const qwb_tensor *t : {&d->gate, &d->up, &d->down}) {
+        if (t->nb[0] != row_bytes(t->type, block_elems(t->type))) return QWB_ERR_LAYOUT;
+        if (t->nb[1] < row_bytes(t->type, t->ne[0]) || t->nb[2] < t->nb[1] * (size_t) t->ne[1]) return QWB_ERR_LAYOUT;
+        const uintptr_t al = (uintptr_t) t->data | t->nb[1] | t->nb[2];
+        if (t->type == QWB_TYPE_Q4_K ? al % 16 : al % 2) return QWB_ERR_ALIGNMENT;
+    }
+    cudaStream_t s = (cudaStream_t) stream;
+    char *w = (char *) ws;
+    const int64_t H = d->H, F = d->F, E = d->E, T = d->T, K = d->n_used;
+    const int64_t n_mat = d->gate.ne[2];
+    int32_t *sel = d->selected ? d->selected : (int32_t *) (w + p.off_sel);
+    float *wts = d->weights ? d->weights : (float *) (w + p.off_w);
+    float *logits = (float *) (w + p.off_logits);
+    Q8Planes xq = planes_at(w + p.off_xq, T, H, p.kq_gu);
+    MmidIndex ix = mmid_index_at(w + p.off_index, std::max<int64_t>(p.P, 1), E, p.NT);
+    float *act = d->act ? d->act : (float *) (w + p.off_act);
+    const int32_t *g2s_g = d->g2s, *g2s_u = d->g2s ? d->g2s + E : nullptr, *g2s_d = d->g2s ? d->g2s + 2 * E : nullptr;
+    cudaError_t e;
+
+    const bool decode = T == 1;
+    profile_mark(s, 0);
+    if (T <= kMaxRouterT) {
+        RouterArgs r{};
+        r.x = d->x; r.router_w = d->router_w; r.mask = d->mask;
+        r.H = H; r.E = E; r.T = T; r.n_used = K;
+        r.logits = logits;
+        r.counter = (unsigned *) w;
+        r.selected = sel; r.weights = wts;
+        r.xq = xq; r.kq = p.kq_gu;
+        if (decode) { r.tiles = ix.tiles; r.pairs = ix.pairs; r.n_tiles = ix.n_tiles; }
+        e = launch_router_fused(r, s);
+    } else {
+        e = launch_logits_gemm(d->x, d->router_w, logits, T, E, H, s);
+        if (e == cudaSuccess) e = launch_route(logits, d->mask, E, T, K, 1, 0.0f, sel, wts, s);
+        if (e == cudaSuccess) e = launch_quantize_rows(p.kq_gu ? 0 : 1, d->x, H, T, H, nullptr, xq, nullptr, s);
+    }
+    if (e != cudaSuccess) return QWB_ERR_CUDA;
+    profile_mark(s, QWB_KERNEL_ROUTER);
+    if (!decode) {
+        e = launch_index(sel, 1, K, (int) K, (int) T, (int) E, p.NT, ix, nullptr, 0, 0, 0, st, s);
+        if (e != cudaSuccess) return QWB_ERR_CUDA;
+    }
+    // gate + up + SwiGLU -> act [T][n_used][F]
+    {
+        GemvArgs a{};
+        a.W = (const uint8_t *) d->gate.data; a.nb1 = d->gate.nb[1]; a.nb2 = d->gate.nb[2];
+        a.W2 = (const uint8_t *) d->up.data; a.nb1_2 = d->up.nb[1]; a.nb2_2 = d->up.nb[2];
+        a.row_bytes = row_bytes(d->gate.type, H);
+        a.M = F; a.K = H;
+        a.act = xq;
+        a.tiles = ix.tiles; a.n_tiles = ix.n_tiles; a.pairs = ix.pairs;
+        a.n_used = (int) K; a.n_b = 1;
+        a.dst = act; a.dnb1 = (size_t) F * 4; a.dnb2 = (size_t) K * F * 4;
+        a.remap = g2s_g; a.remap2 = g2s_u; a.n_slots = n_mat;
+        a.st = st;
+        const int NT = decode ? 1 : p.NT;
+        gemv_geometry(a, NT, true);
+        e = launch_gemv(d->gate.type, true, a, NT, decode ? (int) K : ix.max_tiles, s);
+        if (e != cudaSuccess) return QWB_ERR_CUDA;
+        profile_mark(s, QWB_KERNEL_GATE_UP);
+    }
+    if (decode) {
+        DownArgs dn{};
+        dn.W = (const uint8_t *) d->down.data; dn.nb1 = d->down.nb[1]; dn.nb2 = d->down.nb[2];
+        dn.row_bytes = row_bytes(d->down.type, F);
+        dn.n_slots = n_mat; dn.E = E;
+        dn.remap = g2s_d; dn.selected = sel; dn.weights = wts; dn.n_used = (int) K;
+        dn.act = act; dn.F = F; dn.H = H;
+        dn.out = d->out; dn.residual = d->residual;
+        dn.st = st;
+        e = launch_down(d->down.type, dn, s);
+        if (e != cudaSuccess) return QWB_ERR_CUDA;
+        profile_mark(s, QWB_KERNEL_DOWN);
+        return QWB_OK;
+    }
+    // batched: act -> Q8, down GEMV per (slot, token), weighted sum
+    Q8Planes aq = planes_at(w + p.off_actq, p.P, F, p.kq_d);
+    e = launch_quantize_rows(p.kq_d ? 0 : 1, act, F, p.P, F, nullptr, aq, nullptr, s);
+    if (e != cudaSuccess) return QWB_ERR_CUDA;
+    float *experts = (float *) (w + p.off_experts);
+    {
+        GemvArgs a{};
+        a.W = (const uint8_t *) d->down.data; a.nb1 = d->down.nb[1]; a.nb2 = d->down.nb[2];
+        a.row_bytes = row_bytes(d->down.type, F);
+        a.M = H; a.K = F;
+        a.act = aq;
+        a.tiles = ix.tiles; a.n_tiles = ix.n_tiles; a.pairs = ix.pairs;
+        a.n_used = (int) K; a.n_b = (int) K;
+        a.dst = experts; a.dnb1 = (size_t) H * 4; a.dnb2 = (size_t) K * H * 4;
+        a.remap = g2s_d; a.n_slots = n_mat;
+        a.st = st;
+        gemv_geometry(a, p.NT, false);
+        e = launch_gemv(d->down.type, false, a, p.NT, ix.max_tiles, s);
+        if (e != cudaSuccess) return QWB_ERR_CUDA;
+        profile_mark(s, QWB_KERNEL_DOWN);
+    }
+    e = launch_weighted_sum(experts, wts, d->residual, d->out, H, K, T, s);
+    if (e != cudaSuccess) return QWB_ERR_CUDA;
+    profile_mark(s, QWB_KERNEL_OTHER);
+    return QWB_OK;
+}

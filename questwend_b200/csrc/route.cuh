@@ -1,0 +1,36 @@
+// route.cuh - router / reduction launchers shared by the MoE entry points.
+#pragma once
+
+#include "common.cuh"
+
+namespace qwb {
+
+constexpr int kMaxUsed = 32;      // n_expert_used limit of the routing kernels
+constexpr int kMaxExperts = 1024; // n_expert limit of the routing kernels
+constexpr int kMaxRouterT = 16;   // tokens handled by the fused router GEMV
+
+struct RouterArgs {
+    const float *x;         // [T][H]
+    const float *router_w;  // [E][H]
+    const float *mask;      // [T][E] or null
+    int64_t H, E, T, n_used;
+    float *logits;          // [T][E] workspace
+    unsigned *counter;      // workspace word, zero between launches
+    int32_t *selected;      // [T][n_used]
+    float *weights;         // [T][n_used]
+    Q8Planes xq;            // quantized x out (qs null: skip)
+    int kq;                 // 1: Q8_K planes, 0: Q8_0 planes
+    int4 *tiles;            // decode tile list out (T == 1) or null
+    int *pairs;
+    int *n_tiles;
+};
+
+cudaError_t launch_route(const float *logits, const float *mask, int64_t E, int64_t T, int64_t k, int norm,
+                         float scale, int32_t *selected, float *weights, cudaStream_t s);
+cudaError_t launch_router_fused(const RouterArgs &r, cudaStream_t s);
+cudaError_t launch_logits_gemm(const float *x, const float *w, float *out, int64_t T, int64_t E, int64_t H,
+                               cudaStream_t s);
+cudaError_t launch_weighted_sum(const float *ex, const float *w, const float *res, float *out, int64_t H,
+                                int64_t n_used, int64_t T, cudaStream_t s);
+
+}  // namespace qwb
