@@ -3,9 +3,9 @@
 Workload (one "step"): batch-1 decode of one token through the 48 MoE FFN layers of a
 Qwen3-30B-A3B-shaped decoder: hidden 2048, 128 experts, top-8
 softmax routing with renormalisation, expert intermediate 768, Q4_K gate/up, Q6_K down,
-f32 router; each layer is QuestWend's build_moe graph (router mul_mat -> route ->
-3x mul_mat_id -> swiglu -> weighted sum) plus the residual add, chained so layer l+1
-routes on layer l's output.  Attention, norms and the output head are outside the hot
+f32 router; each layer is QuestWend's ffn_norm + build_moe graph (rms_norm * ffn_norm
+weight -> router mul_mat -> route -> 3x mul_mat_id -> swiglu -> weighted sum) plus the
+residual add, chained so layer l+1 routes on layer l's output.  Attention, norms and the output head are outside the hot
 path and not run.  All 48 x 128 x 3 expert matrices are resident in HBM (18.8 GB), so a
 step streams ~1.17 GB of distinct expert weights, far more than the 126 MB L2: inputs
 are larger than L2, no flush is needed.
@@ -138,8 +138,10 @@ def cpu_reference_layer_ms(threads, iters, layers_experts):
     rw = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
     x = rng.standard_normal((1, H)).astype(np.float32)
     reps = E // UNIQUE
+    nw = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
     gate, up, down = (np.tile(a, reps) for a in (g, u, d))
-    r = O.moe_layer(x, rw, Q4_K, gate, up, Q6_K, down, F, E, K_USED, impl="ref", iters=iters)
+    r = O.moe_layer(x, rw, Q4_K, gate, up, Q6_K, down, F, E, K_USED, impl="ref", iters=iters,
+                    norm_w=nw, norm_eps=1e-6)
     return r["ms"]
 
 
@@ -174,8 +176,8 @@ def run_reference(args):
     }))
 
 
-def workload_config(n):
-    return {"workload": "qwen3-30b-a3b MoE FFN stack, batch-1 decode", "layers": LAYERS, "hidden": H,
+def workload_config(n, n_layers=LAYERS):
+    return {"workload": "qwen3-30b-a3b MoE FFN stack, batch-1 decode", "layers": n_layers, "hidden": H,
             "experts": E, "top_k": K_USED, "expert_ffn": F, "gate_up": "Q4_K", "down": "Q6_K",
             "router": "f32", "global_batch": n, "parallelism": f"replicas{n}" if n > 1 else "single",
             "l2": "inputs larger than L2 (1.17 GB of distinct expert weights per step)"}
@@ -188,6 +190,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="qwb", choices=["qwb", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="MoE layers per step (default 48; fewer only for profiling captures)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -214,8 +218,9 @@ def main():
     gen.manual_seed(1234 + rank)
     reps = E // UNIQUE
     base = [torch.from_numpy(a).to(dev) for a in (g, u, d)]
+    n_layers = args.layers
     layers = []
-    for layer in range(LAYERS):
+    for layer in range(n_layers):
         pools = []
         for role, (t, rows, K) in enumerate(((Q4_K, F, H), (Q4_K, F, H), (Q6_K, H, F))):
             buf = torch.empty(base[role].numel() * reps + 16, dtype=torch.uint8, device=dev)
@@ -224,15 +229,18 @@ def main():
             buf[:-16].view(reps, -1).copy_(rolled.expand(reps, -1))
             pools.append(q.QTensor(buf[:-16], t, (K, rows, E, 1)))
         rw = torch.randn((E, H), generator=gen, device=dev) * 0.02
-        layers.append((rw, pools))
-    xs = [torch.empty(H, device=dev) for _ in range(LAYERS + 1)]
+        nw = 1.0 + 0.1 * torch.randn(H, generator=gen, device=dev)
+        layers.append((rw, nw, pools))
+    xs = [torch.empty(H, device=dev) for _ in range(n_layers + 1)]
     xs[0].copy_(torch.randn(H, generator=gen, device=dev))
-    sel = torch.empty((LAYERS, K_USED), dtype=torch.int32, device=dev)
-    wts = torch.empty((LAYERS, K_USED), dtype=torch.float32, device=dev)
+    sel = torch.empty((n_layers, K_USED), dtype=torch.int32, device=dev)
+    wts = torch.empty((n_layers, K_USED), dtype=torch.float32, device=dev)
     descs = []
-    for layer, (rw, (pg, pu, pd)) in enumerate(layers):
+    for layer, (rw, nw, (pg, pu, pd)) in enumerate(layers):
+        # l_out = build_moe(rms_norm(cur) * ffn_norm) + cur  (core/runtime.cpp:2979-2993)
         descs.append(q.ops.moe_ffn_desc(xs[layer].view(1, H), rw, pg, pu, pd, K_USED, xs[layer + 1].view(1, H),
-                                        residual=xs[layer].view(1, H), selected=sel[layer], weights=wts[layer]))
+                                        residual=xs[layer].view(1, H), selected=sel[layer], weights=wts[layer],
+                                        norm_w=nw, norm_eps=1e-6))
     import ctypes as C
     need = lib.qwb_moe_ffn_workspace_size(C.byref(descs[0]))
     ws = q.ops.workspace(need)
@@ -244,18 +252,36 @@ def main():
             if rc:
                 raise L.QwbError("qwb_moe_ffn", rc)
 
-    # eager warm-up (also configures kernel attributes outside capture)
+    # eager warm-up, layer by layer with checks (also configures kernel attributes
+    # outside capture)
     s_main = torch.cuda.current_stream()
-    step(C.c_void_p(s_main.cuda_stream))
-    torch.cuda.synchronize()
-    n_marks = LAYERS * 4 + 4
-    L.check("qwb_profile_enable", lib.qwb_profile_enable(n_marks))
+    for layer, dsc in enumerate(descs):
+        rc = lib.qwb_moe_ffn(C.byref(dsc), ws.data_ptr(), ws.numel(), status.data_ptr(),
+                             C.c_void_p(s_main.cuda_stream))
+        if rc:
+            raise L.QwbError("qwb_moe_ffn", rc)
+        try:
+            torch.cuda.synchronize()
+        except Exception as ex:
+            raise RuntimeError(f"eager warm-up failed at layer {layer}") from ex
+        flags, bad, cnt = q.read_status()
+        xo = xs[layer + 1]
+        if flags or not torch.isfinite(xo).all():
+            raise RuntimeError(f"layer {layer}: device flags {flags} (value {bad}, count {cnt}), "
+                               f"finite={bool(torch.isfinite(xo).all())}, selected={sel[layer].tolist()}")
+    # two graphs of the same step: `graph` (timed) and `pgraph` (same kernels plus an
+    # event record after each, for the per-kernel breakdown)
     graph = torch.cuda.CUDAGraph()
     cs = torch.cuda.Stream()
     cs.wait_stream(s_main)
     with torch.cuda.stream(cs):
-        lib.qwb_profile_reset()
         with torch.cuda.graph(graph, stream=cs):
+            step(C.c_void_p(cs.cuda_stream))
+    L.check("qwb_profile_enable", lib.qwb_profile_enable(n_layers * 4 + 4))
+    pgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cs):
+        lib.qwb_profile_reset()
+        with torch.cuda.graph(pgraph, stream=cs):
             step(C.c_void_p(cs.cuda_stream))
     n_rec = lib.qwb_profile_count()
     torch.cuda.synchronize()
@@ -274,13 +300,15 @@ def main():
         t1.record()
         torch.cuda.synchronize()
     ms_step = t0.elapsed_time(t1) / args.steps
-    # per-kernel durations of the last replay of the timed region
+    # per-kernel durations: replays of the profiled graph right after the timed region
+    per_kernel = {}
     ms = (C.c_float * (n_rec - 1))()
     tags = (C.c_int32 * (n_rec - 1))()
-    L.check("qwb_profile_read", lib.qwb_profile_read(ms, tags, n_rec - 1))
-    per_kernel = {}
-    for m, tg in zip(ms, tags):
-        per_kernel.setdefault(int(tg), []).append(float(m))
+    for _ in range(3):
+        pgraph.replay()
+        L.check("qwb_profile_read", lib.qwb_profile_read(ms, tags, n_rec - 1))
+        for m, tg in zip(ms, tags):
+            per_kernel.setdefault(int(tg), []).append(float(m))
     flags, bad, cnt = q.read_status()
 
     # ------------------------------------------------------------------ e2e
@@ -292,7 +320,7 @@ def main():
     for _ in range(args.steps):
         xs[0].copy_(x_host, non_blocking=True)
         graph.replay()
-        y_host.copy_(xs[LAYERS], non_blocking=True)
+        y_host.copy_(xs[n_layers], non_blocking=True)
         torch.cuda.current_stream().synchronize()
     e1.record()
     torch.cuda.synchronize()
@@ -304,7 +332,7 @@ def main():
     ms_step, ms_e2e = times.tolist()
 
     # graph replays of the same step are identical: check the output is finite and sane
-    out = xs[LAYERS].float().cpu().numpy()
+    out = xs[n_layers].float().cpu().numpy()
     assert np.isfinite(out).all()
 
     hbm, kind = peaks()
@@ -313,14 +341,14 @@ def main():
     gu_bytes = K_USED * 2 * EXPERT_GU + K_USED * (H + 4 * 8 + 2 * 128)  # weights + q8 activation rows
     dn = per_kernel.get(3, [])
     dn_ms = float(np.mean(dn)) if dn else None
-    step_bytes = LAYERS * (K_USED * (2 * EXPERT_GU + EXPERT_D) + E * H * 4)
+    step_bytes = n_layers * (K_USED * (2 * EXPERT_GU + EXPERT_D) + E * H * 4)
     achieved = gu_bytes / (gu_ms * 1e-3) / 1e9 if gu_ms else None
     result = {
         "metric": "decode_tokens_per_s", "value": world * 1000.0 / ms_step, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "q4_K/q6_K x q8_K -> f32", "data": "synthetic (seeded N(0,0.02) weights, ggml quantizer)",
-        "config": workload_config(world),
+        "config": workload_config(world, n_layers),
         "decode_hbm_gbs": step_bytes / (ms_step * 1e-3) / 1e9,
         "decode_hbm_frac": step_bytes / (ms_step * 1e-3) / 1e9 / hbm,
         "roofline": {"bound": "hbm", "kernel": "moe gate/up GEMV (GLU) per layer", "achieved": achieved,
@@ -332,7 +360,7 @@ def main():
         "down_gbs": (K_USED * EXPERT_D) / (dn_ms * 1e-3) / 1e9 if dn_ms else None,
         "e2e": {"value": world * 1000.0 / ms_e2e, "unit": "tokens/s", "h2d_bytes_per_step": H * 4,
                 "d2h_bytes_per_step": H * 4},
-        "gpu_launches": args.steps * (n_rec - 1),
+        "gpu_launches": args.steps * 3 * n_layers,
         "device_errors": flags,
         "clocks": clk.summary(),
     }
@@ -340,12 +368,12 @@ def main():
         threads = os.cpu_count() or 1
         lm = cpu_reference_layer_ms(threads, 20, (g, u, d))
         if lm is not None:
-            result["cpu_baseline"] = {"value": 1000.0 / (lm * LAYERS), "unit": "tokens/s", "cores": threads,
+            result["cpu_baseline"] = {"value": 1000.0 / (lm * n_layers), "unit": "tokens/s", "cores": threads,
                                       "kind": "reference",
-                                      "sample": f"one MoE layer x 20 evaluations ({lm:.3f} ms each), scaled x{LAYERS}"}
+                                      "sample": f"one MoE layer x 20 evaluations ({lm:.3f} ms each), scaled x{n_layers}"}
     if rank == 0:
         print(json.dumps(result))
-    del graph
+    del graph, pgraph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

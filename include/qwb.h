@@ -160,7 +160,8 @@ QWB_API qwb_status qwb_moe_weighted_sum(const float *experts, const float *weigh
 
 /* ---------------------------------------------------------- fused MoE layer
  * replaces the whole build_moe subgraph (core/runtime.cpp:2743-2816, and the cached
- * fast path's slot remap :2769-2778):
+ * fast path's slot remap :2769-2778), optionally with the ffn_norm that feeds it (:2979):
+ *   x      = rms_norm(x) * norm_w    (when norm_w != NULL; ops.cpp:4107-4162)
  *   logits = router_w . x            (F32 mul_mat, :2750)
  *   selected, weights = route(...)   (as qwb_moe_route, norm on)
  *   slot_r = g2s[r][selected]        (r = gate, up, down; skipped when g2s == NULL)
@@ -182,6 +183,11 @@ typedef struct qwb_moe_ffn_desc {
     float *weights;          /* [n_used, T] out, or NULL */
     float *act;              /* [F, n_used, T] out: swiglu(gate, up), the down projection's
                                 input (ggml's "act" node), or NULL */
+    const float *norm_w;     /* [H] ffn_norm weight, or NULL.  When set the layer input is
+                                rms_norm(x, norm_eps) * norm_w (core/runtime.cpp:2979, the
+                                ffn_in of build_moe), fused into the router kernel; the
+                                residual is still added un-normalised. */
+    float norm_eps;
 } qwb_moe_ffn_desc;
 
 QWB_API size_t qwb_moe_ffn_workspace_size(const qwb_moe_ffn_desc *desc);

@@ -77,6 +77,7 @@ def port():
         lib.qo_swiglu.argtypes = [vp, vp, vp, i64]
         lib.qo_moe_layer.argtypes = [vp, i64, i64, vp, i64, i64, i32, vp, vp, i32, vp, i64, i64,
                                      vp, vp, vp, vp, vp, vp]
+        lib.qo_rms_norm_mul.argtypes = [vp, vp, f32, i64, i64, vp]
         lib.qo_fp32_to_fp16.restype = C.c_uint16
         lib.qo_fp32_to_fp16.argtypes = [f32]
         _port = lib
@@ -121,7 +122,7 @@ def ref():
         lib.qref_route.argtypes = [vp, i64, i64, i64, i32, f32, vp, vp, vp, i32]
         lib.qref_moe_layer.restype = f64
         lib.qref_moe_layer.argtypes = [vp, i64, i64, vp, i64, i64, i32, vp, vp, i32, vp, i64, i64,
-                                       vp, vp, vp, vp, vp, vp, i32]
+                                       vp, vp, vp, vp, vp, vp, i32, vp, f32]
         _ref = lib
     return _ref
 
@@ -219,11 +220,23 @@ def route(logits: np.ndarray, n_used: int, norm: bool = True, scale: float = 0.0
     return sel, w
 
 
-def moe_layer(x, router_w, type_gu, gate, up, type_d, down, F, n_mat, n_used,
-              g2s=None, mask=None, impl: str = "port", iters: int = 0, want_act=False):
-    """One build_moe layer.  x [T, H], router_w [E, H]; returns dict(out, selected, weights,
-    act, ms)."""
+def rms_norm_mul(x, w, eps):
     x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    y = np.zeros_like(x)
+    port().qo_rms_norm_mul(_p(x), _p(w), eps, x.shape[0], x.shape[1], _p(y))
+    return y
+
+
+def moe_layer(x, router_w, type_gu, gate, up, type_d, down, F, n_mat, n_used,
+              g2s=None, mask=None, impl: str = "port", iters: int = 0, want_act=False,
+              norm_w=None, norm_eps: float = 1e-6):
+    """One build_moe layer.  x [T, H], router_w [E, H]; with norm_w the layer input is
+    rms_norm(x) * norm_w (the ffn_norm).  Returns dict(out, selected, weights, act, ms)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    nw = None if norm_w is None else np.ascontiguousarray(norm_w, dtype=np.float32)
+    if nw is not None and impl != "ref":
+        x = rms_norm_mul(x, nw, norm_eps)
     router_w = np.ascontiguousarray(router_w, dtype=np.float32)
     T, H = x.shape
     E = router_w.shape[0]
@@ -237,7 +250,7 @@ def moe_layer(x, router_w, type_gu, gate, up, type_d, down, F, n_mat, n_used,
     if impl == "ref":
         ms = ref().qref_moe_layer(_p(x), H, T, _p(router_w), E, n_used, type_gu, _p(gate), _p(up),
                                   type_d, _p(down), F, n_mat, _p(g2), _p(m), _p(out), _p(sel),
-                                  _p(w), _p(act), iters)
+                                  _p(w), _p(act), iters, _p(nw), norm_eps)
     else:
         rc = port().qo_moe_layer(_p(x), H, T, _p(router_w), E, n_used, type_gu, _p(gate), _p(up),
                                  type_d, _p(down), F, n_mat, _p(g2), _p(m), _p(out), _p(sel),

@@ -720,3 +720,17 @@ int qo_moe_layer(const float *x, int64_t H, int64_t T,
     free(logits); free(sel); free(w); free(g); free(u); free(a); free(ex);
     return rc;
 }
+
+/* ggml-cpu/ops.cpp:4107-4162 ggml_compute_forward_rms_norm_f32 fused with the following
+ * MUL by the norm weight: sum of f32 squares accumulated in double, mean = (float)
+ * (sum / H), scale = 1/sqrtf(mean + eps), y = x * scale * w. */
+void qo_rms_norm_mul(const float *x, const float *w, float eps, int64_t T, int64_t H, float *y) {
+    for (int64_t t = 0; t < T; ++t) {
+        const float *xr = x + t * H;
+        double sum = 0.0;
+        for (int64_t i = 0; i < H; ++i) sum += (double) (xr[i] * xr[i]);
+        const float mean = (float) (sum / (double) H);
+        const float scale = 1.0f / sqrtf(mean + eps);
+        for (int64_t i = 0; i < H; ++i) y[t * H + i] = xr[i] * scale * w[i];
+    }
+}

@@ -76,6 +76,9 @@ int qo_moe_layer(const float *x, int64_t H, int64_t T,
                  const int32_t *g2s, const float *mask,
                  float *out, int32_t *selected, float *weights, float *act_out);
 
+/* ggml_rms_norm(x, eps) * w per row of H (ggml-cpu/ops.cpp:4107-4162) */
+void qo_rms_norm_mul(const float *x, const float *w, float eps, int64_t T, int64_t H, float *y);
+
 #ifdef __cplusplus
 }
 #endif

@@ -203,7 +203,7 @@ double qref_moe_layer(const float * x, int64_t H, int64_t T,
                       int type_d, const void * down, int64_t F, int64_t n_mat,
                       const int32_t * g2s, const float * mask,
                       float * out, int32_t * selected, float * weights, float * act_out,
-                      int iters) {
+                      int iters, const float * norm_w, float norm_eps) {
     Graph g(1024);
     ggml_context * ctx = g.ctx;
     ggml_tensor * tx  = ggml_new_tensor_2d(ctx, GGML_TYPE_F32, H, T);
@@ -213,8 +213,11 @@ double qref_moe_layer(const float * x, int64_t H, int64_t T,
     ggml_tensor * td  = ggml_new_tensor_3d(ctx, (ggml_type) type_d, F, H, n_mat);
     ggml_tensor * tm  = mask ? ggml_new_tensor_2d(ctx, GGML_TYPE_F32, E, T) : nullptr;
     ggml_tensor * tg2s = g2s ? ggml_new_tensor_3d(ctx, GGML_TYPE_I32, 1, E, 3) : nullptr;
+    ggml_tensor * tnw = norm_w ? ggml_new_tensor_1d(ctx, GGML_TYPE_F32, H) : nullptr;
 
-    ggml_tensor * logits = ggml_mul_mat(ctx, trw, tx);  // [E, T]
+    // ffn_in = rms_norm(cur) * ffn_norm.weight (core/runtime.cpp:2979)
+    ggml_tensor * xin = tnw ? ggml_mul(ctx, ggml_rms_norm(ctx, tx, norm_eps), tnw) : tx;
+    ggml_tensor * logits = ggml_mul_mat(ctx, trw, xin);  // [E, T]
     if (tm) logits = ggml_add(ctx, logits, tm);
     ggml_tensor * probs = ggml_soft_max(ctx, logits);
     ggml_tensor * sel = ggml_argsort_top_k(ctx, probs, n_used);
@@ -236,7 +239,7 @@ double qref_moe_layer(const float * x, int64_t H, int64_t T,
         };
         ids_g = remap(0); ids_u = remap(1); ids_d = remap(2);
     }
-    ggml_tensor * x3 = ggml_reshape_3d(ctx, tx, H, 1, T);
+    ggml_tensor * x3 = ggml_reshape_3d(ctx, xin, H, 1, T);
     ggml_tensor * tup   = ggml_mul_mat_id(ctx, tu, x3, ids_u);
     ggml_tensor * tgate = ggml_mul_mat_id(ctx, tg, x3, ids_g);
     ggml_tensor * act = ggml_swiglu_split(ctx, tgate, tup);  // [F, n_used, T]
@@ -267,6 +270,7 @@ double qref_moe_layer(const float * x, int64_t H, int64_t T,
     ggml_backend_tensor_set(trw, router_w, 0, ggml_nbytes(trw));
     if (tm) ggml_backend_tensor_set(tm, mask, 0, ggml_nbytes(tm));
     if (tg2s) ggml_backend_tensor_set(tg2s, g2s, 0, ggml_nbytes(tg2s));
+    if (tnw) ggml_backend_tensor_set(tnw, norm_w, 0, ggml_nbytes(tnw));
     double ms = g.compute(iters);
     ggml_backend_tensor_get(moe, out, 0, ggml_nbytes(moe));
     if (selected) ggml_backend_tensor_get(selc, selected, 0, ggml_nbytes(selc));

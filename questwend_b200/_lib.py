@@ -47,7 +47,8 @@ class MoeFfnDesc(C.Structure):
                 ("gate", Tensor), ("up", Tensor), ("down", Tensor),
                 ("H", C.c_int64), ("F", C.c_int64), ("E", C.c_int64), ("n_used", C.c_int64),
                 ("T", C.c_int64), ("residual", C.c_void_p), ("out", C.c_void_p),
-                ("selected", C.c_void_p), ("weights", C.c_void_p), ("act", C.c_void_p)]
+                ("selected", C.c_void_p), ("weights", C.c_void_p), ("act", C.c_void_p),
+                ("norm_w", C.c_void_p), ("norm_eps", C.c_float)]
 
 
 _lib = None

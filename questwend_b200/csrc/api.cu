@@ -41,7 +41,12 @@ int g_next = 0;
 
 void profile_mark(cudaStream_t s, int tag) {
     if (g_events.empty() || g_next >= (int) g_events.size()) return;
-    if (cudaEventRecord(g_events[g_next], s) == cudaSuccess) g_tags[g_next++] = tag;
+    // under stream capture the record must become an external event-record node, or it
+    // is only a capture-time dependency and never records on replay
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(s, &cs);
+    const unsigned flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : cudaEventRecordDefault;
+    if (cudaEventRecordWithFlags(g_events[g_next], s, flags) == cudaSuccess) g_tags[g_next++] = tag;
 }
 }  // namespace qwb
 

@@ -98,8 +98,8 @@ __global__ void __launch_bounds__(128) mmid_gemv_kernel(const GemvArgs a) {
     // expert slot of a tile for the first / second weight tensor; -1 when the remap
     // table holds an id outside [0, n_slots)
     auto slot_of = [&](int e, const int32_t *rm) -> int64_t {
-        if (!rm) return e;
-        const int64_t sl = rm[e];
+        if (e < 0 || e >= a.n_ids) return -1;
+        const int64_t sl = rm ? (int64_t) rm[e] : (int64_t) e;
         return (sl >= 0 && sl < a.n_slots) ? sl : -1;
     };
     auto issue = [&](int64_t it, uint8_t *stg, uint64_t *b) {
@@ -432,6 +432,8 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
     a.dst = (float *) dst->data;
     a.dnb1 = dst->nb[1];
     a.dnb2 = dst->nb[2];
+    a.n_ids = p.n_as;
+    a.n_slots = p.n_as;
     a.st = st;
     gemv_geometry(a, p.NT, false);
     e = launch_gemv(p.type, false, a, p.NT, ix.max_tiles, s);

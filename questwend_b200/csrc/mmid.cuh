@@ -32,6 +32,7 @@ struct GemvArgs {
     // optional expert -> slot remap (the in-graph get_rows of an I32 [1, E] table,
     // core/runtime.cpp:2769-2778); slot ids must lie in [0, n_slots)
     const int32_t *remap, *remap2;
+    int64_t n_ids;    // tile expert ids must lie in [0, n_ids) (the remap table length)
     int64_t n_slots;
     qwb_status_block *st;
 };

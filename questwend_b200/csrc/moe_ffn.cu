@@ -189,7 +189,7 @@ struct FfnPlan {
     bool kq_gu, kq_d;
     int NT;
     int64_t P;
-    size_t off_logits, off_sel, off_w, off_xq, off_index, off_act, off_actq, off_experts, total;
+    size_t off_logits, off_sel, off_w, off_xq, off_index, off_act, off_xn, off_actq, off_experts, total;
 };
 
 static qwb_status plan_ffn(const qwb_moe_ffn_desc *d, FfnPlan &p) {
@@ -216,6 +216,8 @@ static qwb_status plan_ffn(const qwb_moe_ffn_desc *d, FfnPlan &p) {
     p.off_xq = o; o += planes_bytes(d->T, d->H, p.kq_gu);
     p.off_index = o; o += mmid_index_bytes(std::max<int64_t>(p.P, 1), d->E, p.NT);
     p.off_act = o; o += align_up((size_t) p.P * d->F * 4, 256);
+    p.off_xn = o;
+    if (d->norm_w && d->T > kMaxRouterT) o += align_up((size_t) d->T * d->H * 4, 256);
     p.off_actq = o;
     p.off_experts = o;
     if (d->T > 1) {
@@ -246,7 +248,8 @@ extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, s
     if (!d->x || !d->router_w || !d->out || !d->gate.data || !d->up.data || !d->down.data) return QWB_ERR_INVALID_ARG;
     if (!ws || ws_bytes < p.total) return QWB_ERR_WORKSPACE;
     if ((uintptr_t) ws % 256) return QWB_ERR_ALIGNMENT;
-    if (((uintptr_t) d->x | (uintptr_t) d->router_w | (uintptr_t) d->out | (uintptr_t) d->act) % 16)
+    if (((uintptr_t) d->x | (uintptr_t) d->router_w | (uintptr_t) d->out | (uintptr_t) d->act |
+         (uintptr_t) d->norm_w) % 16)
         return QWB_ERR_ALIGNMENT;
     for (const qwb_tensor *t : {&d->gate, &d->up, &d->down}) {
         if (t->nb[0] != row_bytes(t->type, block_elems(t->type))) return QWB_ERR_LAYOUT;
@@ -277,12 +280,20 @@ extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, s
         r.counter = (unsigned *) w;
         r.selected = sel; r.weights = wts;
         r.xq = xq; r.kq = p.kq_gu;
+        r.norm_w = d->norm_w; r.norm_eps = d->norm_eps;
         if (decode) { r.tiles = ix.tiles; r.pairs = ix.pairs; r.n_tiles = ix.n_tiles; }
         e = launch_router_fused(r, s);
     } else {
-        e = launch_logits_gemm(d->x, d->router_w, logits, T, E, H, s);
+        const float *xin = d->x;
+        if (d->norm_w) {
+            float *xn = (float *) (w + p.off_xn);
+            e = launch_rmsnorm(d->x, d->norm_w, d->norm_eps, T, H, xn, s);
+            if (e != cudaSuccess) return QWB_ERR_CUDA;
+            xin = xn;
+        }
+        e = launch_logits_gemm(xin, d->router_w, logits, T, E, H, s);
         if (e == cudaSuccess) e = launch_route(logits, d->mask, E, T, K, 1, 0.0f, sel, wts, s);
-        if (e == cudaSuccess) e = launch_quantize_rows(p.kq_gu ? 0 : 1, d->x, H, T, H, nullptr, xq, nullptr, s);
+        if (e == cudaSuccess) e = launch_quantize_rows(p.kq_gu ? 0 : 1, xin, H, T, H, nullptr, xq, nullptr, s);
     }
     if (e != cudaSuccess) return QWB_ERR_CUDA;
     profile_mark(s, QWB_KERNEL_ROUTER);
@@ -301,7 +312,7 @@ extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, s
         a.tiles = ix.tiles; a.n_tiles = ix.n_tiles; a.pairs = ix.pairs;
         a.n_used = (int) K; a.n_b = 1;
         a.dst = act; a.dnb1 = (size_t) F * 4; a.dnb2 = (size_t) K * F * 4;
-        a.remap = g2s_g; a.remap2 = g2s_u; a.n_slots = n_mat;
+        a.remap = g2s_g; a.remap2 = g2s_u; a.n_ids = E; a.n_slots = n_mat;
         a.st = st;
         const int NT = decode ? 1 : p.NT;
         gemv_geometry(a, NT, true);
@@ -337,7 +348,7 @@ extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, s
         a.tiles = ix.tiles; a.n_tiles = ix.n_tiles; a.pairs = ix.pairs;
         a.n_used = (int) K; a.n_b = (int) K;
         a.dst = experts; a.dnb1 = (size_t) H * 4; a.dnb2 = (size_t) K * H * 4;
-        a.remap = g2s_d; a.n_slots = n_mat;
+        a.remap = g2s_d; a.n_ids = E; a.n_slots = n_mat;
         a.st = st;
         gemv_geometry(a, p.NT, false);
         e = launch_gemv(d->down.type, false, a, p.NT, ix.max_tiles, s);

@@ -7,18 +7,30 @@
 
 namespace qwb {
 
+// Lane `lane`'s 8 consecutive inputs x[8*lane .. 8*lane+8).  With a norm weight nw the
+// values are first RMS-normalised exactly as ggml's fused rms_norm * weight on the CPU
+// (ggml-cpu/ops.cpp:4161: y = x * scale * w, two rounded products).
+__device__ __forceinline__ void load8_normed(const float *x, float nscale, const float *nw, int lane, float v[8]) {
+    const float4 a = *(const float4 *) (x + 8 * lane);
+    const float4 b = *(const float4 *) (x + 8 * lane + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    if (nw) {
+        const float4 c = *(const float4 *) (nw + 8 * lane);
+        const float4 e = *(const float4 *) (nw + 8 * lane + 4);
+        const float w[8] = {c.x, c.y, c.z, c.w, e.x, e.y, e.z, e.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], nscale), w[i]);
+    }
+}
+
 // One warp quantizes one 256-value Q8_K block; lane l owns values [8l, 8l+8).
 // Outputs (any may be null): packed block_q8_K, or plane qs/d/bsum.
 __device__ __forceinline__ void q8K_block_warp(const float *x, uint8_t *packed, int8_t *pqs, float *pd,
-                                               int16_t *pbsum) {
+                                               int16_t *pbsum, float nscale = 1.f, const float *nw = nullptr) {
     const int lane = threadIdx.x & 31;
     float v[8];
-    {
-        const float4 a = *(const float4 *) (x + 8 * lane);
-        const float4 b = *(const float4 *) (x + 8 * lane + 4);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-    }
+    load8_normed(x, nscale, nw, lane, v);
     // local first-max of |x|
     float lam = 0.f, lmx = 0.f;
 #pragma unroll
@@ -66,15 +78,10 @@ __device__ __forceinline__ void q8K_block_warp(const float *x, uint8_t *packed, 
 
 // One warp quantizes 8 Q8_0 blocks (256 values); lane l owns values [8l, 8l+8) of block l/4.
 __device__ __forceinline__ void q80_8blocks_warp(const float *x, int variant, uint8_t *packed, int8_t *pqs,
-                                                 float *pd) {
+                                                 float *pd, float nscale = 1.f, const float *nw = nullptr) {
     const int lane = threadIdx.x & 31;
     float v[8];
-    {
-        const float4 a = *(const float4 *) (x + 8 * lane);
-        const float4 b = *(const float4 *) (x + 8 * lane + 4);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-    }
+    load8_normed(x, nscale, nw, lane, v);
     float amax = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
@@ -109,13 +116,14 @@ __device__ __forceinline__ void q80_8blocks_warp(const float *x, int variant, ui
 // Quantize one 256-value chunk (row r, columns [c0, c0+256) of a row of length K) of
 // f32 activations at x into q8 planes.  kind: 0 = Q8_K, 1 = Q8_0 cpu, 2 = Q8_0 ref.
 __device__ __forceinline__ void quantize_chunk_warp(int kind, const float *x, const Q8Planes &pl, int64_t r,
-                                                    int64_t c0, int64_t K) {
+                                                    int64_t c0, int64_t K, float nscale = 1.f,
+                                                    const float *nw = nullptr) {
     if (kind == 0) {
         q8K_block_warp(x, nullptr, pl.qs + r * K + c0, pl.d + r * plane_d_stride(K, QK_K) + c0 / QK_K,
-                       pl.bsum + r * plane_bsum_stride(K) + c0 / 16);
+                       pl.bsum + r * plane_bsum_stride(K) + c0 / 16, nscale, nw);
     } else {
         q80_8blocks_warp(x, kind == 2 ? QWB_Q8_0_REF : QWB_Q8_0_CPU, nullptr, pl.qs + r * K + c0,
-                         pl.d + r * plane_d_stride(K, QK8_0) + c0 / QK8_0);
+                         pl.d + r * plane_d_stride(K, QK8_0) + c0 / QK8_0, nscale, nw);
     }
 }
 

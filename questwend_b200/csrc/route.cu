@@ -44,22 +44,27 @@ __device__ __forceinline__ double block_sum_d(double v, double *red) {
 // sp: shared scratch of E floats.  Writes sel[0..k) and w[0..k).
 __device__ void route_token(const float *lg, const float *mk, int E, int k, int norm, float scale, int32_t *sel,
                             float *w, float *sp, int *ssel, float *redf, double *redd) {
+    // a NaN logit ranks last (as -inf) so the top-k is a total order and every one of
+    // the k slots is written
+    for (int j = threadIdx.x; j < k; j += blockDim.x) ssel[j] = j;
     float lmax = -INFINITY;
     for (int i = threadIdx.x; i < E; i += blockDim.x) {
         float v = __ldcg(lg + i);
         if (mk) v = __fadd_rn(v, __ldcg(mk + i));
+        if (isnan(v)) v = -INFINITY;
         sp[i] = v;
         lmax = fmaxf(lmax, v);
     }
     const float mx = block_max(lmax, redf);
     double ls = 0.0;
     for (int i = threadIdx.x; i < E; i += blockDim.x) {
-        const float e = expf(__fsub_rn(sp[i], mx));
+        float e = expf(__fsub_rn(sp[i], mx));
+        if (isnan(e)) e = 0.f;  // every logit -inf: all probabilities 0
         sp[i] = e;
         ls += (double) e;
     }
     const double sum = block_sum_d(ls, redd);
-    const float inv = (float) (1.0 / sum);
+    const float inv = sum > 0.0 ? (float) (1.0 / sum) : 0.f;
     for (int i = threadIdx.x; i < E; i += blockDim.x) sp[i] = __fmul_rn(sp[i], inv);
     __syncthreads();
     for (int i = threadIdx.x; i < E; i += blockDim.x) {
@@ -112,36 +117,88 @@ cudaError_t launch_route(const float *logits, const float *mask, int64_t E, int6
 // as side work, quantizes 256-chunks of x into q8 planes.  The last CTA to finish (an
 // atomicInc on a workspace counter that wraps back to zero) routes every token and,
 // for decode (T == 1), writes the GEMV tile list: one tile per selected expert.
+// sum of squares of a warp's slice of a row, each square rounded to f32 and accumulated
+// in f64 as ggml's rms_norm does (ggml-cpu/ops.cpp:4140-4144)
+__device__ __forceinline__ double warp_sumsq(const float *x, int64_t n, int lane) {
+    double acc = 0.0;
+    for (int64_t h = 4 * lane; h < n; h += 128) {
+        const float4 b = *(const float4 *) (x + h);
+        acc += (double) __fmul_rn(b.x, b.x);
+        acc += (double) __fmul_rn(b.y, b.y);
+        acc += (double) __fmul_rn(b.z, b.z);
+        acc += (double) __fmul_rn(b.w, b.w);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    return acc;
+}
+// scale = 1 / sqrtf(mean + eps), mean = (float)(sum / H)  (ops.cpp:4146-4147)
+__device__ __forceinline__ float rms_scale(double sum, int64_t H, float eps) {
+    const float mean = (float) (sum / (double) H);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
+
 __global__ void __launch_bounds__(128) router_fused_kernel(const RouterArgs r) {
     extern __shared__ float sp[];
     __shared__ float part[4][kMaxRouterT];
+    __shared__ double dpart[4][kMaxRouterT];
+    __shared__ float s_scale[kMaxRouterT];
     __shared__ int ssel[kMaxUsed];
     __shared__ float redf[8];
     __shared__ double redd[8];
     __shared__ int s_last;
     const int e = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t q = r.H / 4;  // H % 1024 == 0 checked on the host
 
-    // side work: quantize x (T rows of H) into q8 planes, one 256-chunk per warp
+    // ffn_norm: every CTA derives the per-token RMS scale itself (x rows are a few KB)
+    if (r.norm_w) {
+        for (int t = 0; t < r.T; ++t) {
+            const double v = warp_sumsq(r.x + (int64_t) t * r.H + warp * q, q, lane);
+            if (lane == 0) dpart[warp][t] = v;
+        }
+        __syncthreads();
+        if (threadIdx.x < r.T) {
+            const int t = threadIdx.x;
+            s_scale[t] = rms_scale(((dpart[0][t] + dpart[1][t]) + dpart[2][t]) + dpart[3][t], r.H, r.norm_eps);
+        }
+        __syncthreads();
+    }
+
+    // side work: quantize (normed) x (T rows of H) into q8 planes, one 256-chunk per warp
     if (r.xq.qs) {
         const int64_t chunks = (int64_t) r.T * (r.H / 256);
         for (int64_t c = (int64_t) blockIdx.x * 4 + warp; c < chunks; c += (int64_t) gridDim.x * 4) {
             const int64_t t = c / (r.H / 256), cc = c % (r.H / 256);
-            quantize_chunk_warp(r.kq ? 0 : 1, r.x + t * r.H + cc * 256, r.xq, t, cc * 256, r.H);
+            quantize_chunk_warp(r.kq ? 0 : 1, r.x + t * r.H + cc * 256, r.xq, t, cc * 256, r.H,
+                                r.norm_w ? s_scale[t] : 1.f, r.norm_w ? r.norm_w + cc * 256 : nullptr);
         }
     }
     // logits
-    const int64_t q = r.H / 4;  // H % 1024 == 0 checked on the host
     const float *wr = r.router_w + (int64_t) e * r.H + warp * q;
+    const float *gw = r.norm_w ? r.norm_w + warp * q : nullptr;
     for (int t = 0; t < r.T; ++t) {
         const float *xr = r.x + (int64_t) t * r.H + warp * q;
         float acc = 0.f;
-        for (int64_t h = 4 * lane; h < q; h += 128) {
-            const float4 a = *(const float4 *) (wr + h);
-            const float4 b = *(const float4 *) (xr + h);
-            acc = fmaf(a.x, b.x, acc);
-            acc = fmaf(a.y, b.y, acc);
-            acc = fmaf(a.z, b.z, acc);
-            acc = fmaf(a.w, b.w, acc);
+        if (gw) {
+            const float sc = s_scale[t];
+            for (int64_t h = 4 * lane; h < q; h += 128) {
+                const float4 a = *(const float4 *) (wr + h);
+                const float4 b = *(const float4 *) (xr + h);
+                const float4 g = *(const float4 *) (gw + h);
+                acc = fmaf(a.x, __fmul_rn(__fmul_rn(b.x, sc), g.x), acc);
+                acc = fmaf(a.y, __fmul_rn(__fmul_rn(b.y, sc), g.y), acc);
+                acc = fmaf(a.z, __fmul_rn(__fmul_rn(b.z, sc), g.z), acc);
+                acc = fmaf(a.w, __fmul_rn(__fmul_rn(b.w, sc), g.w), acc);
+            }
+        } else {
+            for (int64_t h = 4 * lane; h < q; h += 128) {
+                const float4 a = *(const float4 *) (wr + h);
+                const float4 b = *(const float4 *) (xr + h);
+                acc = fmaf(a.x, b.x, acc);
+                acc = fmaf(a.y, b.y, acc);
+                acc = fmaf(a.z, b.z, acc);
+                acc = fmaf(a.w, b.w, acc);
+            }
         }
         acc = warp_sum(acc);
         if (lane == 0) part[warp][t] = acc;
@@ -220,6 +277,31 @@ cudaError_t launch_logits_gemm(const float *x, const float *w, float *out, int64
                                cudaStream_t s) {
     dim3 grid((unsigned) ceil_div(E, 64), (unsigned) ceil_div(T, 64));
     logits_gemm_kernel<<<grid, 256, 0, s>>>(x, w, out, T, E, H);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ rms norm
+// one CTA (128 threads) per row
+__global__ void __launch_bounds__(128) rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                                                      float eps, int64_t H, float *__restrict__ y) {
+    __shared__ double dpart[4];
+    __shared__ float s_sc;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t q = H / 4;
+    const float *xr = x + (int64_t) blockIdx.x * H;
+    const double v = warp_sumsq(xr + warp * q, q, lane);
+    if (lane == 0) dpart[warp] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) s_sc = rms_scale(((dpart[0] + dpart[1]) + dpart[2]) + dpart[3], H, eps);
+    __syncthreads();
+    const float sc = s_sc;
+    float *yr = y + (int64_t) blockIdx.x * H;
+    for (int64_t h = threadIdx.x; h < H; h += blockDim.x) yr[h] = __fmul_rn(__fmul_rn(xr[h], sc), w[h]);
+}
+
+cudaError_t launch_rmsnorm(const float *x, const float *w, float eps, int64_t T, int64_t H, float *y, cudaStream_t s) {
+    if (T == 0) return cudaSuccess;
+    rmsnorm_kernel<<<(unsigned) T, 128, 0, s>>>(x, w, eps, H, y);
     return cudaGetLastError();
 }
 

@@ -23,6 +23,8 @@ struct RouterArgs {
     int4 *tiles;            // decode tile list out (T == 1) or null
     int *pairs;
     int *n_tiles;
+    const float *norm_w;    // [H] ffn_norm weight: route and quantize rms_norm(x) * norm_w
+    float norm_eps;
 };
 
 cudaError_t launch_route(const float *logits, const float *mask, int64_t E, int64_t T, int64_t k, int norm,
@@ -30,6 +32,8 @@ cudaError_t launch_route(const float *logits, const float *mask, int64_t E, int6
 cudaError_t launch_router_fused(const RouterArgs &r, cudaStream_t s);
 cudaError_t launch_logits_gemm(const float *x, const float *w, float *out, int64_t T, int64_t E, int64_t H,
                                cudaStream_t s);
+// y[t] = rms_norm(x[t]) * w  (ggml-cpu/ops.cpp:4107-4162, fused RMS_NORM + MUL)
+cudaError_t launch_rmsnorm(const float *x, const float *w, float eps, int64_t T, int64_t H, float *y, cudaStream_t s);
 cudaError_t launch_weighted_sum(const float *ex, const float *w, const float *res, float *out, int64_t H,
                                 int64_t n_used, int64_t T, cudaStream_t s);
 

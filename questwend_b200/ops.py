@@ -226,7 +226,8 @@ def moe_weighted_sum(experts: torch.Tensor, weights: torch.Tensor) -> torch.Tens
 
 
 def moe_ffn_desc(x, router_w, gate: QTensor, up: QTensor, down: QTensor, n_used: int, out,
-                 g2s=None, mask=None, residual=None, selected=None, weights=None, act=None) -> L.MoeFfnDesc:
+                 g2s=None, mask=None, residual=None, selected=None, weights=None, act=None,
+                 norm_w=None, norm_eps: float = 1e-6) -> L.MoeFfnDesc:
     T, H = x.shape
     d = L.MoeFfnDesc()
     d.x = x.data_ptr()
@@ -240,21 +241,24 @@ def moe_ffn_desc(x, router_w, gate: QTensor, up: QTensor, down: QTensor, n_used:
     d.selected = selected.data_ptr() if selected is not None else None
     d.weights = weights.data_ptr() if weights is not None else None
     d.act = act.data_ptr() if act is not None else None
+    d.norm_w = norm_w.data_ptr() if norm_w is not None else None
+    d.norm_eps = norm_eps
     return d
 
 
 def moe_ffn(x, router_w, gate: QTensor, up: QTensor, down: QTensor, n_used: int,
-            g2s=None, mask=None, residual=None, out=None, act=None):
+            g2s=None, mask=None, residual=None, out=None, act=None, norm_w=None, norm_eps: float = 1e-6):
     """One MoE FFN layer (build_moe).  x (T, H) f32, router_w (E, H) f32, gate/up ggml
     [H, F, n_mat], down [F, H, n_mat]; g2s (3, E) int32 expert->slot tables (gate, up,
-    down) or None; act: optional (T, n_used, F) f32 tensor receiving swiglu(gate, up).
+    down) or None; act: optional (T, n_used, F) f32 tensor receiving swiglu(gate, up);
+    norm_w: optional ffn_norm weight (H,): the layer then runs on rms_norm(x) * norm_w.
     Returns (out (T, H), selected (T, n_used), weights (T, n_used))."""
     T, H = x.shape
     if out is None:
         out = torch.empty((T, H), dtype=torch.float32, device=x.device)
     sel = torch.empty((T, n_used), dtype=torch.int32, device=x.device)
     w = torch.empty((T, n_used), dtype=torch.float32, device=x.device)
-    d = moe_ffn_desc(x, router_w, gate, up, down, n_used, out, g2s, mask, residual, sel, w, act)
+    d = moe_ffn_desc(x, router_w, gate, up, down, n_used, out, g2s, mask, residual, sel, w, act, norm_w, norm_eps)
     lib = L.lib()
     need = lib.qwb_moe_ffn_workspace_size(C.byref(d))
     if need == 0:

@@ -122,3 +122,27 @@ def test_moe_ffn_config1_shapes(qwb, T, tgu, td):
     assert e_down <= TOL, (e_down, O.max_abs_rel(out - res, want))
     e_chain = O.nrmse(out - res, r["out"])
     assert e_chain <= 3e-4, (e_chain, O.max_abs_rel(out - res, r["out"]))
+
+
+@pytest.mark.parametrize("T", [1, 4, 24])
+def test_moe_ffn_with_ffn_norm(qwb, T):
+    """ffn_in = rms_norm(x) * ffn_norm.weight fused into the router kernel (T <= 16) or a
+    separate rms-norm kernel (T > 16); the residual is the un-normalised x."""
+    H, F, E, k = 2048, 768, 16, 8
+    rw = (D.rng(1).standard_normal((E, H)) * 0.02).astype(np.float32)
+    g = D.weights(O.Q4_K, E, F, H, seed=2)
+    u = D.weights(O.Q4_K, E, F, H, seed=3)
+    d = D.weights(O.Q6_K, E, H, F, seed=4)
+    nw = (1 + 0.1 * D.rng(7).standard_normal(H)).astype(np.float32)
+    x = D.acts((T, H), seed=8) * np.float32(5.0)
+    Wg = qwb.QTensor.from_bytes(g, O.Q4_K, (H, F, E))
+    Wu = qwb.QTensor.from_bytes(u, O.Q4_K, (H, F, E))
+    Wd = qwb.QTensor.from_bytes(d, O.Q6_K, (F, H, E))
+    act = torch.empty((T, k, F), device="cuda")
+    out, sel, w = qwb.moe_ffn(cu(x), cu(rw), Wg, Wu, Wd, k, residual=cu(x), act=act, norm_w=cu(nw), norm_eps=1e-6)
+    r = O.moe_layer(x, rw, O.Q4_K, g, u, O.Q6_K, d, F, E, k, want_act=True, norm_w=nw, norm_eps=1e-6)
+    sel, act = sel.cpu().numpy(), act.cpu().numpy()
+    assert np.array_equal(sel, r["selected"])
+    assert O.nrmse(act, r["act"]) <= TOL
+    e = O.nrmse(out.cpu().numpy() - x, r["out"])
+    assert e <= 3e-4, e
