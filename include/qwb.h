@@ -136,6 +136,26 @@ QWB_API qwb_status qwb_mul_mat_id(const qwb_tensor *as, const qwb_tensor *b, con
                                   const qwb_tensor *dst, void *workspace, size_t workspace_bytes,
                                   qwb_status_block *d_status, qwb_stream_t stream);
 
+/* MUL_MAT_ID without a workspace, for callers that cannot allocate device memory: a
+ * ggml backend inside graph_compute, code running under another framework's CUDA graph
+ * capture (where cudaMalloc is not allowed), or a host whose device memory is all
+ * committed to its expert-slot pool.  This entry point has no counterpart in the
+ * reference; it computes exactly what qwb_mul_mat_id computes, using a fixed scratch
+ * array of QWB_NOALLOC_SCRATCH_BYTES that the library's device image carries (the CUDA
+ * driver reserves it on every GPU that loads the library, until the process exits).
+ *   - Problems needing more than QWB_NOALLOC_SCRATCH_BYTES of workspace
+ *     (qwb_mul_mat_id_workspace_size) return QWB_ERR_LIMIT.
+ *   - All calls on a device share the array, which keeps the last call's contents (every
+ *     byte a call reads it has written first); calls that overlap on the GPU race on it,
+ *     so the caller must order them (one stream, or events).
+ *   - The first call on each device resolves the array's address with that device
+ *     current; make it before any stream capture.
+ * No cudaMalloc, cudaFree or other allocating call is made. */
+#define QWB_NOALLOC_SCRATCH_BYTES (8u << 20) /* 8 MiB per device */
+QWB_API qwb_status qwb_mul_mat_id_noalloc(const qwb_tensor *as, const qwb_tensor *b,
+                                          const qwb_tensor *ids, const qwb_tensor *dst,
+                                          qwb_status_block *d_status, qwb_stream_t stream);
+
 /* ------------------------------------------------------------ small MoE ops */
 /* replaces the route_experts subgraph (core/runtime.cpp:2693-2734): soft_max
  * (ops.cpp:5813) -> argsort_top_k (ggml.c:5462) -> get_rows of probs -> sum_rows ->

@@ -21,6 +21,7 @@ STATUS = {
     8: "QWB_ERR_DEVICE", 9: "QWB_ERR_LIMIT",
 }
 DEVERR_ID_RANGE, DEVERR_ROW_RANGE, DEVERR_TIMEOUT = 1, 2, 4
+NOALLOC_SCRATCH_BYTES = 8 << 20  # QWB_NOALLOC_SCRATCH_BYTES
 
 
 class QwbError(RuntimeError):
@@ -64,6 +65,7 @@ SIGNATURES = [
     ("qwb_get_rows", C.c_int, [_TP, _TP, _TP, _P, _P]),
     ("qwb_mul_mat_id_workspace_size", C.c_size_t, [_TP, _TP, _TP]),
     ("qwb_mul_mat_id", C.c_int, [_TP, _TP, _TP, _TP, _P, C.c_size_t, _P, _P]),
+    ("qwb_mul_mat_id_noalloc", C.c_int, [_TP, _TP, _TP, _TP, _P, _P]),
     ("qwb_moe_route", C.c_int, [_P, _P, C.c_int64, C.c_int64, C.c_int64, C.c_int, C.c_float, _P, _P, _P]),
     ("qwb_swiglu", C.c_int, [_P, _P, _P, C.c_int64, _P]),
     ("qwb_moe_weighted_sum", C.c_int, [_P, _P, _P, C.c_int64, C.c_int64, C.c_int64, _P]),
