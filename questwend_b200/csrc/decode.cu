@@ -1,0 +1,731 @@
+// decode.cu - batch-1 decode MoE layer (T == 1) as three kernels chained with
+// programmatic dependent launch (PDL).
+//
+// Reference: the same build_moe subgraph as moe_ffn.cu (core/runtime.cpp:2743-2816, ffn_norm
+// :2979), at the decode shape QuestWend runs per token (SURVEY config 1/2).  Decode is
+// HBM-bound: per layer 8 experts x (gate + up + down) are streamed once.  Layout of the work:
+//
+//   router_decode   CTA = 2 router rows.  Before waiting on the previous kernel it
+//                   bulk-copies its router rows into shared memory; then rms_norm(x)*w,
+//                   logits, Q8_K of the normed x (side work of the first CTAs), and the
+//                   last CTA to finish routes (softmax, top-k, renorm) and resolves the
+//                   expert -> slot ids of the three pools.
+//   gateup_decode   one CTA per SM (8 warps).  The CTA owns a contiguous range of
+//                   (expert, row) pairs; right after the routing is visible it issues
+//                   bulk copies of all its gate and up rows (chunked, one mbarrier per
+//                   chunk), then lets the down kernel launch.  Lane = (row, superblock):
+//                   each lane computes one whole Q4_K superblock dot against the
+//                   activation superblock it holds in registers, so scales are decoded
+//                   once per superblock; SwiGLU in the epilogue.
+//   down_decode     one CTA per SM (8 warps; registers and shared memory are sized so it
+//                   can be resident next to gate/up).  Its weights depend only on the
+//                   routing, so it copies them while gate/up is still running; then it
+//                   waits for act, quantizes
+//                   it to Q8_K in shared memory, and each warp produces one output row for
+//                   all selected experts (lane = (expert, superblock)), weighted sum and
+//                   residual included, no atomics.
+//
+// Arithmetic is that of dot.cuh (exact integer sub-block sums on the reference's Q8_K
+// activation bytes, fp32 combine).  Every mbarrier wait is bounded.
+#include <algorithm>
+
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "decode.cuh"
+#include "kernels.cuh"
+#include "quant_dev.cuh"
+
+namespace qwb {
+
+// Optional phase timestamps for pipeline analysis (compiled in only with
+// -DQWB_DECODE_TRACE; no effect on the default build): thread 0 of each CTA records the
+// global timer at numbered points of each kernel.
+#ifdef QWB_DECODE_TRACE
+__device__ unsigned long long g_decode_trace[3][160][8];
+#define QWB_TRACE(k, p)                                                                   \
+    do {                                                                                 \
+        if (threadIdx.x == 0 && blockIdx.x < 160) g_decode_trace[k][blockIdx.x][p] = globaltimer_ns(); \
+    } while (0)
+#else
+#define QWB_TRACE(k, p) \
+    do {                \
+    } while (0)
+#endif
+
+// ------------------------------------------------------------------- helpers
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// silu(g) * u as ggml_vec_swiglu_f32 (vec.cpp:417-447)
+__device__ __forceinline__ float swiglu_f(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
+// unsigned 4 x u8 . signed 4 x s8 dot product accumulate
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// One Q8_K activation superblock held in registers by a lane.
+template <bool KQ6>
+struct ActReg {
+    int q[64];      // 256 int8
+    int bs[KQ6 ? 16 : 8];  // Q4_K: bsum per 32 (pairs of bsum16); Q6_K: bsum per 16
+    float d;
+};
+
+// load superblock s of a q8 plane row (global or shared: qs 16-byte aligned)
+template <bool KQ6>
+__device__ __forceinline__ void load_act(ActReg<KQ6> &a, const int8_t *qs, const int16_t *bsum, float d) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int4 v = *(const int4 *) (qs + 16 * i);
+        a.q[4 * i + 0] = v.x; a.q[4 * i + 1] = v.y; a.q[4 * i + 2] = v.z; a.q[4 * i + 3] = v.w;
+    }
+    if (KQ6) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) a.bs[i] = bsum[i];
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a.bs[i] = (int) bsum[2 * i] + (int) bsum[2 * i + 1];
+    }
+    a.d = d;
+}
+
+// Q4_K superblock (144 B, 16-byte aligned in shared memory) . activation superblock
+// (ggml-cpu/quants.c:696-768): d_w*d_a*sum_j sc_j*isum_j - dmin_w*d_a*sum_j m_j*bsum32_j
+__device__ __forceinline__ float dot_q4K_sb(const uint8_t *sb, const ActReg<false> &a) {
+    const uint4 h = *(const uint4 *) sb;
+    const float dw = h2f((uint16_t) h.x), dmw = h2f((uint16_t) (h.x >> 16));
+    // the 12 packed 6-bit scales/mins -> 8 scales (s0, s1) and 8 mins (m0, m1), one byte
+    // each (same unpacking as get_scale_min_k4, ggml-quants.c:880-887)
+    const uint32_t s0 = h.y & 0x3f3f3f3fu;
+    const uint32_t m0 = h.z & 0x3f3f3f3fu;
+    const uint32_t s1 = (h.w & 0x0f0f0f0fu) | (((h.y >> 6) & 0x03030303u) << 4);
+    const uint32_t m1 = ((h.w >> 4) & 0x0f0f0f0fu) | (((h.z >> 6) & 0x03030303u) << 4);
+    int isum = 0;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        const uint4 w0 = *(const uint4 *) (sb + 16 + 32 * g);
+        const uint4 w1 = *(const uint4 *) (sb + 16 + 32 * g + 16);
+        const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        int il = 0, ih = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            il = dp4a_us(w[i] & 0x0f0f0f0fu, a.q[16 * g + i], il);
+            ih = dp4a_us(w[i] & 0xf0f0f0f0u, a.q[16 * g + 8 + i], ih);  // 16 * hi nibbles
+        }
+        const uint32_t sw = g < 2 ? s0 : s1;
+        const int sc_lo = (sw >> (16 * (g & 1))) & 0xff, sc_hi = (sw >> (16 * (g & 1) + 8)) & 0xff;
+        isum += sc_lo * il + sc_hi * (ih >> 4);
+    }
+    int imin = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) imin += (int) (((j < 4 ? m0 : m1) >> (8 * (j & 3))) & 0xff) * a.bs[j];
+    return __fmul_rn(dw, a.d) * (float) isum - __fmul_rn(dmw, a.d) * (float) imin;
+}
+
+// 32-bit load from a shared-memory address (volatile: never hoisted above the mbarrier
+// wait that makes the bulk-copied bytes visible)
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+// Q6_K superblock (210 B, 2-byte aligned in shared memory) . activation superblock
+// (ggml-cpu/quants.c:851-915): d_w*d_a*sum_g sc_g*sum_{16} (q6-32)*q8, with the -32 applied
+// through the activation's bsum16.  The superblock is read as aligned 32-bit words and
+// realigned with funnel shifts.
+struct Q6Words {
+    uint32_t b;   // shared address of the first aligned word
+    uint32_t sh;  // 0 or 16
+    __device__ __forceinline__ uint32_t operator[](int i) const { return lds32(b + 4u * (uint32_t) i); }
+};
+__device__ __forceinline__ float dot_q6K_sb(const uint8_t *sb, const ActReg<true> &a) {
+    const uint32_t sa = smem_u32(sb);
+    const Q6Words base{sa & ~3u, (sa & 3u) * 8u};
+    const uint32_t sh = base.sh;
+    int gacc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) gacc[i] = 0;
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+        uint32_t raw[17], hr[9];
+#pragma unroll
+        for (int i = 0; i < 17; ++i) raw[i] = base[16 * n + i];
+#pragma unroll
+        for (int i = 0; i < 9; ++i) hr[i] = base[32 + 8 * n + i];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t A = __funnelshift_r(raw[i], raw[i + 1], sh);
+            const uint32_t B = __funnelshift_r(raw[8 + i], raw[9 + i], sh);
+            const uint32_t Hh = __funnelshift_r(hr[i], hr[i + 1], sh);
+            const uint32_t q1 = (A & 0x0f0f0f0fu) | ((Hh << 4) & 0x30303030u);
+            const uint32_t q2 = (B & 0x0f0f0f0fu) | ((Hh << 2) & 0x30303030u);
+            const uint32_t q3 = ((A >> 4) & 0x0f0f0f0fu) | (Hh & 0x30303030u);
+            const uint32_t q4 = ((B >> 4) & 0x0f0f0f0fu) | ((Hh >> 2) & 0x30303030u);
+            const int aw = 32 * n + i;  // activation word of weight n*128 + 4i
+            gacc[8 * n + 0 + i / 4] = dp4a_us(q1, a.q[aw], gacc[8 * n + 0 + i / 4]);
+            gacc[8 * n + 2 + i / 4] = dp4a_us(q2, a.q[aw + 8], gacc[8 * n + 2 + i / 4]);
+            gacc[8 * n + 4 + i / 4] = dp4a_us(q3, a.q[aw + 16], gacc[8 * n + 4 + i / 4]);
+            gacc[8 * n + 6 + i / 4] = dp4a_us(q4, a.q[aw + 24], gacc[8 * n + 6 + i / 4]);
+        }
+    }
+    uint32_t scw[5];
+#pragma unroll
+    for (int i = 0; i < 5; ++i) scw[i] = base[48 + i];
+    const uint32_t sc0 = __funnelshift_r(scw[0], scw[1], sh), sc1 = __funnelshift_r(scw[1], scw[2], sh);
+    const uint32_t sc2 = __funnelshift_r(scw[2], scw[3], sh), sc3 = __funnelshift_r(scw[3], scw[4], sh);
+    const uint32_t sc[4] = {sc0, sc1, sc2, sc3};
+    const uint32_t dword = __funnelshift_r(scw[4], base[53], sh);
+    int isum = 0;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) {
+        const int s = (int) (int8_t) (sc[g >> 2] >> (8 * (g & 3)));
+        isum += s * (gacc[g] - 32 * a.bs[g]);
+    }
+    return __fmul_rn(h2f((uint16_t) dword), a.d) * (float) isum;
+}
+
+// ---------------------------------------------------------------- router
+// The router is ONE thread-block cluster of kRouterCluster CTAs.  Each CTA owns
+// E / kRouterCluster router rows, which it bulk-copies into shared memory before waiting
+// on the previous kernel (they do not depend on it).  After the wait: x -> shared memory,
+// rms_norm * ffn_norm, the CTA's logits, which it stores straight into CTA 0's shared
+// memory (distributed shared memory); one cluster barrier; CTA 0 routes.  The Q8_K of
+// the normed x is side work of a few other CTAs.  No global-memory round trip, fence or
+// atomic lies between the logits and the routing.
+//
+// Routing (route_experts, core/runtime.cpp:2693-2734): softmax over the E logits (+ mask),
+// top-k of the probabilities ranked by a unique key (probability bits, then lower index
+// first: exact ties keep index order), renormalised weights (sum clamped at
+// 6.103515625e-5), and the winners' slot ids in the three pools (g2s remap, validated).
+struct RouterSmemTail {
+    float logit[kMaxRouteE];
+    unsigned long long key[kMaxRouteE];
+    float ev[kMaxRouteE];
+    float red[32];
+    double redd[32];
+    int sel[32];
+};
+
+__device__ void route_in_cta(const RouterDecodeArgs &r, RouterSmemTail &t) {
+    const int tid = threadIdx.x, nth = blockDim.x, warp = tid >> 5, lane = tid & 31, nw = nth >> 5;
+    const int E = (int) r.E, k = r.n_used;
+    // 1. max logit (+ mask)
+    float lmax = -INFINITY;
+    for (int e = tid; e < E; e += nth) {
+        float v = t.logit[e];
+        if (r.mask) v = __fadd_rn(v, r.mask[e]);
+        if (isnan(v)) v = -INFINITY;
+        t.logit[e] = v;
+        lmax = fmaxf(lmax, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    if (lane == 0) t.red[warp] = lmax;
+    __syncthreads();
+    float mx = t.red[0];
+    for (int i = 1; i < nw; ++i) mx = fmaxf(mx, t.red[i]);
+    QWB_TRACE(0, 5);
+    // 2. exp values, unique ranking keys, partial sums
+    float ls = 0.f;
+    for (int e = tid; e < E; e += nth) {
+        float v = expf(__fsub_rn(t.logit[e], mx));
+        if (isnan(v)) v = 0.f;
+        t.ev[e] = v;
+        // probabilities are e * inv with one common inv: ranking the exp values ranks them
+        t.key[e] = ((unsigned long long) __float_as_uint(v) << 32) | (unsigned) (0xffffffffu - (unsigned) e);
+        ls += v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+    if (lane == 0) t.redd[warp] = (double) ls;
+    __syncthreads();
+    QWB_TRACE(0, 6);
+    // 3. rank = number of larger keys; the k winners record themselves
+    for (int e = tid; e < E; e += nth) {
+        const unsigned long long ke = t.key[e];
+        int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
+        const ulonglong2 *k2 = (const ulonglong2 *) t.key;
+        int j = 0;
+        for (; j + 8 <= E; j += 8) {
+            const ulonglong2 a = k2[j / 2], b = k2[j / 2 + 1], c = k2[j / 2 + 2], d = k2[j / 2 + 3];
+            r0 += (a.x > ke) + (a.y > ke);
+            r1 += (b.x > ke) + (b.y > ke);
+            r2 += (c.x > ke) + (c.y > ke);
+            r3 += (d.x > ke) + (d.y > ke);
+        }
+        for (; j < E; ++j) r0 += t.key[j] > ke;
+        const int rank = (r0 + r1) + (r2 + r3);
+        if (rank < k) t.sel[rank] = e;
+    }
+    __syncthreads();
+    QWB_TRACE(0, 7);
+    // 4. weights of the winners, renormalised (sum in rank order, clamped), slot ids
+    if (warp == 0) {
+        float sum = 0.f;
+        for (int i = 0; i < nw; ++i) sum += (float) t.redd[i];
+        const float inv = sum > 0.f ? __fdiv_rn(1.f, sum) : 0.f;
+        const int e = lane < k ? t.sel[lane] : 0;
+        const float pj = lane < k ? __fmul_rn(t.ev[e], inv) : 0.f;
+        float tot = 0.f;
+        for (int j = 0; j < k; ++j) tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, pj, j));
+        const float ws = tot < 6.103515625e-5f ? 6.103515625e-5f : tot;
+        if (lane < k) {
+            r.sel[lane] = e;
+            r.wts[lane] = __fdiv_rn(pj, ws);
+#pragma unroll
+            for (int role = 0; role < 3; ++role) {
+                int64_t sl = r.g2s ? (int64_t) r.g2s[role * E + e] : e;
+                if (sl < 0 || sl >= r.n_slots[role]) {
+                    report(r.st, QWB_DEVERR_ID_RANGE, (int32_t) sl);
+                    sl = -1;
+                }
+                r.slots[role * k + lane] = (int32_t) sl;
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kRouterThreads) router_decode_kernel(const RouterDecodeArgs r) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *bar = (uint64_t *) smem;
+    const int64_t H = r.H;
+    const int rpc = (int) ceil_div(r.E, kRouterCluster);  // rows per CTA
+    RouterSmemTail &tail = *(RouterSmemTail *) (smem + 128);
+    float *rows = (float *) (smem + 128 + align_up(sizeof(RouterSmemTail), 128));  // [rpc][H]
+    float *xs = rows + (size_t) rpc * H;  // [H] x, normalised in place
+    float *gw = xs + H;                   // [H] ffn_norm weight
+    __shared__ double dpart[kRouterThreads / 32];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rank_in_cluster = (int) cluster.block_rank();
+    const int e0 = rank_in_cluster * rpc;
+    const int ne = max(0, min(rpc, (int) r.E - e0));
+
+    QWB_TRACE(0, 0);
+    if (tid == 0) {
+        mbar_init(&bar[0], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {  // router rows and the norm weight do not depend on the previous kernel
+        const uint32_t rbytes = (uint32_t) (ne * H * 4), gbytes = r.norm_w ? (uint32_t) (H * 4) : 0u;
+        mbar_arrive_expect_tx(&bar[0], rbytes + gbytes);
+        if (rbytes) bulk_span_issue(rows, r.router_w + (int64_t) e0 * H, rbytes, &bar[0]);
+        if (r.norm_w) bulk_span_issue(gw, r.norm_w, gbytes, &bar[0]);
+    }
+    pdl_trigger();
+    pdl_wait();  // x is the previous layer's output
+    QWB_TRACE(0, 1);
+
+    // x -> shared memory, sum of squares (f32 squares, f64 sum as ggml's rms_norm)
+    double acc = 0.0;
+    for (int64_t i = 4 * tid; i < H; i += 4 * kRouterThreads) {
+        const float4 b = *(const float4 *) (r.x + i);
+        *(float4 *) (xs + i) = b;
+        acc += (double) __fmul_rn(b.x, b.x);
+        acc += (double) __fmul_rn(b.y, b.y);
+        acc += (double) __fmul_rn(b.z, b.z);
+        acc += (double) __fmul_rn(b.w, b.w);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) dpart[warp] = acc;
+    bool ok = mbar_wait(&bar[0], 0);
+    ok = __syncthreads_and(ok);
+    QWB_TRACE(0, 2);
+    if (!ok && tid == 0) {  // copies never landed: record it, drain; these rows route as -inf
+        report(r.st, QWB_DEVERR_TIMEOUT, rank_in_cluster);
+        mbar_wait(&bar[0], 0);
+    }
+    if (r.norm_w) {
+        double sum = 0.0;
+        for (int i = 0; i < kRouterThreads / 32; ++i) sum += dpart[i];
+        const float mean = (float) (sum / (double) H);
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, r.norm_eps)));
+        for (int64_t i = 4 * tid; i < H; i += 4 * kRouterThreads) {
+            float4 b = *(const float4 *) (xs + i);
+            const float4 g = *(const float4 *) (gw + i);
+            b.x = __fmul_rn(__fmul_rn(b.x, scale), g.x);
+            b.y = __fmul_rn(__fmul_rn(b.y, scale), g.y);
+            b.z = __fmul_rn(__fmul_rn(b.z, scale), g.z);
+            b.w = __fmul_rn(__fmul_rn(b.w, scale), g.w);
+            *(float4 *) (xs + i) = b;
+        }
+        __syncthreads();
+    }
+    QWB_TRACE(0, 3);
+    // logits of this CTA's rows (one warp per row, rows strided over warps), stored in CTA 0
+    float *logit0 = cluster.map_shared_rank(tail.logit, 0);
+    for (int er = warp; er < ne; er += kRouterThreads / 32) {
+        const float *wr = rows + (int64_t) er * H;
+        float a0 = 0.f, a1 = 0.f;
+        for (int h = 4 * lane; h < (int) H; h += 256) {
+            const float4 w4 = *(const float4 *) (wr + h);
+            const float4 x4 = *(const float4 *) (xs + h);
+            a0 = fmaf(w4.x, x4.x, a0);
+            a0 = fmaf(w4.y, x4.y, a0);
+            a0 = fmaf(w4.z, x4.z, a0);
+            a0 = fmaf(w4.w, x4.w, a0);
+            if (h + 128 < (int) H) {
+                const float4 w5 = *(const float4 *) (wr + h + 128);
+                const float4 x5 = *(const float4 *) (xs + h + 128);
+                a1 = fmaf(w5.x, x5.x, a1);
+                a1 = fmaf(w5.y, x5.y, a1);
+                a1 = fmaf(w5.z, x5.z, a1);
+                a1 = fmaf(w5.w, x5.w, a1);
+            }
+        }
+        const float a = warp_sum(a0 + a1);
+        if (lane == 0) logit0[e0 + er] = ok ? a : -INFINITY;
+    }
+    cluster.sync();  // every logit is in CTA 0's shared memory
+    QWB_TRACE(0, 4);
+    if (rank_in_cluster != 0) {
+        // side work of CTAs 1..: Q8 of the normed x, one 256-chunk per warp (needed by the
+        // next kernel, which waits for this grid to complete)
+        const int64_t c = (int64_t) (rank_in_cluster - 1) * (kRouterThreads / 32) + warp;
+        if (c < H / 256) quantize_chunk_warp(r.kq ? 0 : 1, xs + c * 256, r.xq, 0, c * 256, H);
+        return;
+    }
+    route_in_cta(r, tail);
+}
+
+// ---------------------------------------------------------------- gate/up
+template <int NSB>
+__global__ void __launch_bounds__(kDecodeThreads, 2) gateup_decode_kernel(const GateUpDecodeArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *bar = (uint64_t *) smem;  // [kChunks]
+    uint8_t *buf = smem + 128;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t P = (int64_t) a.n_used * a.F;
+    const int64_t p0 = P * blockIdx.x / gridDim.x, p1 = P * (blockIdx.x + 1) / gridDim.x;
+    const int n = (int) (p1 - p0);
+    const int rb = (int) a.row_bytes;
+    const int nch = min(kDecodeChunks, max(1, n));
+    auto chunk_lo = [&](int c) { return (int) ((int64_t) n * c / nch); };
+    __shared__ int s_sg[32], s_su[32];
+
+    QWB_TRACE(1, 0);
+    if (tid == 0) {
+        for (int c = 0; c < nch; ++c) mbar_init(&bar[c], 1);
+        fence_mbar_init();
+    }
+    pdl_wait();  // the routing and the quantized x are ready
+    QWB_TRACE(1, 1);
+    if (tid < a.n_used) {  // validated by the router (-1: invalid)
+        const int sg = a.slots[tid], su = a.slots[a.n_used + tid];
+        const bool ok = sg >= 0 && sg < a.n_slots_g && su >= 0 && su < a.n_slots_u;
+        s_sg[tid] = ok ? sg : -1;
+        s_su[tid] = ok ? su : -1;
+    }
+    __syncthreads();
+    if (tid < nch) {  // thread c issues chunk c
+        const int c = tid;
+        const int c0 = chunk_lo(c), c1 = chunk_lo(c + 1), nc = c1 - c0;
+        uint8_t *cb = buf + (size_t) 2 * c0 * rb;
+        uint32_t bytes = 0;
+        const int F = (int) a.F;
+        for (int pass = 0; pass < 2; ++pass) {  // pass 0 counts, pass 1 issues
+            if (pass == 1) mbar_arrive_expect_tx(&bar[c], bytes);
+            int j = (int) ((p0 + c0) / F), r = (int) ((p0 + c0) % F);
+            for (int off = 0; off < nc;) {
+                const int len = min(nc - off, F - r);
+                const int sg = s_sg[j], su = s_su[j];
+                if (sg >= 0) {
+                    if (pass == 0) bytes += 2u * (uint32_t) (len * rb);
+                    else {
+                        bulk_span_issue(cb + off * rb, a.Wg + (size_t) sg * a.g_nb2 + (size_t) r * rb,
+                                        (size_t) len * rb, &bar[c]);
+                        bulk_span_issue(cb + (size_t) (nc + off) * rb, a.Wu + (size_t) su * a.u_nb2 + (size_t) r * rb,
+                                        (size_t) len * rb, &bar[c]);
+                    }
+                }
+                off += len;
+                r = 0;
+                ++j;
+            }
+        }
+    }
+    QWB_TRACE(1, 2);
+    pdl_trigger();  // the down kernel may start copying its weights now
+
+    // the activation superblock of this lane (x has one row: T == 1)
+    const int s = lane % NSB;
+    ActReg<false> act;
+    load_act<false>(act, a.xq.qs + (int64_t) s * 256, a.xq.bsum + s * 16, a.xq.d[s]);
+    QWB_TRACE(1, 3);
+
+    constexpr int RPW = 32 / (2 * NSB);  // (gate, up) row pairs per warp step
+    const int pp_in = lane / (2 * NSB), mat = (lane / NSB) & 1;
+    const int F = (int) a.F;
+    const int j_first = (int) (p0 / F), r_first = (int) (p0 % F);  // expert/row of the CTA's first pair
+    const uint32_t buf_sa = smem_u32(buf);
+    bool alive = true;
+    for (int c = 0; c < nch; ++c) {
+        const int c0 = chunk_lo(c), c1 = chunk_lo(c + 1), nc = c1 - c0;
+        const uint32_t cb = buf_sa + (uint32_t) (2 * c0 * rb);
+        if (!mbar_wait(&bar[c], 0)) {
+            if (lane == 0) report(a.st, QWB_DEVERR_TIMEOUT, c);
+            alive = false;
+            break;
+        }
+        if (c == 0) QWB_TRACE(1, 4);
+        for (int g = warp; g * RPW < nc; g += kDecodeThreads / 32) {
+            const int i = g * RPW + pp_in;  // row pair within the chunk
+            int j = j_first, r = r_first + c0 + i;
+            while (r >= F) { r -= F; ++j; }
+            float v = 0.f;
+            if (i < nc && s_sg[j] >= 0)
+                v = dot_q4K_sb(buf + (cb - buf_sa) + (uint32_t) ((mat * nc + i) * rb) + (uint32_t) (s * Q4K_BYTES), act);
+#pragma unroll
+            for (int o = 1; o < NSB; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            const float up = __shfl_down_sync(0xffffffffu, v, NSB);
+            if (i < nc && mat == 0 && s == 0) a.act[j * F + r] = swiglu_f(v, up);
+        }
+    }
+    QWB_TRACE(1, 5);
+    // a timed-out wait leaves copies possibly in flight: drain them before the CTA exits
+    if (!__syncthreads_and(alive) && tid == 0)
+        for (int c = 0; c < nch; ++c) mbar_wait(&bar[c], 0);
+    QWB_TRACE(1, 6);
+}
+
+// ---------------------------------------------------------------- down
+// bytes reserved per expert weight span: the CTA's rows plus the 16-byte widening,
+// rounded to 16 mod 128 so consecutive experts start on different shared-memory banks
+__host__ __device__ inline size_t down_span_stride(int n, size_t rb) {
+    const size_t b = align_up((size_t) n * rb + 32, 16);
+    return align_up(b + 112, 128) + 16;
+}
+
+// Warp w handles selected expert j = w (and j + 8, ... when more experts than warps);
+// lane = (row, superblock): 32 / NSB rows per warp step.  Expert j's rows of this CTA are
+// one bulk copy completing on barrier j, issued by thread j.  Each warp quantizes its
+// expert's act row into its own shared-memory scratch and keeps its lane's superblock in
+// registers; per-(expert, row) partial sums meet in shared memory and the weighted sum
+// over experts runs in expert order, so the result does not depend on scheduling.
+template <int TYPE, int NSB>
+__global__ void __launch_bounds__(kDecodeThreads, 2) down_decode_kernel(const DownDecodeArgs a) {
+    constexpr bool KQ6 = TYPE == QWB_TYPE_Q6_K;
+    constexpr int SBB = KQ6 ? Q6K_BYTES : Q4K_BYTES;
+    constexpr int NW = kDecodeThreads / 32;
+    constexpr int RPS = 32 / NSB;  // rows per warp step
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *bar = (uint64_t *) smem;  // [n_used] (<= 32)
+    __shared__ int s_slot[32];
+    __shared__ float s_w[32];
+    __shared__ int s_off[32];  // misalignment of each expert's span
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nu = a.n_used;
+    const int64_t h0 = a.H * blockIdx.x / gridDim.x, h1 = a.H * (blockIdx.x + 1) / gridDim.x;
+    const int n = (int) (h1 - h0);
+    const size_t rb = a.row_bytes;
+    // shared memory: [bars 256][act Q8_K: NW warps x NSB superblocks x 320 B]
+    //                [partials: nu x n floats][weight spans, one per expert]
+    uint8_t *actq = smem + 256;
+    float *part = (float *) (actq + (size_t) NW * NSB * 320);
+    uint8_t *wbuf = (uint8_t *) part + align_up((size_t) nu * n * 4, 128);
+    const size_t span_stride = down_span_stride(n, rb);
+
+    QWB_TRACE(2, 0);
+    // the router grid completed before the gate/up grid passed its wait, so its outputs
+    // are visible here while gate/up is still running
+    if (tid < nu) {
+        const int sl = a.slots[tid];
+        s_slot[tid] = (sl >= 0 && sl < a.n_slots) ? sl : -1;
+        s_w[tid] = a.wts[tid];
+        mbar_init(&bar[tid], 1);
+    }
+    fence_mbar_init();
+    __syncthreads();
+    if (tid < nu) {  // thread j copies expert j's rows
+        const int j = tid;
+        if (s_slot[j] >= 0) {
+            const uint8_t *src = a.W + (size_t) s_slot[j] * a.nb2 + (size_t) h0 * rb;
+            mbar_arrive_expect_tx(&bar[j], bulk_span_bytes(src, (size_t) n * rb));
+            s_off[j] = (int) bulk_span_issue(wbuf + (size_t) j * span_stride, src, (size_t) n * rb, &bar[j]);
+        } else {
+            s_off[j] = 0;
+            mbar_arrive_expect_tx(&bar[j], 0);
+        }
+    }
+    QWB_TRACE(2, 1);
+    pdl_trigger();  // the next layer's router may prefetch its rows
+    pdl_wait();     // act (gate/up output) is ready
+    QWB_TRACE(2, 2);
+    __syncthreads();  // s_off visible
+
+    const int li = lane / NSB, ls = lane % NSB;
+    bool alive = true;
+    for (int j = warp; j < nu; j += NW) {
+        // this warp's expert: act row -> Q8_K superblocks in its scratch -> lane registers;
+        // all NSB superblocks' inputs are loaded before quantizing (one L2 round trip)
+        uint8_t *scr = actq + (size_t) warp * NSB * 320;
+        float xv[NSB][8];
+#pragma unroll
+        for (int sb = 0; sb < NSB; ++sb) load8_normed(a.act + (int64_t) j * a.F + sb * 256, 1.f, nullptr, lane, xv[sb]);
+        __syncwarp();
+#pragma unroll
+        for (int sb = 0; sb < NSB; ++sb)
+            q8K_block_vals(xv[sb], nullptr, (int8_t *) (scr + sb * 320), (float *) (scr + sb * 320 + 256),
+                           (int16_t *) (scr + sb * 320 + 272));
+        __syncwarp();
+        if (j == 0) QWB_TRACE(2, 3);
+        ActReg<KQ6> act;
+        {
+            const uint8_t *src = scr + (size_t) ls * 320;
+            load_act<KQ6>(act, (const int8_t *) src, (const int16_t *) (src + 272), *(const float *) (src + 256));
+        }
+        const bool valid = s_slot[j] >= 0;
+        if (!mbar_wait(&bar[j], 0)) {
+            if (lane == 0) report(a.st, QWB_DEVERR_TIMEOUT, j);
+            alive = false;
+            continue;
+        }
+        if (j == 0) QWB_TRACE(2, 4);
+        const uint8_t *span = wbuf + (size_t) j * span_stride + s_off[j];
+        for (int i0 = 0; i0 < n; i0 += RPS) {
+            const int i = i0 + li;
+            float v = 0.f;
+            if (valid && li < RPS && i < n) {
+                const uint8_t *sb = span + (size_t) i * rb + (size_t) ls * SBB;
+                if constexpr (KQ6) v = dot_q6K_sb(sb, act);
+                else v = dot_q4K_sb(sb, act);
+            }
+            // sum the NSB superblocks of each row (lanes li*NSB .. li*NSB + NSB-1)
+            float tot = 0.f;
+#pragma unroll
+            for (int q = 0; q < NSB; ++q) tot += __shfl_sync(0xffffffffu, v, (li < RPS ? li : 0) * NSB + q);
+            if (ls == 0 && li < RPS && i < n) part[(size_t) j * n + i] = tot;
+        }
+    }
+    QWB_TRACE(2, 5);
+    const bool all_ok = __syncthreads_and(alive);
+    if (all_ok) {
+        for (int r = tid; r < n; r += kDecodeThreads) {
+            float acc = 0.f;
+            for (int j = 0; j < nu; ++j)
+                if (s_slot[j] >= 0) acc = fmaf(s_w[j], part[(size_t) j * n + r], acc);
+            const int64_t h = h0 + r;
+            a.out[h] = a.residual ? acc + a.residual[h] : acc;
+        }
+    } else if (tid < nu) {
+        mbar_wait(&bar[tid], 0);  // drain copies still in flight before the CTA exits
+    }
+    QWB_TRACE(2, 6);
+}
+
+// ---------------------------------------------------------------- launches
+template <typename Kern, typename Args>
+static cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const Args &args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args);
+}
+
+template <typename Kern>
+static cudaError_t set_smem(Kern kern, size_t smem) {
+    if (smem <= 48 * 1024) return cudaSuccess;
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+}
+
+size_t router_decode_smem(const RouterDecodeArgs &r) {
+    const int64_t rpc = ceil_div(r.E, kRouterCluster);
+    return 128 + align_up(sizeof(RouterSmemTail), 128) + (size_t) (rpc + 2) * r.H * 4;
+}
+
+cudaError_t launch_router_decode(const RouterDecodeArgs &r, cudaStream_t s) {
+    const size_t smem = router_decode_smem(r);
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(router_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    cudaError_t e = set_smem(router_decode_kernel, smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kRouterCluster);
+    cfg.blockDim = dim3(kRouterThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = kRouterCluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, router_decode_kernel, r);
+}
+
+bool gateup_decode_supported(int type, int64_t K, size_t row_bytes, size_t nb1, int64_t F, int n_used) {
+    if (type != QWB_TYPE_Q4_K || nb1 != row_bytes) return false;
+    if (K != 2048 && K != 4096) return false;
+    const int64_t per_cta = ceil_div((int64_t) n_used * F, num_sms());
+    return (size_t) per_cta * 2 * row_bytes + 128 <= 200 * 1024;
+}
+
+cudaError_t launch_gateup_decode(const GateUpDecodeArgs &a, cudaStream_t s) {
+    const int G = num_sms();
+    const int64_t per_cta = ceil_div((int64_t) a.n_used * a.F, G);
+    const size_t smem = 128 + (size_t) per_cta * 2 * a.row_bytes;
+    if (a.K == 2048) {
+        cudaError_t e = set_smem(gateup_decode_kernel<8>, smem);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(gateup_decode_kernel<8>, dim3(G), dim3(kDecodeThreads), smem, s, a);
+    }
+    cudaError_t e = set_smem(gateup_decode_kernel<16>, smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(gateup_decode_kernel<16>, dim3(G), dim3(kDecodeThreads), smem, s, a);
+}
+
+static size_t down_decode_smem(int64_t H, int n_used, int nsb, size_t rb) {
+    const int64_t n = ceil_div(H, num_sms());
+    return 256 + (size_t) (kDecodeThreads / 32) * nsb * 320 + align_up((size_t) n_used * n * 4, 128) +
+           (size_t) n_used * down_span_stride((int) n, rb);
+}
+
+bool down_decode_supported(int type, int64_t F, int64_t H, size_t row_bytes, size_t nb1, int n_used) {
+    if ((type != QWB_TYPE_Q4_K && type != QWB_TYPE_Q6_K) || nb1 != row_bytes) return false;
+    const int nsb = (int) (F / 256);
+    if (nsb != 3 || n_used * nsb > 32) return false;
+    return down_decode_smem(H, n_used, nsb, row_bytes) <= 220 * 1024;
+}
+
+cudaError_t launch_down_decode(int type, const DownDecodeArgs &a, cudaStream_t s) {
+    const int G = num_sms();
+    const size_t smem = down_decode_smem(a.H, a.n_used, 3, a.row_bytes);
+    if (type == QWB_TYPE_Q6_K) {
+        cudaError_t e = set_smem(down_decode_kernel<QWB_TYPE_Q6_K, 3>, smem);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(down_decode_kernel<QWB_TYPE_Q6_K, 3>, dim3(G), dim3(kDecodeThreads), smem, s, a);
+    }
+    cudaError_t e = set_smem(down_decode_kernel<QWB_TYPE_Q4_K, 3>, smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(down_decode_kernel<QWB_TYPE_Q4_K, 3>, dim3(G), dim3(kDecodeThreads), smem, s, a);
+}
+
+}  // namespace qwb
+
+#ifdef QWB_DECODE_TRACE
+extern "C" QWB_API int qwb_debug_decode_trace(void *host, size_t bytes) {
+    return cudaMemcpyFromSymbol(host, qwb::g_decode_trace, bytes) == cudaSuccess ? 0 : 1;
+}
+#endif

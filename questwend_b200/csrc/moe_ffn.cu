@@ -15,6 +15,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "decode.cuh"
 #include "dot.cuh"
 #include "kernels.cuh"
 #include "mmid.cuh"
@@ -189,7 +190,7 @@ struct FfnPlan {
     bool kq_gu, kq_d;
     int NT;
     int64_t P;
-    size_t off_logits, off_sel, off_w, off_xq, off_index, off_act, off_xn, off_actq, off_experts, total;
+    size_t off_logits, off_sel, off_w, off_slots, off_xq, off_index, off_act, off_xn, off_actq, off_experts, total;
 };
 
 static qwb_status plan_ffn(const qwb_moe_ffn_desc *d, FfnPlan &p) {
@@ -213,6 +214,7 @@ static qwb_status plan_ffn(const qwb_moe_ffn_desc *d, FfnPlan &p) {
     p.off_logits = o; o += align_up((size_t) (d->T * d->E) * 4, 256);
     p.off_sel = o; o += align_up((size_t) p.P * 4, 256);
     p.off_w = o; o += align_up((size_t) p.P * 4, 256);
+    p.off_slots = o; o += align_up((size_t) 3 * d->n_used * 4, 256);
     p.off_xq = o; o += planes_bytes(d->T, d->H, p.kq_gu);
     p.off_index = o; o += mmid_index_bytes(std::max<int64_t>(p.P, 1), d->E, p.NT);
     p.off_act = o; o += align_up((size_t) p.P * d->F * 4, 256);
@@ -272,6 +274,40 @@ extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, s
 
     const bool decode = T == 1;
     profile_mark(s, 0);
+    if (decode && E <= kMaxRouteE && E >= kRouterCluster && (E % kRouterCluster) == 0 && K <= 32 &&
+        gateup_decode_supported(d->gate.type, H, row_bytes(d->gate.type, H), d->gate.nb[1], F, (int) K) &&
+        d->up.nb[1] == d->gate.nb[1] &&
+        down_decode_supported(d->down.type, F, H, row_bytes(d->down.type, F), d->down.nb[1], (int) K)) {
+        // batch-1 decode: three PDL-chained kernels (decode.cu)
+        int32_t *slots = (int32_t *) (w + p.off_slots);
+        RouterDecodeArgs r{};
+        r.x = d->x; r.router_w = d->router_w; r.mask = d->mask; r.norm_w = d->norm_w; r.norm_eps = d->norm_eps;
+        r.H = H; r.E = E; r.n_used = (int) K;
+        r.g2s = d->g2s;
+        r.n_slots[0] = d->gate.ne[2]; r.n_slots[1] = d->up.ne[2]; r.n_slots[2] = d->down.ne[2];
+        r.sel = sel; r.wts = wts; r.slots = slots;
+        r.xq = xq; r.kq = 1;
+        r.st = st;
+        e = launch_router_decode(r, s);
+        if (e != cudaSuccess) return QWB_ERR_CUDA;
+        profile_mark(s, QWB_KERNEL_ROUTER);
+        GateUpDecodeArgs g{};
+        g.Wg = (const uint8_t *) d->gate.data; g.Wu = (const uint8_t *) d->up.data;
+        g.g_nb2 = d->gate.nb[2]; g.u_nb2 = d->up.nb[2]; g.row_bytes = row_bytes(d->gate.type, H);
+        g.F = F; g.K = H; g.n_slots_g = d->gate.ne[2]; g.n_slots_u = d->up.ne[2];
+        g.n_used = (int) K; g.slots = slots; g.xq = xq; g.act = act; g.st = st;
+        e = launch_gateup_decode(g, s);
+        if (e != cudaSuccess) return QWB_ERR_CUDA;
+        profile_mark(s, QWB_KERNEL_GATE_UP);
+        DownDecodeArgs dn{};
+        dn.W = (const uint8_t *) d->down.data; dn.nb2 = d->down.nb[2]; dn.row_bytes = row_bytes(d->down.type, F);
+        dn.F = F; dn.H = H; dn.n_slots = d->down.ne[2]; dn.n_used = (int) K;
+        dn.slots = slots + 2 * K; dn.wts = wts; dn.act = act; dn.out = d->out; dn.residual = d->residual; dn.st = st;
+        e = launch_down_decode(d->down.type, dn, s);
+        if (e != cudaSuccess) return QWB_ERR_CUDA;
+        profile_mark(s, QWB_KERNEL_DOWN);
+        return QWB_OK;
+    }
     if (T <= kMaxRouterT) {
         RouterArgs r{};
         r.x = d->x; r.router_w = d->router_w; r.mask = d->mask;

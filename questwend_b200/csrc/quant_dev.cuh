@@ -26,11 +26,18 @@ __device__ __forceinline__ void load8_normed(const float *x, float nscale, const
 
 // One warp quantizes one 256-value Q8_K block; lane l owns values [8l, 8l+8).
 // Outputs (any may be null): packed block_q8_K, or plane qs/d/bsum.
+__device__ __forceinline__ void q8K_block_vals(const float v[8], uint8_t *packed, int8_t *pqs, float *pd,
+                                               int16_t *pbsum);
 __device__ __forceinline__ void q8K_block_warp(const float *x, uint8_t *packed, int8_t *pqs, float *pd,
                                                int16_t *pbsum, float nscale = 1.f, const float *nw = nullptr) {
-    const int lane = threadIdx.x & 31;
     float v[8];
-    load8_normed(x, nscale, nw, lane, v);
+    load8_normed(x, nscale, nw, threadIdx.x & 31, v);
+    q8K_block_vals(v, packed, pqs, pd, pbsum);
+}
+// Same, on values already loaded: lane l holds values [8l, 8l+8) of the block.
+__device__ __forceinline__ void q8K_block_vals(const float v[8], uint8_t *packed, int8_t *pqs, float *pd,
+                                               int16_t *pbsum) {
+    const int lane = threadIdx.x & 31;
     // local first-max of |x|
     float lam = 0.f, lmx = 0.f;
 #pragma unroll

@@ -146,3 +146,39 @@ def test_moe_ffn_with_ffn_norm(qwb, T):
     assert O.nrmse(act, r["act"]) <= TOL
     e = O.nrmse(out.cpu().numpy() - x, r["out"])
     assert e <= 3e-4, e
+
+
+@pytest.mark.parametrize("td", [O.Q6_K, O.Q4_K])
+def test_moe_ffn_decode_slot_pool(qwb, td):
+    """Batch-1 decode on expert-slot pools (the cached fast path: ids remapped through the
+    per-role g2s tables, pools larger than the expert count, roles in different slots),
+    config-1 shapes, with ffn_norm and residual."""
+    H, F, E, k, n_slots = 2048, 768, 32, 8, 48
+    rng = D.rng(90)
+    rw = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    nw = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    g = D.weights(O.Q4_K, E, F, H, seed=91)
+    u = D.weights(O.Q4_K, E, F, H, seed=92)
+    d = D.weights(td, E, H, F, seed=93)
+    g2s = np.stack([rng.permutation(n_slots)[:E] for _ in range(3)]).astype(np.int32)
+    pools, host_pools = [], []
+    for role, (wt, t, rows, K) in enumerate(((g, O.Q4_K, F, H), (u, O.Q4_K, F, H), (d, td, H, F))):
+        rs = O.row_size(t, K) * rows
+        p = np.zeros(n_slots * rs, np.uint8)
+        for e in range(E):
+            p[g2s[role, e] * rs:(g2s[role, e] + 1) * rs] = wt[e * rs:(e + 1) * rs]
+        host_pools.append(p)
+        pools.append(qwb.QTensor.from_bytes(p, t, (K, rows, n_slots)))
+    for step in range(3):  # repeated calls reuse the workspace (router counter protocol)
+        x = D.acts((1, H), seed=94 + step) * np.float32(2.0)
+        act = torch.empty((1, k, F), device="cuda")
+        out, sel, w = qwb.moe_ffn(cu(x), cu(rw), *pools, k, g2s=cu(g2s), residual=cu(x), act=act,
+                                  norm_w=cu(nw), norm_eps=1e-6)
+        r = O.moe_layer(x, rw, O.Q4_K, host_pools[0], host_pools[1], td, host_pools[2], F, n_slots, k,
+                        g2s=g2s, want_act=True, norm_w=nw, norm_eps=1e-6)
+        sel = sel.cpu().numpy()
+        assert np.array_equal(sel, r["selected"])
+        assert O.nrmse(act.cpu().numpy(), r["act"]) <= TOL
+        e = O.nrmse(out.cpu().numpy() - x, r["out"])
+        assert e <= 3e-4, (step, e)
+    assert qwb.read_status()[0] == 0
