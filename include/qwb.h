@@ -217,8 +217,9 @@ QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *desc, void *workspace, si
 /* ------------------------------------------------------------- profiling hook
  * Optional per-kernel timing for benchmarks (no counterpart in the reference, whose
  * QWEN_PROF timers are host wall-clock, core/runtime.cpp:3720).  While enabled,
- * qwb_moe_ffn records a CUDA event on its stream before its first kernel ("mark" with
- * tag 0) and after each kernel (tag = QWB_KERNEL_*).  Event records are stream-capture
+ * qwb_moe_ffn and qwb_mul_mat_id record a CUDA event on their stream before the first
+ * kernel ("mark" with tag 0) and after each kernel or group of preparation kernels
+ * (tag = QWB_KERNEL_*).  Event records are stream-capture
  * safe: inside a captured CUDA graph they become event-record nodes and are re-recorded
  * on every replay, so after a replay qwb_profile_read returns that replay's durations.
  * Not thread-safe; one profiling session per process. */
@@ -226,6 +227,7 @@ QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *desc, void *workspace, si
 #define QWB_KERNEL_GATE_UP 2
 #define QWB_KERNEL_DOWN 3
 #define QWB_KERNEL_OTHER 4
+#define QWB_KERNEL_GROUPED_GEMM 5 /* tensor-core grouped expert GEMM (many tokens per expert) */
 QWB_API qwb_status qwb_profile_enable(int max_marks); /* creates the events; 0 disables */
 QWB_API qwb_status qwb_profile_reset(void);           /* next mark is mark 0 */
 QWB_API int qwb_profile_count(void);                  /* marks recorded since reset */

@@ -19,6 +19,7 @@
 #include "dot.cuh"
 #include "kernels.cuh"
 #include "mmid.cuh"
+#include "prefill.cuh"
 
 namespace qwb {
 
@@ -301,8 +302,10 @@ int pick_nt(int64_t pairs, int64_t n_as) {
     return 8;
 }
 
+int64_t mmid_max_tiles(int64_t P, int64_t n_as, int NT) { return P / NT + std::min<int64_t>(P, n_as) + 1; }
+
 size_t mmid_index_bytes(int64_t P, int64_t n_as, int NT) {
-    const int64_t max_tiles = P / NT + std::min<int64_t>(P, n_as) + 1;
+    const int64_t max_tiles = mmid_max_tiles(P, n_as, NT);
     return align_up(256, 256) + align_up((size_t) P * 4, 256) + align_up((size_t) max_tiles * 16, 256);
 }
 MmidIndex mmid_index_at(void *base, int64_t P, int64_t n_as, int NT) {
@@ -313,7 +316,7 @@ MmidIndex mmid_index_at(void *base, int64_t P, int64_t n_as, int NT) {
     ix.pairs = (int *) c;
     c += align_up((size_t) P * 4, 256);
     ix.tiles = (int4 *) c;
-    ix.max_tiles = (int) (P / NT + std::min<int64_t>(P, n_as) + 1);
+    ix.max_tiles = (int) mmid_max_tiles(P, n_as, NT);
     return ix;
 }
 
@@ -341,10 +344,12 @@ struct MmidPlan {
     int type, vdt;
     int64_t K, M, n_as, n_b, T, n_used, P;
     int NT;
-    size_t planes, index, total;
+    bool pf;  // tensor-core grouped GEMM (many tokens per expert)
+    size_t planes, index, btiles, da, total;
 };
 
-qwb_status plan_mmid(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor *ids, MmidPlan &p) {
+qwb_status plan_mmid(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor *ids, MmidPlan &p,
+                     bool allow_prefill) {
     if (!as || !b || !ids) return QWB_ERR_INVALID_ARG;
     if (as->type != QWB_TYPE_Q4_K && as->type != QWB_TYPE_Q6_K && as->type != QWB_TYPE_Q8_0)
         return QWB_ERR_UNSUPPORTED_TYPE;
@@ -366,27 +371,40 @@ qwb_status plan_mmid(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor
     if (p.K % block_elems(p.type) || p.K % block_elems(p.vdt)) return QWB_ERR_SHAPE;
     p.P = p.n_used * p.T;
     if (p.P > (1 << 24) || p.n_as > 16384 || p.K > (1 << 20) || p.M > (1 << 30)) return QWB_ERR_LIMIT;
-    p.NT = pick_nt(p.P, p.n_as);
+    p.pf = allow_prefill && pf_eligible(p.type, p.K, p.M, p.P, p.n_as);
+    p.NT = p.pf ? kPfTileN : pick_nt(p.P, p.n_as);
     p.planes = planes_bytes(p.n_b * p.T, p.K, p.vdt == QWB_TYPE_Q8_K);
     p.index = mmid_index_bytes(p.P, p.n_as, p.NT);
-    p.total = kCtrlBytes + p.planes + p.index;  // [0, 256) is the control block of the fused kernels
+    p.btiles = p.da = 0;
+    if (p.pf) {
+        const int64_t max_tiles = mmid_max_tiles(p.P, p.n_as, p.NT);
+        p.btiles = align_up((size_t) max_tiles * pf_btile_stride(p.K), 256);
+        p.da = align_up((size_t) max_tiles * pf_da_stride(p.K), 256);
+    }
+    // [0, 256) is the control block of the fused kernels
+    p.total = kCtrlBytes + p.planes + p.index + p.btiles + p.da;
     return QWB_OK;
 }
 
 }  // namespace
 
+size_t qwb::mul_mat_id_workspace(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor *ids,
+                                 bool allow_prefill) {
+    MmidPlan p;
+    if (plan_mmid(as, b, ids, p, allow_prefill) != QWB_OK) return 0;
+    return p.total;
+}
+
 extern "C" QWB_API size_t qwb_mul_mat_id_workspace_size(const qwb_tensor *as, const qwb_tensor *b,
                                                         const qwb_tensor *ids) {
-    MmidPlan p;
-    if (plan_mmid(as, b, ids, p) != QWB_OK) return 0;
-    return p.total;
+    return qwb::mul_mat_id_workspace(as, b, ids, true);
 }
 
 qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor *ids,
                                 const qwb_tensor *dst, void *ws, size_t ws_bytes, qwb_status_block *st,
-                                cudaStream_t s) {
+                                cudaStream_t s, bool allow_prefill) {
     MmidPlan p;
-    qwb_status rc = plan_mmid(as, b, ids, p);
+    qwb_status rc = plan_mmid(as, b, ids, p, allow_prefill);
     if (rc != QWB_OK) return rc;
     if (!dst || dst->type != QWB_TYPE_F32) return dst ? QWB_ERR_UNSUPPORTED_TYPE : QWB_ERR_INVALID_ARG;
     if (dst->ne[0] != p.M || dst->ne[1] != p.n_used || dst->ne[2] != p.T || dst->ne[3] != 1) return QWB_ERR_SHAPE;
@@ -407,6 +425,7 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
     if (b->nb[2] != b->nb[1] * (size_t) p.n_b) return QWB_ERR_LAYOUT;  // rows (j, t) at stride nb1
 
     const bool kq = p.vdt == QWB_TYPE_Q8_K;
+    profile_mark(s, 0);
     Q8Planes pl = planes_at((char *) ws + kCtrlBytes, p.n_b * p.T, p.K, kq);
     MmidIndex ix = mmid_index_at((char *) ws + kCtrlBytes + p.planes, p.P, p.n_as, p.NT);
     cudaError_t e = launch_quantize_rows(kq ? 0 : 1, (const float *) b->data, (int64_t) (b->nb[1] / 4),
@@ -416,6 +435,37 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
                      (int) p.n_used, (int) p.T, (int) p.n_as, p.NT, ix, (float *) dst->data, dst->nb[1], dst->nb[2],
                      p.M, st, s);
     if (e != cudaSuccess) return QWB_ERR_CUDA;
+    if (p.pf) {
+        uint8_t *bt = (uint8_t *) ws + kCtrlBytes + p.planes + p.index;
+        float *da = (float *) (bt + p.btiles);
+        e = launch_pf_gather(pl, p.K, ix.tiles, ix.n_tiles, ix.max_tiles, ix.pairs, (int) p.n_used, (int) p.n_b, bt,
+                             da, s);
+        if (e != cudaSuccess) return QWB_ERR_CUDA;
+        profile_mark(s, QWB_KERNEL_OTHER);
+        PrefillArgs a{};
+        a.W = (const uint8_t *) as->data;
+        a.nb1 = as->nb[1];
+        a.nb2 = as->nb[2];
+        a.M = p.M;
+        a.K = p.K;
+        a.remap = nullptr;
+        a.n_ids = p.n_as;
+        a.n_slots = p.n_as;
+        a.tiles = ix.tiles;
+        a.n_tiles = ix.n_tiles;
+        a.pairs = ix.pairs;
+        a.btiles = bt;
+        a.da = da;
+        a.dst = (float *) dst->data;
+        a.dnb1 = dst->nb[1];
+        a.dnb2 = dst->nb[2];
+        a.n_used = (int) p.n_used;
+        a.m_tiles = (int) ceil_div(p.M, kPfTileM);
+        a.st = st;
+        e = launch_pf_gemm_q4k(a, s);
+        profile_mark(s, QWB_KERNEL_GROUPED_GEMM);
+        return e == cudaSuccess ? QWB_OK : QWB_ERR_CUDA;
+    }
     GemvArgs a{};
     a.W = (const uint8_t *) as->data;
     a.nb1 = as->nb[1];

@@ -40,13 +40,18 @@ struct GemvArgs {
 void gemv_geometry(GemvArgs &a, int NT, bool glu);
 cudaError_t launch_gemv(int type, bool glu, GemvArgs a, int NT, int max_tiles, cudaStream_t s);
 int pick_nt(int64_t pairs, int64_t n_as);
+int64_t mmid_max_tiles(int64_t P, int64_t n_as, int NT);
 size_t mmid_index_bytes(int64_t P, int64_t n_as, int NT);
 MmidIndex mmid_index_at(void *base, int64_t P, int64_t n_as, int NT);
 cudaError_t launch_index(const int32_t *ids, int64_t s0, int64_t s1, int n_used, int T, int n_as, int NT,
                          MmidIndex ix, float *dst, size_t dnb1, size_t dnb2, int64_t M, qwb_status_block *st,
                          cudaStream_t s);
 
+// allow_prefill: take the tensor-core grouped GEMM when the problem has many tokens per
+// expert (its workspace is larger); false keeps the GEMV path for every size.
 qwb_status mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor *ids, const qwb_tensor *dst,
-                           void *ws, size_t ws_bytes, qwb_status_block *st, cudaStream_t s);
+                           void *ws, size_t ws_bytes, qwb_status_block *st, cudaStream_t s,
+                           bool allow_prefill = true);
+size_t mul_mat_id_workspace(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor *ids, bool allow_prefill);
 
 }  // namespace qwb

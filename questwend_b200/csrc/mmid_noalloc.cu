@@ -58,15 +58,16 @@ static qwb_status noalloc_scratch(void **out) {
 extern "C" QWB_API qwb_status qwb_mul_mat_id_noalloc(const qwb_tensor *as, const qwb_tensor *b,
                                                      const qwb_tensor *ids, const qwb_tensor *dst,
                                                      qwb_status_block *d_status, qwb_stream_t stream) {
-    const size_t need = qwb_mul_mat_id_workspace_size(as, b, ids);
+    // the GEMV path at every size: its workspace stays small enough for the scratch array
+    const size_t need = qwb::mul_mat_id_workspace(as, b, ids, false);
     if (need == 0) {
         // malformed arguments: let the regular entry point report the precise status
-        return qwb::mul_mat_id_impl(as, b, ids, dst, nullptr, 0, d_status, (cudaStream_t) stream);
+        return qwb::mul_mat_id_impl(as, b, ids, dst, nullptr, 0, d_status, (cudaStream_t) stream, false);
     }
     if (need > (size_t) QWB_NOALLOC_SCRATCH_BYTES) return QWB_ERR_LIMIT;
     void *scratch = nullptr;
     const qwb_status rc = qwb::noalloc_scratch(&scratch);
     if (rc != QWB_OK) return rc;
     return qwb::mul_mat_id_impl(as, b, ids, dst, scratch, (size_t) QWB_NOALLOC_SCRATCH_BYTES, d_status,
-                                (cudaStream_t) stream);
+                                (cudaStream_t) stream, false);
 }

@@ -24,3 +24,12 @@ def acts(shape, seed):
 
 def sha(a: np.ndarray) -> str:
     return hashlib.sha256(np.ascontiguousarray(a).view(np.uint8).tobytes()).hexdigest()[:16]
+
+
+def zipf_ids(T, E, n_used, seed, s=1.1):
+    """Skewed routing: logits = log Zipf(s) popularity (expert ranks in seeded random
+    order) + Gumbel noise, top-n_used per token -> int32 [T, n_used]."""
+    r = rng(seed)
+    pop = 1.0 / np.arange(1, E + 1, dtype=np.float64) ** s
+    logits = np.log(pop[r.permutation(E)])[None, :] + r.gumbel(size=(T, E))
+    return np.argsort(-logits, axis=1, kind="stable")[:, :n_used].astype(np.int32)
