@@ -115,6 +115,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity, ui
         : "memory");
     return ok != 0;
 }
+// One poll without a suspend-time hint: the hardware may hold the thread for a short,
+// implementation-defined window and returns as soon as the phase completes.  Used on
+// pipelines whose stages turn over every few hundred cycles.
+__device__ __forceinline__ bool mbar_try_wait_fast(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -16,12 +16,18 @@
 // Superblocks whose dmin/d ratio is too large for an fp16 min coefficient (d ~ 0) use
 // dmin as the row scale instead (see pf_row_mode).
 //
-// Work item = (token tile of one expert, 128 weight rows).  One persistent CTA per SM,
-// warp-specialised:
-//   warp 0      producer: bulk copies of the raw Q4_K rows and of the fp16 B tiles
-//   warp 1      TMEM allocation and the MMA-issuing thread
-//   warps 4-7   dequantisation of the raw rows into TMEM (A operand), one row per thread
-//   warps 8-15  epilogue: TMEM accumulator -> registers, per-superblock scale, store
+// Work item = (token tile of one expert, 256 weight rows), computed by a 2-CTA cluster with
+// the CTA-pair MMA (cta_group::2, M = 256): each CTA dequantises its 128 weight rows into
+// its own TMEM and loads its half of the token tile's fp16 B operand, so every B byte
+// fetched from L2 serves 256 weight rows.  One persistent CTA per SM, warp-specialised:
+//   warps 0-7   dequantisation of the raw rows into TMEM (A operand), one row per thread,
+//               one warpgroup per half superblock
+//   warps 8-15  epilogue: TMEM accumulator -> per-superblock scale -> running sums -> store
+//   warp 16     producer of the B halves and activation scales (bulk copies)
+//   warp 17     TMEM allocation; MMA issue (even CTA) / "B half landed" relay (odd CTA)
+// The dequantisers fetch their own raw rows with per-thread async copies (cp.async), kPfPre
+// superblocks ahead: a TMA box of 128 strided 144-byte rows is served row by row and
+// could not keep up.
 // Every wait is bounded; a timeout sets QWB_DEVERR_TIMEOUT and all roles drain and exit.
 #include "prefill.cuh"
 
@@ -55,7 +61,7 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(Q8Planes act, int64_t K,
     const int s = blockIdx.y;
     const int nsb = (int) (K / QK_K);
     const int4 tl = tiles[tile];
-    const int cnt = tl.z, Nt = (cnt + 15) & ~15;
+    const int cnt = tl.z, Nt = pf_tile_cols(cnt), Nh = Nt / 2;
     __shared__ __align__(16) uint8_t q[kPfTileN * kGatherRow];
     __shared__ __align__(16) int16_t bs[kPfTileN][16];
     const int tid = threadIdx.x;
@@ -97,8 +103,9 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(Q8Planes act, int64_t K,
     }
     __syncthreads();
 
-    // write both half-superblock stages in the core-matrix layout:
-    // element (n, p) at (p / 8) * Nt * 16 + n * 16 + (p % 8) * 2
+    // write both half-superblock stages; each stage holds two sub-tiles (tokens [0, Nt/2)
+    // for the even CTA of a pair, [Nt/2, Nt) for the odd one), each in the core-matrix
+    // layout: element (n, p) of sub-tile r at r*Nh*288 + (p / 8) * Nh * 16 + (n - r*Nh) * 16 + (p % 8) * 2
     uint8_t *tb = btiles + (size_t) tile * pf_btile_stride(K) + (size_t) (2 * s) * Nt * kPfHalfK * 2;
     const int chunks = 2 * 18 * Nt;
     for (int c = tid; c < chunks; c += 256) {
@@ -127,8 +134,9 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(Q8Planes act, int64_t K,
                 o[i] = lo | (hi << 16);
             }
         }
-        *(uint4 *) (tb + (size_t) h * Nt * kPfHalfK * 2 + (size_t) pc * Nt * 16 + (size_t) n * 16) =
-            make_uint4(o[0], o[1], o[2], o[3]);
+        const int r = n >= Nh, nr = n - r * Nh;
+        *(uint4 *) (tb + (size_t) h * Nt * kPfHalfK * 2 + (size_t) r * Nh * kPfHalfK * 2 + (size_t) pc * Nh * 16 +
+                    (size_t) nr * 16) = make_uint4(o[0], o[1], o[2], o[3]);
     }
 }
 
@@ -141,34 +149,76 @@ cudaError_t launch_pf_gather(Q8Planes act, int64_t K, const int4 *tiles, const i
 }
 
 // ------------------------------------------------------------------ GEMM
-constexpr int kPfThreads = 512;
-constexpr int kPfRawStages = 2, kPfBStages = 4, kPfAStages = 3;
-constexpr int kPfRawBytes = kPfTileM * Q4K_BYTES;      // 18432
-constexpr int kPfBBytes = kPfTileN * kPfHalfK * 2;     // 36864
-constexpr uint32_t kPfACols = 72;                      // 64 value columns + 8 min columns
-constexpr uint32_t kPfAccCols = 128;
-constexpr uint32_t kPfTmemCols = 512;                  // [0,256) accumulators, [256,472) A stages
-constexpr int kPfOffB = kPfRawStages * kPfRawBytes;
-constexpr int kPfOffBar = kPfOffB + kPfBStages * kPfBBytes;
-constexpr int kPfSmem = kPfOffBar + 256;
+// Optional pipeline timestamps (compiled in only with -DQWB_PF_TRACE; no effect on the
+// default build): CTA 0 records the global timer per role and per superblock.
+#ifdef QWB_PF_TRACE
+__device__ unsigned long long g_pf_trace[16][256];
+#define PF_TRACE(role, idx)                                                               \
+    do {                                                                                 \
+        if (blockIdx.x == 0 && (idx) < 256u) g_pf_trace[role][idx] = globaltimer_ns();   \
+    } while (0)
+#else
+#define PF_TRACE(role, idx) \
+    do {                    \
+    } while (0)
+#endif
 
+constexpr int kPfThreads = 576;  // 18 warps
+constexpr int kPfBStages = 6, kPfAStages = 3, kPfEpStages = 4;
+// raw weight bytes: each dequantiser thread copies (cp.async) its row's 16-byte header and
+// the 64 bytes of its half superblock, kPfPre superblocks ahead, into a private slot
+constexpr int kPfPre = 4;
+constexpr int kPfSlot = 80;
+constexpr int kPfRawStage = 256 * kPfSlot;                 // 20480 per superblock
+constexpr int kPfBBytes = (kPfTileN / 2) * kPfHalfK * 2;   // 18432: this CTA's half of the token tile
+constexpr uint32_t kPfACols = 72;                          // 64 value columns + 8 min columns
+constexpr uint32_t kPfAccCols = 128;
+constexpr uint32_t kPfTmemCols = 512;  // [0,256) accumulators, [256,472) A stages
+constexpr int kPfOffB = kPfPre * kPfRawStage;
+// epilogue ring, one slot per superblock: activation scales of the token tile (bulk copy)
+// and the weight rows' superblock scales (written by the dequantiser)
+constexpr int kPfOffEp = kPfOffB + kPfBStages * kPfBBytes;
+constexpr int kPfEpBytes = 2 * kPfTileN * 4;
+constexpr int kPfOffBar = kPfOffEp + kPfEpStages * kPfEpBytes;
+constexpr int kPfSmem = kPfOffBar + 512;
+
+// Barriers.  The CTA pair runs one MMA stream issued by the even CTA ("leader"); barriers
+// the leader waits on count arrivals from both CTAs, and the MMA completions (commits)
+// arrive on the same barrier offset in both CTAs.
 struct PfBars {
-    uint64_t raw_full[kPfRawStages], raw_empty[kPfRawStages];
-    uint64_t b_full[kPfBStages], b_empty[kPfBStages];
-    uint64_t a_full[kPfAStages], a_empty[kPfAStages];
-    uint64_t acc_full[2], acc_empty[2];
-    uint64_t drain;
+    uint64_t b_full[kPfBStages];                              // local: this CTA's B half landed
+    uint64_t b_peer[kPfBStages];                              // leader: the odd CTA's B half landed
+    uint64_t b_empty[kPfBStages];                             // both (commit)
+    uint64_t a_full[kPfAStages];                              // leader: 128 + 128 dequantiser arrivals
+    uint64_t a_empty[kPfAStages];                             // both (commit)
+    uint64_t acc_full[2];                                     // both (commit)
+    uint64_t acc_empty[2];                                    // leader: 256 + 256 epilogue arrivals
+    uint64_t ep_full[kPfEpStages], ep_empty[kPfEpStages];     // local
+    uint64_t drain;                                           // both (commit)
     uint32_t tmem;
     int abort;
 };
-static_assert(sizeof(PfBars) <= 256, "barrier block");
+static_assert(sizeof(PfBars) <= 512, "barrier block");
 
+__device__ __forceinline__ bool mbar_try_wait_cl(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(200000u)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait (cluster-scope acquire: the barriers also count arrivals from the other CTA
+// of the pair).  The thread is suspended between polls until the phase completes.
 __device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
                                         qwb_status_block *st) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_cl(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_cl(bar, parity)) return true;
         if (*abort) return false;
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
             *abort = 1;
@@ -184,20 +234,26 @@ __device__ __forceinline__ bool pf_wait_warp(uint64_t *bar, uint32_t parity, vol
     if ((threadIdx.x & 31) == 0) ok = pf_wait(bar, parity, abort, st);
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
+// arrive on the barrier at the same offset in CTA `rank` of the cluster
+__device__ __forceinline__ void arrive_on(uint64_t *bar, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(bar)), "r"(rank));
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
 
 struct PfItem {
-    int tile, mt, p0, cnt, Nt, rows;
-    int64_t slot;  // -1: invalid expert id / slot
+    int tile, mp, p0, cnt, Nt, rows;  // rows of this CTA's half of the 256-row weight tile (may be <= 0)
+    int64_t slot;                     // -1: invalid expert id / slot
 };
-__device__ __forceinline__ PfItem pf_item(const PrefillArgs &a, int it) {
+__device__ __forceinline__ PfItem pf_item(const PrefillArgs &a, int it, int rank) {
     PfItem x;
     x.tile = it / a.m_tiles;
-    x.mt = it - x.tile * a.m_tiles;
+    x.mp = it - x.tile * a.m_tiles;
     const int4 t = a.tiles[x.tile];
     x.p0 = t.y;
     x.cnt = t.z;
-    x.Nt = (t.z + 15) & ~15;
-    x.rows = (int) min((int64_t) kPfTileM, a.M - (int64_t) x.mt * kPfTileM);
+    x.Nt = pf_tile_cols(t.z);
+    x.rows = (int) max((int64_t) -1, min((int64_t) kPfTileM, a.M - (int64_t) (2 * x.mp + rank) * kPfTileM));
     x.slot = -1;
     if (t.x >= 0 && t.x < a.n_ids) {
         const int64_t sl = a.remap ? (int64_t) a.remap[t.x] : (int64_t) t.x;
@@ -214,10 +270,6 @@ __device__ __forceinline__ int pf_row_mode(float d, float dmin) {
     if (dmin != 0.f) return 1;
     return 2;
 }
-__device__ __forceinline__ float pf_row_scale(float d, float dmin) {
-    const int mode = pf_row_mode(d, dmin);
-    return mode == 0 ? d : (mode == 1 ? dmin : 0.f);
-}
 
 __device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d;
@@ -229,300 +281,434 @@ __device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
     asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
     return d;
 }
-__device__ __forceinline__ uint32_t h2_splat(float v) {
-    const uint32_t h = f2h_rn(v);
-    return h | (h << 16);
+__device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+// fp16x2 {v, v} of an integer 0 <= v < 1024 without a conversion instruction: the bits
+// 0x6400 | v encode 1024 + v, and subtracting 1024 is exact.
+__device__ __forceinline__ uint32_t h2_int(uint32_t v) {
+    return hsub2_u((v * 0x10001u) | 0x64006400u, 0x64006400u);
+}
+// f32 value of an integer 0 <= v < 2^23 without a conversion instruction
+__device__ __forceinline__ float f_int(uint32_t v) { return __fsub_rn(__uint_as_float(0x4B000000u | v), 8388608.f); }
+// fp16x2 {v, v} (one packed conversion)
+__device__ __forceinline__ uint32_t h2_pack(float v) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.f32 %0, %1, %1;" : "=r"(d) : "f"(v));
+    return d;
+}
+__device__ __forceinline__ uint32_t h2_pack2(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+constexpr uint32_t kH2Neg1024 = 0xE400E400u, kH2Sixteenth = 0x2C002C00u, kH2Neg64 = 0xD400D400u;
+
+// 16-byte async copy global -> shared (L2 only); src_bytes 0 zero-fills the destination
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_q4k_kernel(const PrefillArgs a) {
+// Warp roles (18 warps).  TMEM lane quarter = warp % 4 for every role that touches TMEM.
+constexpr int kPfWarpEpi = 8;    // warps 8..15: epilogue (column half (warp - 8) / 4)
+constexpr int kPfWarpProd = 16;  // producer
+constexpr int kPfWarpMma = 17;   // TMEM allocation; MMA issue (even CTA) / B-landed relay (odd CTA)
+// warps 0..3 / 4..7: dequantiser groups for superblock halves 0 / 1 (A stage 0 / 1)
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
+    pf_gemm_q4k_kernel(const PrefillArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *raw = smem;
     uint8_t *bst = smem + kPfOffB;
+    float *ep = (float *) (smem + kPfOffEp);  // [slot][0..127] activation scales, [slot][128..255] row scales
     PfBars *bars = (PfBars *) (smem + kPfOffBar);
     volatile int *abort = &bars->abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint32_t rank;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
 
-    const int total = *a.n_tiles * a.m_tiles;
-    if ((int) blockIdx.x >= total) return;
+    const int total = *a.n_tiles * a.m_tiles;  // work items: (token tile, 256-row weight tile)
+    if (pair >= total) return;                 // both CTAs of the pair leave together
     const int nsb = (int) (a.K / QK_K);
 
     if (tid == 0) {
-        for (int i = 0; i < kPfRawStages; ++i) {
-            mbar_init(&bars->raw_full[i], 1);
-            mbar_init(&bars->raw_empty[i], 128);
-        }
         for (int i = 0; i < kPfBStages; ++i) {
             mbar_init(&bars->b_full[i], 1);
+            mbar_init(&bars->b_peer[i], 1);
             mbar_init(&bars->b_empty[i], 1);
         }
         for (int i = 0; i < kPfAStages; ++i) {
-            mbar_init(&bars->a_full[i], 128);
+            mbar_init(&bars->a_full[i], 256);
             mbar_init(&bars->a_empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bars->acc_full[i], 1);
-            mbar_init(&bars->acc_empty[i], 256);
+            mbar_init(&bars->acc_empty[i], 512);
+        }
+        for (int i = 0; i < kPfEpStages; ++i) {
+            mbar_init(&bars->ep_full[i], 1 + 128);  // producer (scales copy) + dequantiser group 0
+            mbar_init(&bars->ep_empty[i], 256);
         }
         mbar_init(&bars->drain, 1);
         bars->abort = 0;
         fence_mbar_init();
     }
-    if (warp == 1) {
-        umma::tmem_alloc(&bars->tmem, kPfTmemCols);
-        umma::tmem_relinquish();
+    if (warp == kPfWarpMma) {
+        umma::tmem_alloc2(&bars->tmem, kPfTmemCols);
+        umma::tmem_relinquish2();
     }
     umma::fence_before_sync();
-    __syncthreads();
+    // both CTAs' barriers are initialised before either CTA arrives on the other's
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
     umma::fence_after_sync();
     const uint32_t tbase = bars->tmem;
 
-    if (warp == 0) {
+    if (warp == kPfWarpProd) {
         // ------------------------------------------------------------ producer
-        uint32_t ra_i = 0, b_i = 0;
+        // Per item, the whole warp first asks L2 to prefetch the NEXT item's weight rows as
+        // contiguous row-long runs (one bulk prefetch per row), so DRAM streams them while
+        // the dequantisers read the current rows 144 bytes at a time.  Then lane 0 issues,
+        // per superblock, the token tile's activation scales and this CTA's halves of the
+        // two B stages (bulk copies).
+        const uint32_t rb = (uint32_t) (a.K / QK_K) * Q4K_BYTES;
+        auto prefetch_rows = [&](int it) {
+            if (it >= total) return;
+            const PfItem y = pf_item(a, it, rank);
+            if (y.slot < 0) return;
+            const uint8_t *base = a.W + (size_t) y.slot * a.nb2 + (size_t) (2 * y.mp + rank) * kPfTileM * a.nb1;
+            for (int r = lane; r < y.rows; r += 32)
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + (size_t) r * a.nb1), "r"(rb)
+                             : "memory");
+        };
+        prefetch_rows(pair);
+        uint32_t b_i = 0, ep_i = 0;
         bool ok = true;
-        for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
-            const PfItem x = pf_item(a, it);
-            if (x.slot < 0 && lane == 0 && x.mt == 0) report(a.st, QWB_DEVERR_ID_RANGE, a.tiles[x.tile].x);
-            const uint8_t *wb = x.slot >= 0 ? a.W + (size_t) x.slot * a.nb2 + (size_t) x.mt * kPfTileM * a.nb1 : nullptr;
-            const uint8_t *bt = a.btiles + (size_t) x.tile * pf_btile_stride(a.K);
-            const uint32_t bbytes = (uint32_t) x.Nt * kPfHalfK * 2;
-            for (int s = 0; s < nsb && ok; ++s) {
-                const int ra = ra_i % kPfRawStages;
-                if (!(ok = pf_wait_warp(&bars->raw_empty[ra], ((ra_i / kPfRawStages) & 1) ^ 1, abort, a.st))) break;
-                if (lane == 0) mbar_arrive_expect_tx(&bars->raw_full[ra], wb ? (uint32_t) x.rows * Q4K_BYTES : 0u);
-                __syncwarp();
-                if (wb)
-                    for (int r = lane; r < x.rows; r += 32)
-                        bulk_g2s(raw + ra * kPfRawBytes + r * Q4K_BYTES, wb + (size_t) r * a.nb1 + (size_t) s * Q4K_BYTES,
-                                 Q4K_BYTES, &bars->raw_full[ra]);
-                ++ra_i;
-                for (int h = 0; h < 2; ++h) {
-                    const int bs = b_i % kPfBStages;
-                    if (!(ok = pf_wait_warp(&bars->b_empty[bs], ((b_i / kPfBStages) & 1) ^ 1, abort, a.st))) break;
-                    if (lane == 0) {
+        for (int it = pair; it < total && ok; it += n_pairs) {
+            prefetch_rows(it + n_pairs);
+            if (lane == 0) {
+                const PfItem x = pf_item(a, it, rank);
+                if (x.slot < 0 && x.mp == 0 && rank == 0) report(a.st, QWB_DEVERR_ID_RANGE, a.tiles[x.tile].x);
+                const float *dat = a.da + (size_t) x.tile * nsb * kPfTileN;
+                const uint32_t sbytes = (uint32_t) x.Nt * kPfHalfK * 2;  // one stage, both halves
+                const uint32_t bbytes = sbytes / 2;
+                const uint8_t *bt = a.btiles + (size_t) x.tile * pf_btile_stride(a.K) + rank * bbytes;
+                for (int s = 0; s < nsb && ok; ++s) {
+                    const int es = ep_i % kPfEpStages;
+                    if (!(ok = pf_wait(&bars->ep_empty[es], ((ep_i / kPfEpStages) & 1) ^ 1, abort, a.st))) break;
+                    PF_TRACE(0, ep_i);
+                    mbar_arrive_expect_tx(&bars->ep_full[es], (uint32_t) x.Nt * 4);
+                    bulk_g2s(ep + es * 2 * kPfTileN, dat + (size_t) s * kPfTileN, (uint32_t) x.Nt * 4, &bars->ep_full[es]);
+                    ++ep_i;
+                    for (int h = 0; h < 2; ++h) {
+                        const int bs = b_i % kPfBStages;
+                        if (!(ok = pf_wait(&bars->b_empty[bs], ((b_i / kPfBStages) & 1) ^ 1, abort, a.st))) break;
                         mbar_arrive_expect_tx(&bars->b_full[bs], bbytes);
-                        bulk_g2s(bst + bs * kPfBBytes, bt + (size_t) (2 * s + h) * bbytes, bbytes, &bars->b_full[bs]);
+                        bulk_g2s(bst + bs * kPfBBytes, bt + (size_t) (2 * s + h) * sbytes, bbytes, &bars->b_full[bs]);
+                        ++b_i;
                     }
-                    ++b_i;
+                    PF_TRACE(1, ep_i - 1);
                 }
             }
+            ok = __shfl_sync(0xffffffffu, (int) ok, 0) != 0;
         }
-        // wait for this warp's copies still in flight (only after an abort can there be any)
         if (lane == 0) {
-            for (int k = 0; k < kPfRawStages; ++k)
-                if (ra_i > (uint32_t) k) {
-                    const uint32_t last = ra_i - 1 - ((ra_i - 1 - k) % kPfRawStages);
-                    mbar_wait(&bars->raw_full[k], (last / kPfRawStages) & 1);
-                }
+            // wait for copies still in flight (only after an abort can there be any)
             for (int k = 0; k < kPfBStages; ++k)
                 if (b_i > (uint32_t) k) {
                     const uint32_t last = b_i - 1 - ((b_i - 1 - k) % kPfBStages);
                     mbar_wait(&bars->b_full[k], (last / kPfBStages) & 1);
                 }
+            for (int k = 0; k < kPfEpStages; ++k)
+                if (ep_i > (uint32_t) k) {
+                    const uint32_t last = ep_i - 1 - ((ep_i - 1 - k) % kPfEpStages);
+                    mbar_wait(&bars->ep_full[k], (last / kPfEpStages) & 1);
+                }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        __syncwarp();
+    } else if (warp == kPfWarpMma) {
+        if (lane == 0 && rank == 0) {
+            // -------------------------------------------------------- MMA issuer (even CTA)
             uint32_t b_i = 0, a_i = 0, acc_i = 0;
             bool ok = true;
-            for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
-                const PfItem x = pf_item(a, it);
-                const uint32_t idesc = umma::idesc_f16(kPfTileM, x.Nt);
-                const uint32_t lbo = (uint32_t) x.Nt * 16;
+            for (int it = pair; it < total && ok; it += n_pairs) {
+                const PfItem x = pf_item(a, it, rank);
+                const uint32_t idesc = umma::idesc_f16(2 * kPfTileM, x.Nt);
+                const uint32_t lbo = (uint32_t) (x.Nt / 2) * 16;
                 for (int s = 0; s < nsb && ok; ++s) {
                     const int ab = acc_i & 1;
                     if (!(ok = pf_wait(&bars->acc_empty[ab], ((acc_i >> 1) & 1) ^ 1, abort, a.st))) break;
+                    PF_TRACE(4, acc_i);
                     umma::fence_after_sync();
                     const uint32_t d_t = tbase + (uint32_t) ab * kPfAccCols;
                     for (int h = 0; h < 2; ++h) {
                         const int bs = b_i % kPfBStages, as = a_i % kPfAStages;
-                        if (!(ok = pf_wait(&bars->b_full[bs], (b_i / kPfBStages) & 1, abort, a.st))) break;
+                        const uint32_t bpar = (b_i / kPfBStages) & 1;
+                        if (!(ok = pf_wait(&bars->b_full[bs], bpar, abort, a.st))) break;
+                        if (!(ok = pf_wait(&bars->b_peer[bs], bpar, abort, a.st))) break;
                         if (!(ok = pf_wait(&bars->a_full[as], (a_i / kPfAStages) & 1, abort, a.st))) break;
                         umma::fence_after_sync();
                         const uint32_t b_s = smem_u32(bst + bs * kPfBBytes);
                         const uint32_t a_t = tbase + 2 * kPfAccCols + (uint32_t) as * kPfACols;
 #pragma unroll
                         for (int ks = 0; ks < 8; ++ks)
-                            umma::mma_f16_ts(d_t, a_t + ks * 8, umma::sdesc(b_s + ks * 2 * lbo, lbo, 128), idesc,
-                                             (h | ks) != 0);
-                        umma::mma_f16_ts(d_t, a_t + 64, umma::sdesc(b_s + 16 * lbo, lbo, 128), idesc, 1u);
-                        umma::commit(&bars->b_empty[bs]);
-                        umma::commit(&bars->a_empty[as]);
+                            umma::mma2_f16_ts(d_t, a_t + ks * 8, umma::sdesc(b_s + ks * 2 * lbo, lbo, 128), idesc,
+                                              (h | ks) != 0);
+                        umma::mma2_f16_ts(d_t, a_t + 64, umma::sdesc(b_s + 16 * lbo, lbo, 128), idesc, 1u);
+                        umma::commit2_mc(&bars->b_empty[bs], 3);
+                        umma::commit2_mc(&bars->a_empty[as], 3);
                         ++b_i;
                         ++a_i;
                     }
                     if (!ok) break;
-                    umma::commit(&bars->acc_full[ab]);
+                    umma::commit2_mc(&bars->acc_full[ab], 3);
+                    PF_TRACE(5, acc_i);
                     ++acc_i;
                 }
             }
-            // all MMAs issued by this thread have completed before TMEM is released
-            umma::commit(&bars->drain);
+            // all MMAs (which write both CTAs' TMEM) complete before either CTA frees it
+            umma::commit2_mc(&bars->drain, 3);
+            mbar_wait(&bars->drain, 0);
+        } else if (lane == 0) {
+            // -------------------------------------------------------- relay (odd CTA)
+            // tells the MMA issuer when this CTA's half of each B stage has landed
+            uint32_t b_i = 0;
+            bool ok = true;
+            for (int it = pair; it < total && ok; it += n_pairs) {
+                for (int s = 0; s < nsb && ok; ++s)
+                    for (int h = 0; h < 2; ++h, ++b_i) {
+                        const int bs = b_i % kPfBStages;
+                        if (!(ok = pf_wait(&bars->b_full[bs], (b_i / kPfBStages) & 1, abort, a.st))) break;
+                        arrive_on(&bars->b_peer[bs], 0);
+                    }
+            }
+            // the issuer's final commit also arrives here: no MMA is in flight after it
             mbar_wait(&bars->drain, 0);
         }
         __syncwarp();
-    } else if (warp >= 4 && warp < 8) {
-        // ------------------------------------------------------------ dequantiser
-        const int qd = warp - 4, m = qd * 32 + lane;
+    } else if (warp < kPfWarpEpi) {
+        // ------------------------------------------------------------ dequantisers
+        // group grp turns half grp of every superblock (Q4_K chunks 2grp, 2grp+1: 64 bytes
+        // of nibbles) into 64 TMEM columns of packed fp16(sc*q) pairs plus 8 min columns
+        // (group 0: fp16 high parts of -(dmin/d)*m, group 1: the low parts).
+        const int grp = warp >> 2, qd = warp & 3, m = qd * 32 + lane;
         const uint32_t lane_base = (uint32_t) (qd * 32) << 16;
-        uint32_t ra_i = 0, a_i = 0;
-        bool ok = true;
-        for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
-            const PfItem x = pf_item(a, it);
-            const bool live = x.slot >= 0 && m < x.rows;
-            for (int s = 0; s < nsb && ok; ++s) {
-                const int ra = ra_i % kPfRawStages;
-                if (!(ok = pf_wait_warp(&bars->raw_full[ra], (ra_i / kPfRawStages) & 1, abort, a.st))) break;
-                uint32_t w[36];
-                if (live) {
-                    const uint4 *src = (const uint4 *) (raw + ra * kPfRawBytes + m * Q4K_BYTES);
+        uint8_t *mine = raw + (size_t) (grp * 128 + m) * kPfSlot;
+        // this CTA's superblocks in order: f -> (item f / nsb, superblock f % nsb); the row
+        // pointer of the item being fetched is cached (null: invalid slot or row past M)
+        const int n_sb = (total - pair + n_pairs - 1) / n_pairs * nsb;
+        int f_item = -1;
+        const uint8_t *f_row = nullptr;
+        auto fetch = [&](int f) {
+            if (f < n_sb) {
+                const int k = f / nsb, s = f - k * nsb;
+                if (k != f_item) {
+                    const PfItem y = pf_item(a, pair + k * n_pairs, rank);
+                    f_row = (y.slot >= 0 && m < y.rows)
+                                ? a.W + (size_t) y.slot * a.nb2 + ((size_t) (2 * y.mp + rank) * kPfTileM + m) * a.nb1
+                                : nullptr;
+                    f_item = k;
+                }
+                const bool v = f_row != nullptr;
+                const uint8_t *src = v ? f_row + (size_t) s * Q4K_BYTES : a.W;
+                uint8_t *dst = mine + (f % kPfPre) * kPfRawStage;
+                const uint32_t n = v ? 16u : 0u;  // 0: zero-fill
+                cp_async16(dst, src, n);
 #pragma unroll
-                    for (int i = 0; i < 9; ++i) {
-                        const uint4 v = src[i];
+                for (int i = 0; i < 4; ++i) cp_async16(dst + 16 + 16 * i, src + 16 + 64 * grp + 16 * i, n);
+            }
+            cp_async_commit();
+        };
+#pragma unroll 1
+        for (int f = 0; f < kPfPre; ++f) fetch(f);
+        uint32_t sb_i = 0;
+        bool ok = true;
+        for (int it = pair; it < total && ok; it += n_pairs) {
+            for (int s = 0; s < nsb && ok; ++s, ++sb_i) {
+                cp_async_wait<kPfPre - 1>();  // superblock sb_i has landed
+                if (tid == 0) PF_TRACE(2, sb_i);
+                // header + scales (16 bytes) and this half's 64 bytes of nibbles
+                uint32_t hw[4], w[16];
+                {
+                    const uint4 *src = (const uint4 *) (mine + (sb_i % kPfPre) * kPfRawStage);
+                    const uint4 h4 = src[0];
+                    hw[0] = h4.x; hw[1] = h4.y; hw[2] = h4.z; hw[3] = h4.w;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint4 v = src[1 + i];
                         w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
                     }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 36; ++i) w[i] = 0;
                 }
-                umma::mbar_arrive(&bars->raw_empty[ra]);
-                ++ra_i;
-                const float d = h2f((uint16_t) (w[0] & 0xFFFF)), dmin = h2f((uint16_t) (w[0] >> 16));
+                fetch((int) sb_i + kPfPre);  // into the slot just read
+                if (tid == 0) PF_TRACE(8, sb_i);
+                const float d = h2f((uint16_t) (hw[0] & 0xFFFF)), dmin = h2f((uint16_t) (hw[0] >> 16));
                 const int mode = pf_row_mode(d, dmin);
-                uint8_t sb[12];
-#pragma unroll
-                for (int i = 0; i < 12; ++i) sb[i] = (uint8_t) (w[1 + i / 4] >> (8 * (i % 4)));
-                int sc[8], mn[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    if (j < 4) {
-                        sc[j] = sb[j] & 63;
-                        mn[j] = sb[j + 4] & 63;
-                    } else {
-                        sc[j] = (sb[j + 4] & 0xF) | ((sb[j - 4] >> 6) << 4);
-                        mn[j] = (sb[j + 4] >> 4) | ((sb[j] >> 6) << 4);
-                    }
+                if (grp == 0) {
+                    const int es = sb_i % kPfEpStages;
+                    if (!(ok = pf_wait_warp(&bars->ep_empty[es], ((sb_i / kPfEpStages) & 1) ^ 1, abort, a.st))) break;
+                    ep[es * 2 * kPfTileN + kPfTileN + m] = mode == 0 ? d : (mode == 1 ? dmin : 0.f);
+                    umma::mbar_arrive(&bars->ep_full[es]);
                 }
+                // 6-bit scale / min of sub-block j (get_scale_min_k4, ggml-quants.c:880-887)
+                auto sbyte = [&](int i) -> uint32_t { return (hw[1 + i / 4] >> (8 * (i % 4))) & 0xFFu; };
+                auto scale_of = [&](int j) -> uint32_t {
+                    return j < 4 ? (sbyte(j) & 63u) : ((sbyte(j + 4) & 0xFu) | ((sbyte(j - 4) >> 6) << 4));
+                };
+                auto min_of = [&](int j) -> uint32_t {
+                    return j < 4 ? (sbyte(j + 4) & 63u) : ((sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4));
+                };
                 const float r = mode == 0 ? dmin / d : (mode == 1 ? d / dmin : 0.f);
-                const uint32_t k2 = mode == 1 ? h2_splat(r) : 0u;
-                for (int h = 0; h < 2 && ok; ++h) {
-                    const int as = a_i % kPfAStages;
-                    if (!(ok = pf_wait_warp(&bars->a_empty[as], ((a_i / kPfAStages) & 1) ^ 1, abort, a.st))) break;
-                    umma::fence_after_sync();
-                    const uint32_t a_t = tbase + lane_base + 2 * kPfAccCols + (uint32_t) as * kPfACols;
+                const uint32_t k2 = mode == 1 ? h2_pack(r) : 0u;
+                if (tid == 0) PF_TRACE(12, sb_i);
+                const uint32_t a_i = 2 * sb_i + (uint32_t) grp;  // A stages are used in turn by the halves
+                const int as = a_i % kPfAStages;
+                if (!(ok = pf_wait_warp(&bars->a_empty[as], ((a_i / kPfAStages) & 1) ^ 1, abort, a.st))) break;
+                if (tid == 0) PF_TRACE(10, sb_i);
+                umma::fence_after_sync();
+                const uint32_t a_t = tbase + lane_base + 2 * kPfAccCols + (uint32_t) as * kPfACols;
 #pragma unroll
-                    for (int jj = 0; jj < 2; ++jj) {
-                        const int j = 2 * h + jj;
-                        const uint32_t slo = h2_splat((float) sc[2 * j]), blo = h2_splat(-1024.f * (float) sc[2 * j]);
-                        const uint32_t shi = h2_splat((float) sc[2 * j + 1]),
-                                       bhi = h2_splat(-1024.f * (float) sc[2 * j + 1]);
+                for (int jj = 0; jj < 2; ++jj) {
+                    // chunk j = 2grp + jj: low nibbles -> sub-block 2j, high nibbles -> 2j+1.
+                    // Low nibble q: fp16 bits 0x6400|q = 1024+q, times sc minus 1024*sc.
+                    // High nibble in place: 0x6400|(q<<4) = 1024+16q, times sc/16 minus 64*sc.
+                    // Both fused multiply-adds are exact (results are integers <= 945).
+                    const int j = 2 * grp + jj;
+                    const uint32_t slo = h2_int(scale_of(2 * j)), blo = hmul2_u(slo, kH2Neg1024);
+                    const uint32_t sh1 = h2_int(scale_of(2 * j + 1));
+                    const uint32_t shi = hmul2_u(sh1, kH2Sixteenth), bhi = hmul2_u(sh1, kH2Neg64);
 #pragma unroll
-                        for (int g = 0; g < 2; ++g) {
-                            uint32_t o[16];
+                    for (int g = 0; g < 2; ++g) {
+                        uint32_t o[16];
 #pragma unroll
-                            for (int ww = 0; ww < 4; ++ww) {
-                                const uint32_t xw = w[4 + 8 * j + 4 * g + ww];
-                                o[4 * ww + 0] = hfma2_u((xw & 0x000F000Fu) | 0x64006400u, slo, blo);
-                                o[4 * ww + 1] = hfma2_u(((xw >> 8) & 0x000F000Fu) | 0x64006400u, slo, blo);
-                                o[4 * ww + 2] = hfma2_u(((xw >> 4) & 0x000F000Fu) | 0x64006400u, shi, bhi);
-                                o[4 * ww + 3] = hfma2_u(((xw >> 12) & 0x000F000Fu) | 0x64006400u, shi, bhi);
-                            }
-                            if (mode != 0) {
-#pragma unroll
-                                for (int i = 0; i < 16; ++i) o[i] = hmul2_u(o[i], k2);
-                            }
-                            umma::st16(a_t + (uint32_t) (jj * 32 + g * 16), o);
+                        for (int ww = 0; ww < 4; ++ww) {
+                            const uint32_t xw = w[8 * jj + 4 * g + ww], yw = xw >> 8;
+                            o[4 * ww + 0] = hfma2_u((xw & 0x000F000Fu) | 0x64006400u, slo, blo);
+                            o[4 * ww + 1] = hfma2_u((yw & 0x000F000Fu) | 0x64006400u, slo, blo);
+                            o[4 * ww + 2] = hfma2_u((xw & 0x00F000F0u) | 0x64006400u, shi, bhi);
+                            o[4 * ww + 3] = hfma2_u((yw & 0x00F000F0u) | 0x64006400u, shi, bhi);
                         }
-                    }
-                    uint32_t o8[8];
+                        if (mode != 0) {
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        float hi = 0.f, lo = 0.f;
-                        if (mode == 0) {
-                            const float v = -r * (float) mn[c];
-                            hi = __half2float(__float2half_rn(v));
-                            lo = v - hi;
-                        } else if (mode == 1) {
-                            hi = -(float) mn[c];
+                            for (int i = 0; i < 16; ++i) o[i] = hmul2_u(o[i], k2);
                         }
-                        o8[c] = h2_splat(h == 0 ? hi : lo);
+                        umma::st16(a_t + (uint32_t) (jj * 32 + g * 16), o);
                     }
-                    umma::st8(a_t + 64, o8);
-                    umma::wait_st();
-                    umma::fence_before_sync();
-                    umma::mbar_arrive(&bars->a_full[as]);
-                    ++a_i;
                 }
+                if (tid == 0) PF_TRACE(11, sb_i);
+                // min coefficients -(dmin/d)*m as hi + lo: Veltkamp split (factor 2^13 + 1)
+                // leaves 11 significant bits in hi, so hi is an fp16 value and lo = full - hi
+                // is exact; fp16(lo) then carries the next 11 bits.
+                uint32_t o8[8];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const float mc = f_int(min_of(c));
+                    float v = 0.f;
+                    if (mode == 0) {
+                        const float full = __fmul_rn(-r, mc);
+                        const float t = __fmul_rn(full, 8193.f);
+                        const float hi = __fsub_rn(t, __fsub_rn(t, full));
+                        v = grp == 0 ? hi : __fsub_rn(full, hi);
+                    } else if (mode == 1) {
+                        v = grp == 0 ? -mc : 0.f;
+                    }
+                    o8[c] = h2_pack(v);
+                }
+                umma::st8(a_t + 64, o8);
+                if (tid == 0) PF_TRACE(13, sb_i);
+                umma::wait_st();
+                if (tid == 0) PF_TRACE(14, sb_i);
+                umma::fence_before_sync();
+                if (rank == 0) umma::mbar_arrive(&bars->a_full[as]);
+                else arrive_on(&bars->a_full[as], 0);
+                if (tid == 0) PF_TRACE(9, sb_i);
+                if (tid == 128) PF_TRACE(3, sb_i);
             }
         }
-    } else if (warp >= 8) {
+    } else if (warp < kPfWarpProd) {
         // ------------------------------------------------------------ epilogue
-        const int qd = warp & 3, g = (warp - 8) >> 2, m = qd * 32 + lane;
+        // one thread per (weight row, half of the token columns): 64 running sums in registers
+        const int qd = warp & 3, g = (warp - kPfWarpEpi) >> 2, m = qd * 32 + lane;
         const uint32_t lane_base = (uint32_t) (qd * 32) << 16;
         uint32_t acc_i = 0;
         bool ok = true;
-        for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
-            const PfItem x = pf_item(a, it);
-            const bool live = x.slot >= 0 && m < x.rows;
-            const uint8_t *hdr =
-                live ? a.W + (size_t) x.slot * a.nb2 + ((size_t) x.mt * kPfTileM + m) * a.nb1 : nullptr;
-            const float *dap = a.da + (size_t) x.tile * nsb * kPfTileN + 64 * g;
+        for (int it = pair; it < total && ok; it += n_pairs) {
+            const PfItem x = pf_item(a, it, rank);
+            // output row offsets (in floats, < 2^32 checked on the host) of columns
+            // 64g + lane and 64g + 32 + lane
+            uint32_t off[2] = {0, 0};
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int n = 64 * g + 32 * u + lane;
+                if (n < x.cnt) {
+                    const int p = __ldg(a.pairs + x.p0 + n);
+                    const int t = p / a.n_used, j = p - t * a.n_used;
+                    off[u] = (uint32_t) (((size_t) j * a.dnb1 + (size_t) t * a.dnb2) >> 2);
+                }
+            }
             float out[64];
 #pragma unroll
             for (int i = 0; i < 64; ++i) out[i] = 0.f;
-            for (int s = 0; s < nsb && ok; ++s) {
-                float S = 0.f;
-                if (hdr) {
-                    const uint32_t hw = __ldg((const unsigned int *) (hdr + (size_t) s * Q4K_BYTES));
-                    S = pf_row_scale(h2f((uint16_t) (hw & 0xFFFF)), h2f((uint16_t) (hw >> 16)));
-                }
+            for (int s = 0; s < nsb && ok; ++s, ++acc_i) {
+                const int es = acc_i % kPfEpStages;
+                if (!(ok = pf_wait_warp(&bars->ep_full[es], (acc_i / kPfEpStages) & 1, abort, a.st))) break;
+                const float *eps = ep + es * 2 * kPfTileN;
+                const float S = eps[kPfTileN + m];
                 const int ab = acc_i & 1;
                 if (!(ok = pf_wait_warp(&bars->acc_full[ab], (acc_i >> 1) & 1, abort, a.st))) break;
+                if (tid == kPfWarpEpi * 32) PF_TRACE(6, acc_i);
                 umma::fence_after_sync();
                 const uint32_t d_t = tbase + lane_base + (uint32_t) ab * kPfAccCols + 64 * g;
-                const float *ds = dap + (size_t) s * kPfTileN;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    if (64 * g + 16 * c < x.Nt) {  // warp-uniform
-                        uint32_t v[16];
-                        umma::ld16(d_t + 16 * c, v);
+                for (int c = 0; c < 8; ++c) {
+                    const int c0 = 64 * g + 8 * c;
+                    if (c0 < x.Nt) {  // warp-uniform
+                        uint32_t v[8];
+                        umma::ld8(d_t + 8 * c, v);
                         umma::wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 16; i += 4) {
-                            const float4 dv = __ldg((const float4 *) (ds + 16 * c + i));
-                            out[16 * c + i + 0] = fmaf(S * dv.x, __uint_as_float(v[i + 0]), out[16 * c + i + 0]);
-                            out[16 * c + i + 1] = fmaf(S * dv.y, __uint_as_float(v[i + 1]), out[16 * c + i + 1]);
-                            out[16 * c + i + 2] = fmaf(S * dv.z, __uint_as_float(v[i + 2]), out[16 * c + i + 2]);
-                            out[16 * c + i + 3] = fmaf(S * dv.w, __uint_as_float(v[i + 3]), out[16 * c + i + 3]);
-                        }
+                        const float4 da0 = *(const float4 *) (eps + c0), da1 = *(const float4 *) (eps + c0 + 4);
+                        float *o = out + 8 * c;
+                        o[0] = fmaf(S * da0.x, __uint_as_float(v[0]), o[0]);
+                        o[1] = fmaf(S * da0.y, __uint_as_float(v[1]), o[1]);
+                        o[2] = fmaf(S * da0.z, __uint_as_float(v[2]), o[2]);
+                        o[3] = fmaf(S * da0.w, __uint_as_float(v[3]), o[3]);
+                        o[4] = fmaf(S * da1.x, __uint_as_float(v[4]), o[4]);
+                        o[5] = fmaf(S * da1.y, __uint_as_float(v[5]), o[5]);
+                        o[6] = fmaf(S * da1.z, __uint_as_float(v[6]), o[6]);
+                        o[7] = fmaf(S * da1.w, __uint_as_float(v[7]), o[7]);
                     }
                 }
                 umma::fence_before_sync();
-                umma::mbar_arrive(&bars->acc_empty[ab]);
-                ++acc_i;
+                if (rank == 0) umma::mbar_arrive(&bars->acc_empty[ab]);
+                else arrive_on(&bars->acc_empty[ab], 0);
+                umma::mbar_arrive(&bars->ep_empty[es]);
+                if (tid == kPfWarpEpi * 32) PF_TRACE(7, acc_i);
             }
             if (!ok) break;
-            if (m < x.rows) {
-                const int64_t row = (int64_t) x.mt * kPfTileM + m;
+            // rows of an invalid expert slot come out as zeros (row scale 0)
+            const int64_t row = (int64_t) (2 * x.mp + rank) * kPfTileM + m;
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const int n = 64 * g + i;
-                    if (n < x.cnt) {
-                        const int p = __ldg(a.pairs + x.p0 + n);
-                        const int t = p / a.n_used, j = p - t * a.n_used;
-                        float *o = (float *) ((char *) a.dst + (size_t) j * a.dnb1 + (size_t) t * a.dnb2);
-                        o[row] = out[i];
-                    }
-                }
+            for (int i = 0; i < 64; ++i) {
+                const uint32_t o = __shfl_sync(0xffffffffu, off[i >> 5], i & 31);
+                if (m < x.rows && 64 * g + i < x.cnt) a.dst[(size_t) o + row] = out[i];
             }
         }
     }
 
+    // no MMA is in flight (both CTAs waited for the issuer's final commit) and no TMEM
+    // load or store is pending: free the pair's TMEM
     umma::fence_before_sync();
-    __syncthreads();
-    if (warp == 1) {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (warp == kPfWarpMma) {
         umma::fence_after_sync();
-        umma::tmem_dealloc(tbase, kPfTmemCols);
+        umma::tmem_dealloc2(tbase, kPfTmemCols);
     }
 }
 
@@ -533,9 +719,18 @@ cudaError_t launch_pf_gemm_q4k(const PrefillArgs &a, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    pf_gemm_q4k_kernel<<<num_sms(), kPfThreads, kPfSmem, s>>>(a);
+    // an even number of CTAs (pairs), one per SM
+    pf_gemm_q4k_kernel<<<num_sms() & ~1, kPfThreads, kPfSmem, s>>>(a);
     return cudaGetLastError();
 }
+
+#ifdef QWB_PF_TRACE
+}  // namespace qwb
+extern "C" QWB_API int qwb_debug_pf_trace(void *host, size_t bytes) {
+    return cudaMemcpyFromSymbol(host, qwb::g_pf_trace, bytes) == cudaSuccess ? 0 : 1;
+}
+namespace qwb {
+#endif
 
 bool pf_eligible(int type, int64_t K, int64_t M, int64_t P, int64_t n_as) {
     if (type != QWB_TYPE_Q4_K || K % QK_K || K < QK_K || M < 1) return false;
