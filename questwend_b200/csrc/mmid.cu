@@ -460,7 +460,7 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
         a.dnb1 = dst->nb[1];
         a.dnb2 = dst->nb[2];
         a.n_used = (int) p.n_used;
-        a.m_tiles = (int) ceil_div(p.M, 2 * kPfTileM);  // 256-row weight tiles (one per CTA pair)
+        a.m_tiles = (int) ceil_div(p.M, kPfTileM);
         a.st = st;
         e = launch_pf_gemm_q4k(a, s);
         profile_mark(s, QWB_KERNEL_GROUPED_GEMM);

@@ -16,18 +16,15 @@
 // Superblocks whose dmin/d ratio is too large for an fp16 min coefficient (d ~ 0) use
 // dmin as the row scale instead (see pf_row_mode).
 //
-// Work item = (token tile of one expert, 256 weight rows), computed by a 2-CTA cluster with
-// the CTA-pair MMA (cta_group::2, M = 256): each CTA dequantises its 128 weight rows into
-// its own TMEM and loads its half of the token tile's fp16 B operand, so every B byte
-// fetched from L2 serves 256 weight rows.  One persistent CTA per SM, warp-specialised:
+// Work item = (token tile of one expert, 128 weight rows).  One persistent CTA per SM,
+// warp-specialised (18 warps):
 //   warps 0-7   dequantisation of the raw rows into TMEM (A operand), one row per thread,
-//               one warpgroup per half superblock
+//               one warpgroup per half superblock; each thread fetches its own row bytes
+//               with 16-byte async copies (cp.async) several superblocks ahead
 //   warps 8-15  epilogue: TMEM accumulator -> per-superblock scale -> running sums -> store
-//   warp 16     producer of the B halves and activation scales (bulk copies)
-//   warp 17     TMEM allocation; MMA issue (even CTA) / "B half landed" relay (odd CTA)
-// The dequantisers fetch their own raw rows with per-thread async copies (cp.async), kPfPre
-// superblocks ahead: a TMA box of 128 strided 144-byte rows is served row by row and
-// could not keep up.
+//   warp 16     producer: L2 prefetch of the next item's weight rows; bulk copies of the
+//               B stages and the activation scales
+//   warp 17     TMEM allocation and the MMA-issuing thread
 // Every wait is bounded; a timeout sets QWB_DEVERR_TIMEOUT and all roles drain and exit.
 #include "prefill.cuh"
 
@@ -61,7 +58,7 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(Q8Planes act, int64_t K,
     const int s = blockIdx.y;
     const int nsb = (int) (K / QK_K);
     const int4 tl = tiles[tile];
-    const int cnt = tl.z, Nt = pf_tile_cols(cnt), Nh = Nt / 2;
+    const int cnt = tl.z, Nt = pf_tile_cols(cnt);
     __shared__ __align__(16) uint8_t q[kPfTileN * kGatherRow];
     __shared__ __align__(16) int16_t bs[kPfTileN][16];
     const int tid = threadIdx.x;
@@ -103,9 +100,8 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(Q8Planes act, int64_t K,
     }
     __syncthreads();
 
-    // write both half-superblock stages; each stage holds two sub-tiles (tokens [0, Nt/2)
-    // for the even CTA of a pair, [Nt/2, Nt) for the odd one), each in the core-matrix
-    // layout: element (n, p) of sub-tile r at r*Nh*288 + (p / 8) * Nh * 16 + (n - r*Nh) * 16 + (p % 8) * 2
+    // write both half-superblock stages in the core-matrix layout:
+    // element (n, p) at (p / 8) * Nt * 16 + n * 16 + (p % 8) * 2
     uint8_t *tb = btiles + (size_t) tile * pf_btile_stride(K) + (size_t) (2 * s) * Nt * kPfHalfK * 2;
     const int chunks = 2 * 18 * Nt;
     for (int c = tid; c < chunks; c += 256) {
@@ -134,9 +130,8 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(Q8Planes act, int64_t K,
                 o[i] = lo | (hi << 16);
             }
         }
-        const int r = n >= Nh, nr = n - r * Nh;
-        *(uint4 *) (tb + (size_t) h * Nt * kPfHalfK * 2 + (size_t) r * Nh * kPfHalfK * 2 + (size_t) pc * Nh * 16 +
-                    (size_t) nr * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+        *(uint4 *) (tb + (size_t) h * Nt * kPfHalfK * 2 + (size_t) pc * Nt * 16 + (size_t) n * 16) =
+            make_uint4(o[0], o[1], o[2], o[3]);
     }
 }
 
@@ -152,10 +147,10 @@ cudaError_t launch_pf_gather(Q8Planes act, int64_t K, const int4 *tiles, const i
 // Optional pipeline timestamps (compiled in only with -DQWB_PF_TRACE; no effect on the
 // default build): CTA 0 records the global timer per role and per superblock.
 #ifdef QWB_PF_TRACE
-__device__ unsigned long long g_pf_trace[16][256];
-#define PF_TRACE(role, idx)                                                               \
-    do {                                                                                 \
-        if (blockIdx.x == 0 && (idx) < 256u) g_pf_trace[role][idx] = globaltimer_ns();   \
+__device__ unsigned long long g_pf_trace[32][256];
+#define PF_TRACE(role, idx)                                                                          \
+    do {                                                                                            \
+        if (blockIdx.x < 2 && (idx) < 256u) g_pf_trace[(role) + 16 * blockIdx.x][idx] = globaltimer_ns(); \
     } while (0)
 #else
 #define PF_TRACE(role, idx) \
@@ -164,16 +159,16 @@ __device__ unsigned long long g_pf_trace[16][256];
 #endif
 
 constexpr int kPfThreads = 576;  // 18 warps
-constexpr int kPfBStages = 6, kPfAStages = 3, kPfEpStages = 4;
+constexpr int kPfBStages = 4, kPfAStages = 3, kPfEpStages = 4;
 // raw weight bytes: each dequantiser thread copies (cp.async) its row's 16-byte header and
 // the 64 bytes of its half superblock, kPfPre superblocks ahead, into a private slot
-constexpr int kPfPre = 4;
+constexpr int kPfPre = 3;
 constexpr int kPfSlot = 80;
 constexpr int kPfRawStage = 256 * kPfSlot;                 // 20480 per superblock
-constexpr int kPfBBytes = (kPfTileN / 2) * kPfHalfK * 2;   // 18432: this CTA's half of the token tile
+constexpr int kPfBBytes = kPfTileN * kPfHalfK * 2;         // 36864: one half-superblock B stage
 constexpr uint32_t kPfACols = 72;                          // 64 value columns + 8 min columns
 constexpr uint32_t kPfAccCols = 128;
-constexpr uint32_t kPfTmemCols = 512;  // [0,256) accumulators, [256,472) A stages
+constexpr uint32_t kPfTmemCols = 512;                      // [0,256) accumulators, [256,472) A stages
 constexpr int kPfOffB = kPfPre * kPfRawStage;
 // epilogue ring, one slot per superblock: activation scales of the token tile (bulk copy)
 // and the weight rows' superblock scales (written by the dequantiser)
@@ -182,43 +177,24 @@ constexpr int kPfEpBytes = 2 * kPfTileN * 4;
 constexpr int kPfOffBar = kPfOffEp + kPfEpStages * kPfEpBytes;
 constexpr int kPfSmem = kPfOffBar + 512;
 
-// Barriers.  The CTA pair runs one MMA stream issued by the even CTA ("leader"); barriers
-// the leader waits on count arrivals from both CTAs, and the MMA completions (commits)
-// arrive on the same barrier offset in both CTAs.
 struct PfBars {
-    uint64_t b_full[kPfBStages];                              // local: this CTA's B half landed
-    uint64_t b_peer[kPfBStages];                              // leader: the odd CTA's B half landed
-    uint64_t b_empty[kPfBStages];                             // both (commit)
-    uint64_t a_full[kPfAStages];                              // leader: 128 + 128 dequantiser arrivals
-    uint64_t a_empty[kPfAStages];                             // both (commit)
-    uint64_t acc_full[2];                                     // both (commit)
-    uint64_t acc_empty[2];                                    // leader: 256 + 256 epilogue arrivals
-    uint64_t ep_full[kPfEpStages], ep_empty[kPfEpStages];     // local
-    uint64_t drain;                                           // both (commit)
+    uint64_t b_full[kPfBStages], b_empty[kPfBStages];
+    uint64_t a_full[kPfAStages], a_empty[kPfAStages];
+    uint64_t acc_full[2], acc_empty[2];
+    uint64_t ep_full[kPfEpStages], ep_empty[kPfEpStages];
+    uint64_t drain;
     uint32_t tmem;
     int abort;
 };
 static_assert(sizeof(PfBars) <= 512, "barrier block");
 
-__device__ __forceinline__ bool mbar_try_wait_cl(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(200000u)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait (cluster-scope acquire: the barriers also count arrivals from the other CTA
-// of the pair).  The thread is suspended between polls until the phase completes.
+// Bounded wait.  The thread is suspended between polls until the phase completes.
 __device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
                                         qwb_status_block *st) {
-    if (mbar_try_wait_cl(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity, 200000u)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
-        if (mbar_try_wait_cl(bar, parity)) return true;
+        if (mbar_try_wait(bar, parity, 200000u)) return true;
         if (*abort) return false;
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
             *abort = 1;
@@ -234,26 +210,27 @@ __device__ __forceinline__ bool pf_wait_warp(uint64_t *bar, uint32_t parity, vol
     if ((threadIdx.x & 31) == 0) ok = pf_wait(bar, parity, abort, st);
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
-// arrive on the barrier at the same offset in CTA `rank` of the cluster
-__device__ __forceinline__ void arrive_on(uint64_t *bar, uint32_t rank) {
-    uint32_t remote;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(bar)), "r"(rank));
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+// One arrival of count 32 on behalf of the whole warp, after every lane's own memory and
+// tcgen05 operations are ordered by the caller's fences.
+__device__ __forceinline__ void warp_arrive(uint64_t *bar) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0)
+        asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0], 32;" ::"r"(smem_u32(bar)) : "memory");
 }
 
 struct PfItem {
-    int tile, mp, p0, cnt, Nt, rows;  // rows of this CTA's half of the 256-row weight tile (may be <= 0)
-    int64_t slot;                     // -1: invalid expert id / slot
+    int tile, mt, p0, cnt, Nt, rows;
+    int64_t slot;  // -1: invalid expert id / slot
 };
-__device__ __forceinline__ PfItem pf_item(const PrefillArgs &a, int it, int rank) {
+__device__ __forceinline__ PfItem pf_item(const PrefillArgs &a, int it) {
     PfItem x;
     x.tile = it / a.m_tiles;
-    x.mp = it - x.tile * a.m_tiles;
+    x.mt = it - x.tile * a.m_tiles;
     const int4 t = a.tiles[x.tile];
     x.p0 = t.y;
     x.cnt = t.z;
     x.Nt = pf_tile_cols(t.z);
-    x.rows = (int) max((int64_t) -1, min((int64_t) kPfTileM, a.M - (int64_t) (2 * x.mp + rank) * kPfTileM));
+    x.rows = (int) min((int64_t) kPfTileM, a.M - (int64_t) x.mt * kPfTileM);
     x.slot = -1;
     if (t.x >= 0 && t.x < a.n_ids) {
         const int64_t sl = a.remap ? (int64_t) a.remap[t.x] : (int64_t) t.x;
@@ -299,11 +276,6 @@ __device__ __forceinline__ uint32_t h2_pack(float v) {
     asm("cvt.rn.f16x2.f32 %0, %1, %1;" : "=r"(d) : "f"(v));
     return d;
 }
-__device__ __forceinline__ uint32_t h2_pack2(float lo, float hi) {
-    uint32_t d;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-    return d;
-}
 constexpr uint32_t kH2Neg1024 = 0xE400E400u, kH2Sixteenth = 0x2C002C00u, kH2Neg64 = 0xD400D400u;
 
 // 16-byte async copy global -> shared (L2 only); src_bytes 0 zero-fills the destination
@@ -320,11 +292,10 @@ __device__ __forceinline__ void cp_async_wait() {
 // Warp roles (18 warps).  TMEM lane quarter = warp % 4 for every role that touches TMEM.
 constexpr int kPfWarpEpi = 8;    // warps 8..15: epilogue (column half (warp - 8) / 4)
 constexpr int kPfWarpProd = 16;  // producer
-constexpr int kPfWarpMma = 17;   // TMEM allocation; MMA issue (even CTA) / B-landed relay (odd CTA)
-// warps 0..3 / 4..7: dequantiser groups for superblock halves 0 / 1 (A stage 0 / 1)
+constexpr int kPfWarpMma = 17;   // TMEM allocation + MMA issue
+// warps 0..3 / 4..7: dequantiser groups for superblock halves 0 / 1
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
-    pf_gemm_q4k_kernel(const PrefillArgs a) {
+__global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_q4k_kernel(const PrefillArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *raw = smem;
     uint8_t *bst = smem + kPfOffB;
@@ -332,27 +303,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
     PfBars *bars = (PfBars *) (smem + kPfOffBar);
     volatile int *abort = &bars->abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    uint32_t rank;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
-    const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
 
-    const int total = *a.n_tiles * a.m_tiles;  // work items: (token tile, 256-row weight tile)
-    if (pair >= total) return;                 // both CTAs of the pair leave together
+    const int total = *a.n_tiles * a.m_tiles;  // work items: (token tile, 128-row weight tile)
+    if ((int) blockIdx.x >= total) return;
     const int nsb = (int) (a.K / QK_K);
 
     if (tid == 0) {
         for (int i = 0; i < kPfBStages; ++i) {
             mbar_init(&bars->b_full[i], 1);
-            mbar_init(&bars->b_peer[i], 1);
             mbar_init(&bars->b_empty[i], 1);
         }
         for (int i = 0; i < kPfAStages; ++i) {
-            mbar_init(&bars->a_full[i], 256);
+            mbar_init(&bars->a_full[i], 128);
             mbar_init(&bars->a_empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bars->acc_full[i], 1);
-            mbar_init(&bars->acc_empty[i], 512);
+            mbar_init(&bars->acc_empty[i], 256);
         }
         for (int i = 0; i < kPfEpStages; ++i) {
             mbar_init(&bars->ep_full[i], 1 + 128);  // producer (scales copy) + dequantiser group 0
@@ -363,44 +330,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
         fence_mbar_init();
     }
     if (warp == kPfWarpMma) {
-        umma::tmem_alloc2(&bars->tmem, kPfTmemCols);
-        umma::tmem_relinquish2();
+        umma::tmem_alloc(&bars->tmem, kPfTmemCols);
+        umma::tmem_relinquish();
     }
     umma::fence_before_sync();
-    // both CTAs' barriers are initialised before either CTA arrives on the other's
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    __syncthreads();
     umma::fence_after_sync();
     const uint32_t tbase = bars->tmem;
 
     if (warp == kPfWarpProd) {
         // ------------------------------------------------------------ producer
         // Per item, the whole warp first asks L2 to prefetch the NEXT item's weight rows as
-        // contiguous row-long runs (one bulk prefetch per row), so DRAM streams them while
-        // the dequantisers read the current rows 144 bytes at a time.  Then lane 0 issues,
-        // per superblock, the token tile's activation scales and this CTA's halves of the
-        // two B stages (bulk copies).
+        // contiguous row-long runs (one bulk prefetch per row).  Then lane 0 issues, per
+        // superblock, the token tile's activation scales and the two B stages (bulk copies).
         const uint32_t rb = (uint32_t) (a.K / QK_K) * Q4K_BYTES;
         auto prefetch_rows = [&](int it) {
             if (it >= total) return;
-            const PfItem y = pf_item(a, it, rank);
+            const PfItem y = pf_item(a, it);
             if (y.slot < 0) return;
-            const uint8_t *base = a.W + (size_t) y.slot * a.nb2 + (size_t) (2 * y.mp + rank) * kPfTileM * a.nb1;
+            const uint8_t *base = a.W + (size_t) y.slot * a.nb2 + (size_t) y.mt * kPfTileM * a.nb1;
             for (int r = lane; r < y.rows; r += 32)
                 asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + (size_t) r * a.nb1), "r"(rb)
                              : "memory");
         };
-        prefetch_rows(pair);
+        prefetch_rows(blockIdx.x);
         uint32_t b_i = 0, ep_i = 0;
         bool ok = true;
-        for (int it = pair; it < total && ok; it += n_pairs) {
-            prefetch_rows(it + n_pairs);
+        for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
+            prefetch_rows(it + gridDim.x);
             if (lane == 0) {
-                const PfItem x = pf_item(a, it, rank);
-                if (x.slot < 0 && x.mp == 0 && rank == 0) report(a.st, QWB_DEVERR_ID_RANGE, a.tiles[x.tile].x);
+                const PfItem x = pf_item(a, it);
+                if (x.slot < 0 && x.mt == 0) report(a.st, QWB_DEVERR_ID_RANGE, a.tiles[x.tile].x);
                 const float *dat = a.da + (size_t) x.tile * nsb * kPfTileN;
-                const uint32_t sbytes = (uint32_t) x.Nt * kPfHalfK * 2;  // one stage, both halves
-                const uint32_t bbytes = sbytes / 2;
-                const uint8_t *bt = a.btiles + (size_t) x.tile * pf_btile_stride(a.K) + rank * bbytes;
+                const uint32_t bbytes = (uint32_t) x.Nt * kPfHalfK * 2;
+                const uint8_t *bt = a.btiles + (size_t) x.tile * pf_btile_stride(a.K);
                 for (int s = 0; s < nsb && ok; ++s) {
                     const int es = ep_i % kPfEpStages;
                     if (!(ok = pf_wait(&bars->ep_empty[es], ((ep_i / kPfEpStages) & 1) ^ 1, abort, a.st))) break;
@@ -412,7 +375,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
                         const int bs = b_i % kPfBStages;
                         if (!(ok = pf_wait(&bars->b_empty[bs], ((b_i / kPfBStages) & 1) ^ 1, abort, a.st))) break;
                         mbar_arrive_expect_tx(&bars->b_full[bs], bbytes);
-                        bulk_g2s(bst + bs * kPfBBytes, bt + (size_t) (2 * s + h) * sbytes, bbytes, &bars->b_full[bs]);
+                        bulk_g2s(bst + bs * kPfBBytes, bt + (size_t) (2 * s + h) * bbytes, bbytes, &bars->b_full[bs]);
                         ++b_i;
                     }
                     PF_TRACE(1, ep_i - 1);
@@ -435,14 +398,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
         }
         __syncwarp();
     } else if (warp == kPfWarpMma) {
-        if (lane == 0 && rank == 0) {
-            // -------------------------------------------------------- MMA issuer (even CTA)
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
             uint32_t b_i = 0, a_i = 0, acc_i = 0;
             bool ok = true;
-            for (int it = pair; it < total && ok; it += n_pairs) {
-                const PfItem x = pf_item(a, it, rank);
-                const uint32_t idesc = umma::idesc_f16(2 * kPfTileM, x.Nt);
-                const uint32_t lbo = (uint32_t) (x.Nt / 2) * 16;
+            for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
+                const PfItem x = pf_item(a, it);
+                const uint32_t idesc = umma::idesc_f16(kPfTileM, x.Nt);
+                const uint32_t lbo = (uint32_t) x.Nt * 16;
                 for (int s = 0; s < nsb && ok; ++s) {
                     const int ab = acc_i & 1;
                     if (!(ok = pf_wait(&bars->acc_empty[ab], ((acc_i >> 1) & 1) ^ 1, abort, a.st))) break;
@@ -451,46 +414,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
                     const uint32_t d_t = tbase + (uint32_t) ab * kPfAccCols;
                     for (int h = 0; h < 2; ++h) {
                         const int bs = b_i % kPfBStages, as = a_i % kPfAStages;
-                        const uint32_t bpar = (b_i / kPfBStages) & 1;
-                        if (!(ok = pf_wait(&bars->b_full[bs], bpar, abort, a.st))) break;
-                        if (!(ok = pf_wait(&bars->b_peer[bs], bpar, abort, a.st))) break;
+                        if (!(ok = pf_wait(&bars->b_full[bs], (b_i / kPfBStages) & 1, abort, a.st))) break;
+                        if (h == 0) PF_TRACE(11, acc_i);
                         if (!(ok = pf_wait(&bars->a_full[as], (a_i / kPfAStages) & 1, abort, a.st))) break;
+                        PF_TRACE(h == 0 ? 13 : 14, acc_i);
                         umma::fence_after_sync();
                         const uint32_t b_s = smem_u32(bst + bs * kPfBBytes);
                         const uint32_t a_t = tbase + 2 * kPfAccCols + (uint32_t) as * kPfACols;
 #pragma unroll
                         for (int ks = 0; ks < 8; ++ks)
-                            umma::mma2_f16_ts(d_t, a_t + ks * 8, umma::sdesc(b_s + ks * 2 * lbo, lbo, 128), idesc,
-                                              (h | ks) != 0);
-                        umma::mma2_f16_ts(d_t, a_t + 64, umma::sdesc(b_s + 16 * lbo, lbo, 128), idesc, 1u);
-                        umma::commit2_mc(&bars->b_empty[bs], 3);
-                        umma::commit2_mc(&bars->a_empty[as], 3);
+                            umma::mma_f16_ts(d_t, a_t + ks * 8, umma::sdesc(b_s + ks * 2 * lbo, lbo, 128), idesc,
+                                             (h | ks) != 0);
+                        umma::mma_f16_ts(d_t, a_t + 64, umma::sdesc(b_s + 16 * lbo, lbo, 128), idesc, 1u);
+                        umma::commit(&bars->b_empty[bs]);
+                        umma::commit(&bars->a_empty[as]);
                         ++b_i;
                         ++a_i;
                     }
                     if (!ok) break;
-                    umma::commit2_mc(&bars->acc_full[ab], 3);
+                    umma::commit(&bars->acc_full[ab]);
                     PF_TRACE(5, acc_i);
                     ++acc_i;
                 }
             }
-            // all MMAs (which write both CTAs' TMEM) complete before either CTA frees it
-            umma::commit2_mc(&bars->drain, 3);
-            mbar_wait(&bars->drain, 0);
-        } else if (lane == 0) {
-            // -------------------------------------------------------- relay (odd CTA)
-            // tells the MMA issuer when this CTA's half of each B stage has landed
-            uint32_t b_i = 0;
-            bool ok = true;
-            for (int it = pair; it < total && ok; it += n_pairs) {
-                for (int s = 0; s < nsb && ok; ++s)
-                    for (int h = 0; h < 2; ++h, ++b_i) {
-                        const int bs = b_i % kPfBStages;
-                        if (!(ok = pf_wait(&bars->b_full[bs], (b_i / kPfBStages) & 1, abort, a.st))) break;
-                        arrive_on(&bars->b_peer[bs], 0);
-                    }
-            }
-            // the issuer's final commit also arrives here: no MMA is in flight after it
+            // all MMAs issued by this thread have completed before TMEM is released
+            umma::commit(&bars->drain);
             mbar_wait(&bars->drain, 0);
         }
         __syncwarp();
@@ -504,16 +452,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
         uint8_t *mine = raw + (size_t) (grp * 128 + m) * kPfSlot;
         // this CTA's superblocks in order: f -> (item f / nsb, superblock f % nsb); the row
         // pointer of the item being fetched is cached (null: invalid slot or row past M)
-        const int n_sb = (total - pair + n_pairs - 1) / n_pairs * nsb;
+        const int n_sb = (total - (int) blockIdx.x + (int) gridDim.x - 1) / (int) gridDim.x * nsb;
         int f_item = -1;
         const uint8_t *f_row = nullptr;
         auto fetch = [&](int f) {
             if (f < n_sb) {
                 const int k = f / nsb, s = f - k * nsb;
                 if (k != f_item) {
-                    const PfItem y = pf_item(a, pair + k * n_pairs, rank);
+                    const PfItem y = pf_item(a, (int) blockIdx.x + k * (int) gridDim.x);
                     f_row = (y.slot >= 0 && m < y.rows)
-                                ? a.W + (size_t) y.slot * a.nb2 + ((size_t) (2 * y.mp + rank) * kPfTileM + m) * a.nb1
+                                ? a.W + (size_t) y.slot * a.nb2 + ((size_t) y.mt * kPfTileM + m) * a.nb1
                                 : nullptr;
                     f_item = k;
                 }
@@ -531,7 +479,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
         for (int f = 0; f < kPfPre; ++f) fetch(f);
         uint32_t sb_i = 0;
         bool ok = true;
-        for (int it = pair; it < total && ok; it += n_pairs) {
+        for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
             for (int s = 0; s < nsb && ok; ++s, ++sb_i) {
                 cp_async_wait<kPfPre - 1>();  // superblock sb_i has landed
                 if (tid == 0) PF_TRACE(2, sb_i);
@@ -555,7 +503,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
                     const int es = sb_i % kPfEpStages;
                     if (!(ok = pf_wait_warp(&bars->ep_empty[es], ((sb_i / kPfEpStages) & 1) ^ 1, abort, a.st))) break;
                     ep[es * 2 * kPfTileN + kPfTileN + m] = mode == 0 ? d : (mode == 1 ? dmin : 0.f);
-                    umma::mbar_arrive(&bars->ep_full[es]);
+                    warp_arrive(&bars->ep_full[es]);
                 }
                 // 6-bit scale / min of sub-block j (get_scale_min_k4, ggml-quants.c:880-887)
                 auto sbyte = [&](int i) -> uint32_t { return (hw[1 + i / 4] >> (8 * (i % 4))) & 0xFFu; };
@@ -567,9 +515,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
                 };
                 const float r = mode == 0 ? dmin / d : (mode == 1 ? d / dmin : 0.f);
                 const uint32_t k2 = mode == 1 ? h2_pack(r) : 0u;
-                if (tid == 0) PF_TRACE(12, sb_i);
                 const uint32_t a_i = 2 * sb_i + (uint32_t) grp;  // A stages are used in turn by the halves
                 const int as = a_i % kPfAStages;
+                if (tid == 0) PF_TRACE(12, sb_i);
                 if (!(ok = pf_wait_warp(&bars->a_empty[as], ((a_i / kPfAStages) & 1) ^ 1, abort, a.st))) break;
                 if (tid == 0) PF_TRACE(10, sb_i);
                 umma::fence_after_sync();
@@ -602,7 +550,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
                         umma::st16(a_t + (uint32_t) (jj * 32 + g * 16), o);
                     }
                 }
-                if (tid == 0) PF_TRACE(11, sb_i);
                 // min coefficients -(dmin/d)*m as hi + lo: Veltkamp split (factor 2^13 + 1)
                 // leaves 11 significant bits in hi, so hi is an fp16 value and lo = full - hi
                 // is exact; fp16(lo) then carries the next 11 bits.
@@ -622,12 +569,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
                     o8[c] = h2_pack(v);
                 }
                 umma::st8(a_t + 64, o8);
-                if (tid == 0) PF_TRACE(13, sb_i);
                 umma::wait_st();
-                if (tid == 0) PF_TRACE(14, sb_i);
                 umma::fence_before_sync();
-                if (rank == 0) umma::mbar_arrive(&bars->a_full[as]);
-                else arrive_on(&bars->a_full[as], 0);
+                warp_arrive(&bars->a_full[as]);
                 if (tid == 0) PF_TRACE(9, sb_i);
                 if (tid == 128) PF_TRACE(3, sb_i);
             }
@@ -639,8 +583,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
         const uint32_t lane_base = (uint32_t) (qd * 32) << 16;
         uint32_t acc_i = 0;
         bool ok = true;
-        for (int it = pair; it < total && ok; it += n_pairs) {
-            const PfItem x = pf_item(a, it, rank);
+        for (int it = blockIdx.x; it < total && ok; it += gridDim.x) {
+            const PfItem x = pf_item(a, it);
             // output row offsets (in floats, < 2^32 checked on the host) of columns
             // 64g + lane and 64g + 32 + lane
             uint32_t off[2] = {0, 0};
@@ -686,14 +630,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
                     }
                 }
                 umma::fence_before_sync();
-                if (rank == 0) umma::mbar_arrive(&bars->acc_empty[ab]);
-                else arrive_on(&bars->acc_empty[ab], 0);
-                umma::mbar_arrive(&bars->ep_empty[es]);
+                warp_arrive(&bars->acc_empty[ab]);
+                warp_arrive(&bars->ep_empty[es]);
                 if (tid == kPfWarpEpi * 32) PF_TRACE(7, acc_i);
             }
             if (!ok) break;
             // rows of an invalid expert slot come out as zeros (row scale 0)
-            const int64_t row = (int64_t) (2 * x.mp + rank) * kPfTileM + m;
+            const int64_t row = (int64_t) x.mt * kPfTileM + m;
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
                 const uint32_t o = __shfl_sync(0xffffffffu, off[i >> 5], i & 31);
@@ -702,13 +645,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPfThreads, 1)
         }
     }
 
-    // no MMA is in flight (both CTAs waited for the issuer's final commit) and no TMEM
-    // load or store is pending: free the pair's TMEM
     umma::fence_before_sync();
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    __syncthreads();
     if (warp == kPfWarpMma) {
         umma::fence_after_sync();
-        umma::tmem_dealloc2(tbase, kPfTmemCols);
+        umma::tmem_dealloc(tbase, kPfTmemCols);
     }
 }
 
@@ -719,8 +660,7 @@ cudaError_t launch_pf_gemm_q4k(const PrefillArgs &a, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    // an even number of CTAs (pairs), one per SM
-    pf_gemm_q4k_kernel<<<num_sms() & ~1, kPfThreads, kPfSmem, s>>>(a);
+    pf_gemm_q4k_kernel<<<num_sms(), kPfThreads, kPfSmem, s>>>(a);
     return cudaGetLastError();
 }
 

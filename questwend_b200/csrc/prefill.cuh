@@ -14,9 +14,8 @@ constexpr int kPfTileM = 128;
 // 16 block sums each (the min-term columns).
 constexpr int kPfHalfK = 144;
 
-// Token columns of a tile of `cnt` pairs: the CTA-pair MMA needs N % 32 == 0 (each CTA
-// of the pair holds N/2 token rows of B).
-__host__ __device__ inline int pf_tile_cols(int cnt) { return (cnt + 31) & ~31; }
+// Token columns of a tile of `cnt` pairs (the M=128 MMA takes N in steps of 16).
+__host__ __device__ inline int pf_tile_cols(int cnt) { return (cnt + 15) & ~15; }
 
 // Bytes of the B tile buffer for `max_tiles` tiles of a K-long activation.
 __host__ __device__ inline size_t pf_btile_stride(int64_t K) { return (size_t) kPfTileN * (size_t) (K / QK_K) * 2 * kPfHalfK * 2; }
@@ -36,7 +35,7 @@ struct PrefillArgs {
     float *dst;             // dst[m, j, t] at dst + j*dnb1 + t*dnb2 (bytes) + 4m
     size_t dnb1, dnb2;
     int n_used;
-    int m_tiles;            // 256-row weight tiles, ceil(M / 256)
+    int m_tiles;            // 128-row weight tiles, ceil(M / 128)
     qwb_status_block *st;
 };
 

@@ -164,6 +164,17 @@ __device__ __forceinline__ void mma2_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         "r"(0u), "r"(0u)
         : "memory");
 }
+__device__ __forceinline__ void mma2_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}" ::"r"(
+            d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u),
+        "r"(0u), "r"(0u)
+        : "memory");
+}
 // Arrive on the mbarrier at this smem offset in every CTA of `cta_mask` once the MMAs
 // issued so far by this thread have completed.
 __device__ __forceinline__ void commit2_mc(uint64_t *bar, uint16_t cta_mask) {
