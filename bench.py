@@ -19,6 +19,16 @@ the token's hidden state copied from pinned host memory and the layer output cop
 every step.  `roofline` is the gate/up GEMV kernel (the largest weight stream per layer).
 `cpu_baseline` times the reference's own ggml CPU backend (oracle/_ref, built from the
 reference sources) on one layer of the same shapes, scaled to 48 layers.
+
+`prefill` (rank 0): BASELINE config 3, the prefill grouped-GEMM sweep of MUL_MAT_ID on
+Q4_K experts (hidden 4096, 128 experts, top-8, expert intermediate 1536; gate/up shape
+[4096 -> 1536] with one activation row per token and down shape [1536 -> 4096] with one
+per (token, slot)), n_tokens in {512, 2048, 8192}, routing from Gumbel-perturbed
+Zipf(1.1) expert popularity.  TFLOPS = 2 * T * 8 * K * M / time: `tflops` for the whole
+qwb_mul_mat_id call (activation quantisation, expert sort, B-tile gather, GEMM), `gemm_tflops`
+for the tensor-core kernel alone (event marks around it).  The weights of all 128 experts
+(453 MB per matrix) exceed L2.  Its `roofline` compares the GEMM kernel with the measured
+dense bf16 peak; its `cpu_baseline` times the reference CPU backend on T = 512, gate shape.
 """
 from __future__ import annotations
 
@@ -176,6 +186,114 @@ def run_reference(args):
     }))
 
 
+PF_H, PF_F, PF_UNIQUE, PF_TOKENS = 4096, 1536, 8, (512, 2048, 8192)
+
+
+def zipf_ids(T, n_exp, n_used, seed, s=1.1):
+    """top-n_used of log Zipf(s) popularity (seeded expert ranks) + Gumbel noise."""
+    r = np.random.default_rng(seed)
+    pop = 1.0 / np.arange(1, n_exp + 1, dtype=np.float64) ** s
+    logits = np.log(pop[r.permutation(n_exp)])[None, :] + r.gumbel(size=(T, n_exp))
+    return np.argsort(-logits, axis=1, kind="stable")[:, :n_used].astype(np.int32)
+
+
+def prefill_experts(seed=7):
+    """PF_UNIQUE distinct Q4_K experts for the gate/up shape [PF_H -> PF_F] and the down
+    shape [PF_F -> PF_H]: N(0, 0.02) weights quantized with the reference quantizer."""
+    import concurrent.futures as cf
+
+    import oracle as O
+
+    def one(args):
+        role, i = args
+        rng = np.random.default_rng(seed * 1000 + role * 100 + i)
+        rows, k = (PF_F, PF_H) if role == 0 else (PF_H, PF_F)
+        x = (rng.standard_normal((rows, k), dtype=np.float32) * 0.02).astype(np.float32)
+        return O.quantize_weights(Q4_K, x)
+
+    with cf.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as ex:
+        out = list(ex.map(one, [(r, i) for r in range(2) for i in range(PF_UNIQUE)]))
+    return [np.concatenate(out[r * PF_UNIQUE:(r + 1) * PF_UNIQUE]) for r in range(2)]
+
+
+def prefill_sweep(q, lib, dev, warmup, iters, cpu):
+    import ctypes as C
+
+    import torch
+
+    from questwend_b200 import _lib as L
+    experts = prefill_experts()
+    reps = E // PF_UNIQUE
+    pools = []
+    for role, (k, rows) in enumerate(((PF_H, PF_F), (PF_F, PF_H))):
+        base = torch.from_numpy(experts[role]).to(dev)
+        buf = torch.empty(base.numel() * reps + 16, dtype=torch.uint8, device=dev)
+        buf[:-16].view(reps, -1).copy_(base.expand(reps, -1))
+        pools.append((q.QTensor(buf[:-16], Q4_K, (k, rows, E, 1)), k, rows))
+    L.check("qwb_profile_enable", lib.qwb_profile_enable(8))
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+    points = []
+    for T in PF_TOKENS:
+        ids = torch.from_numpy(zipf_ids(T, E, K_USED, seed=T)).to(dev)
+        for name, (W, k, rows) in zip(("gate_up", "down"), pools):
+            nb = 1 if name == "gate_up" else K_USED
+            b = torch.randn((T, nb, k), generator=gen, device=dev)
+            out = torch.empty((T, K_USED, rows), device=dev)
+            for _ in range(max(3, warmup)):
+                q.mul_mat_id(W, b, ids, out)
+            torch.cuda.synchronize()
+            tot, gemm = [], []
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            for _ in range(iters):
+                lib.qwb_profile_reset()
+                e0.record()
+                q.mul_mat_id(W, b, ids, out)
+                e1.record()
+                torch.cuda.synchronize()
+                tot.append(e0.elapsed_time(e1))
+                n = lib.qwb_profile_count() - 1
+                ms = (C.c_float * max(n, 1))()
+                tg = (C.c_int32 * max(n, 1))()
+                L.check("qwb_profile_read", lib.qwb_profile_read(ms, tg, n))
+                gemm.append(sum(m for m, t in zip(ms[:n], tg[:n]) if t == 5))
+            assert torch.isfinite(out).all()
+            fl = 2.0 * T * K_USED * k * rows
+            t_ms, g_ms = float(np.median(tot)), float(np.median(gemm))
+            points.append({"tokens": T, "shape": name, "ms": t_ms, "tflops": fl / (t_ms * 1e-3) / 1e12,
+                           "gemm_ms": g_ms, "gemm_tflops": fl / (g_ms * 1e-3) / 1e12 if g_ms > 0 else None})
+    L.check("qwb_profile_enable", lib.qwb_profile_enable(0))
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, pkind = json.load(f)["bf16_tflops"], "measured bf16 burst"
+    except Exception:
+        peak, pkind = 1590.0, "fallback"
+    top = [p for p in points if p["tokens"] == PF_TOKENS[-1] and p["shape"] == "gate_up"][0]
+    res = {"config": {"workload": "C3 prefill grouped GEMM, MUL_MAT_ID Q4_K x Q8_K", "hidden": PF_H,
+                      "expert_ffn": PF_F, "experts": E, "top_k": K_USED, "routing": "Zipf(1.1) + Gumbel",
+                      "tokens": list(PF_TOKENS), "l2": "weights 453 MB per matrix > L2"},
+           "points": points,
+           "roofline": {"bound": "tensor", "kernel": f"grouped GEMM, gate/up shape, T={PF_TOKENS[-1]}",
+                        "achieved": top["gemm_tflops"], "peak": peak, "peak_kind": pkind, "unit": "TFLOP/s",
+                        "frac": top["gemm_tflops"] / peak if top["gemm_tflops"] else None, "traffic": None}}
+    if cpu:
+        import oracle as O
+        if O.ref_available():
+            threads = os.cpu_count() or 1
+            O.set_ref_threads(threads)
+            T = PF_TOKENS[0]
+            ids = zipf_ids(T, E, K_USED, seed=T)
+            x = np.random.default_rng(3).standard_normal((T, 1, PF_H)).astype(np.float32)
+            w = np.tile(experts[0], reps)
+            O.mul_mat_id(Q4_K, w, PF_H, PF_F, E, x, ids, impl="ref", iters=1)
+            _, ms = O.mul_mat_id(Q4_K, w, PF_H, PF_F, E, x, ids, impl="ref", iters=3)
+            fl = 2.0 * T * K_USED * PF_H * PF_F
+            res["cpu_baseline"] = {"value": fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "cores": threads,
+                                   "kind": "reference",
+                                   "sample": f"reference ggml CPU mul_mat_id, T={T}, gate shape, 3 calls ({ms:.1f} ms each)"}
+    return res
+
+
 def workload_config(n, n_layers=LAYERS):
     return {"workload": "qwen3-30b-a3b MoE FFN stack, batch-1 decode", "layers": n_layers, "hidden": H,
             "experts": E, "top_k": K_USED, "expert_ffn": F, "gate_up": "Q4_K", "down": "Q6_K",
@@ -186,12 +304,13 @@ def workload_config(n, n_layers=LAYERS):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=500)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="qwb", choices=["qwb", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="MoE layers per step (default 48; fewer only for profiling captures)")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (config 3) sweep")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -371,9 +490,11 @@ def main():
             result["cpu_baseline"] = {"value": 1000.0 / (lm * n_layers), "unit": "tokens/s", "cores": threads,
                                       "kind": "reference",
                                       "sample": f"one MoE layer x 20 evaluations ({lm:.3f} ms each), scaled x{n_layers}"}
+    del graph, pgraph
+    if rank == 0 and not args.no_prefill:
+        result["prefill"] = prefill_sweep(q, lib, dev, args.warmup, 10, cpu=(world == 1 and not args.no_cpu))
     if rank == 0:
         print(json.dumps(result))
-    del graph, pgraph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
