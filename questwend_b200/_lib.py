@@ -52,6 +52,20 @@ class MoeFfnDesc(C.Structure):
                 ("norm_w", C.c_void_p), ("norm_eps", C.c_float)]
 
 
+class MoeEpPrepareDesc(C.Structure):
+    _fields_ = [("x", C.c_void_p), ("norm_w", C.c_void_p), ("norm_eps", C.c_float), ("router_w", C.c_void_p),
+                ("mask", C.c_void_p), ("H", C.c_int64), ("E", C.c_int64), ("n_used", C.c_int64), ("T", C.c_int64),
+                ("act_type", C.c_int32), ("reserved", C.c_int32), ("xq", C.c_void_p), ("selected", C.c_void_p),
+                ("weights", C.c_void_p)]
+
+
+class MoeEpExpertsDesc(C.Structure):
+    _fields_ = [("xq", C.c_void_p), ("selected", C.c_void_p), ("weights", C.c_void_p),
+                ("gate", Tensor), ("up", Tensor), ("down", Tensor), ("expert_lo", C.c_int64),
+                ("H", C.c_int64), ("F", C.c_int64), ("E", C.c_int64), ("n_used", C.c_int64), ("T", C.c_int64),
+                ("out", C.c_void_p)]
+
+
 _lib = None
 
 # (name, restype, argtypes) for every QWB_API symbol of include/qwb.h
@@ -71,6 +85,10 @@ SIGNATURES = [
     ("qwb_moe_weighted_sum", C.c_int, [_P, _P, _P, C.c_int64, C.c_int64, C.c_int64, _P]),
     ("qwb_moe_ffn_workspace_size", C.c_size_t, [C.POINTER(MoeFfnDesc)]),
     ("qwb_moe_ffn", C.c_int, [C.POINTER(MoeFfnDesc), _P, C.c_size_t, _P, _P]),
+    ("qwb_moe_ep_prepare_workspace_size", C.c_size_t, [C.POINTER(MoeEpPrepareDesc)]),
+    ("qwb_moe_ep_prepare", C.c_int, [C.POINTER(MoeEpPrepareDesc), _P, C.c_size_t, _P, _P]),
+    ("qwb_moe_ep_experts_workspace_size", C.c_size_t, [C.POINTER(MoeEpExpertsDesc)]),
+    ("qwb_moe_ep_experts", C.c_int, [C.POINTER(MoeEpExpertsDesc), _P, C.c_size_t, _P, _P]),
     ("qwb_profile_enable", C.c_int, [C.c_int]),
     ("qwb_profile_reset", C.c_int, []),
     ("qwb_profile_count", C.c_int, []),

@@ -28,7 +28,7 @@ namespace qwb {
 __global__ void __launch_bounds__(1024) mmid_index_kernel(const int32_t *__restrict__ ids, int64_t ids_s0,
                                                           int64_t ids_s1, int n_used, int T, int n_as, int NT,
                                                           MmidIndex ix, float *dst, size_t dnb1, size_t dnb2,
-                                                          int64_t M, qwb_status_block *st) {
+                                                          int64_t M, qwb_status_block *st, int skip_neg) {
     extern __shared__ int sh[];
     int *cnt = sh;              // [n_as]
     int *off = sh + n_as;       // [n_as] pair offset, later running cursor
@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(1024) mmid_index_kernel(const int32_t *__restr
         if (e >= 0 && e < n_as) {
             const int pos = atomicAdd(&off[e], 1);
             ix.pairs[pos] = p;
-        } else {
+        } else if (!(skip_neg && e == -1)) {
             report(st, QWB_DEVERR_ID_RANGE, e);
             if (dst) {
                 float *o = (float *) ((char *) dst + (size_t) j * dnb1 + (size_t) t * dnb2);
@@ -322,7 +322,7 @@ MmidIndex mmid_index_at(void *base, int64_t P, int64_t n_as, int NT) {
 
 cudaError_t launch_index(const int32_t *ids, int64_t s0, int64_t s1, int n_used, int T, int n_as, int NT,
                          MmidIndex ix, float *dst, size_t dnb1, size_t dnb2, int64_t M, qwb_status_block *st,
-                         cudaStream_t s) {
+                         cudaStream_t s, int skip_neg) {
     const size_t smem = (size_t) 3 * n_as * 4;
     static size_t configured = 0;
     if (smem > 48 * 1024 && smem > configured) {
@@ -330,7 +330,7 @@ cudaError_t launch_index(const int32_t *ids, int64_t s0, int64_t s1, int n_used,
         if (e != cudaSuccess) return e;
         configured = smem;
     }
-    mmid_index_kernel<<<1, 1024, smem, s>>>(ids, s0, s1, n_used, T, n_as, NT, ix, dst, dnb1, dnb2, M, st);
+    mmid_index_kernel<<<1, 1024, smem, s>>>(ids, s0, s1, n_used, T, n_as, NT, ix, dst, dnb1, dnb2, M, st, skip_neg);
     return cudaGetLastError();
 }
 

@@ -43,9 +43,11 @@ int pick_nt(int64_t pairs, int64_t n_as);
 int64_t mmid_max_tiles(int64_t P, int64_t n_as, int NT);
 size_t mmid_index_bytes(int64_t P, int64_t n_as, int NT);
 MmidIndex mmid_index_at(void *base, int64_t P, int64_t n_as, int NT);
+// skip_neg: ids equal to -1 (pairs routed to another GPU's experts) are left out silently;
+// every other id outside [0, n_as) is reported (and its dst row zeroed when dst is given).
 cudaError_t launch_index(const int32_t *ids, int64_t s0, int64_t s1, int n_used, int T, int n_as, int NT,
                          MmidIndex ix, float *dst, size_t dnb1, size_t dnb2, int64_t M, qwb_status_block *st,
-                         cudaStream_t s);
+                         cudaStream_t s, int skip_neg = 0);
 
 // allow_prefill: take the tensor-core grouped GEMM when the problem has many tokens per
 // expert (its workspace is larger); false keeps the GEMV path for every size.
