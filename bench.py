@@ -12,9 +12,13 @@ are larger than L2, no flush is needed.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl qwb|reference]
 
-Prints one JSON line (rank 0).  `value` is decode tokens/s of the whole job (all ranks;
-each rank decodes its own token stream: the layer has no cross-GPU exchange at batch 1
-in this arm, "scaling": "weak").  `e2e` is the same metric through the public C ABI with
+Prints one JSON line (rank 0).  `value` is decode tokens/s of the whole job.  At N = 1 the
+step is the fused single-GPU layer (qwb_moe_ffn).  At N > 1 the experts are sharded over
+the ranks (expert parallelism: rank r holds experts [r*128/N, (r+1)*128/N) of every layer,
+router replicated) and every rank decodes its own token, so a step is N tokens
+("scaling": "weak"): per layer each rank routes and quantizes its token, NCCL all-gathers
+the Q8_K rows and routing, runs its experts over all N tokens and reduce-scatters the f32
+partial outputs (questwend_b200.expert_parallel).  `e2e` is the same metric through the public C ABI with
 the token's hidden state copied from pinned host memory and the layer output copied back
 every step.  `roofline` is the gate/up GEMV kernel (the largest weight stream per layer).
 `cpu_baseline` times the reference's own ggml CPU backend (oracle/_ref, built from the
@@ -294,6 +298,116 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu):
     return res
 
 
+def run_ep(args, world, rank, local):
+    """N > 1: the same 48-layer decode stack with the experts sharded over the ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import questwend_b200 as q
+    from questwend_b200.expert_parallel import ExpertShard, moe_layer, shard_range
+    q.lib()
+    dev = torch.device("cuda", local)
+    lo, n = shard_range(E, world, rank)
+    g, u, d = quantized_experts(seed=0)
+    base = [torch.from_numpy(a).to(dev) for a in (g, u, d)]
+    n_layers = args.layers
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234)  # router and ffn_norm weights replicated on every rank
+    layers = []
+    for layer in range(n_layers):
+        mats = []
+        for role, (t, rows, K) in enumerate(((Q4_K, F, H), (Q4_K, F, H), (Q6_K, H, F))):
+            # global expert e of this layer is unique expert (e - layer) mod UNIQUE, as in
+            # the single-GPU arm
+            idx = torch.tensor([((lo + i) % UNIQUE - layer) % UNIQUE for i in range(n)], device=dev)
+            sel_rows = base[role].view(UNIQUE, -1).index_select(0, idx).reshape(-1)
+            buf = torch.empty(sel_rows.numel() + 16, dtype=torch.uint8, device=dev)
+            buf[:-16].copy_(sel_rows)
+            mats.append(q.QTensor(buf[:-16], t, (K, rows, n, 1)))
+        rw = torch.randn((E, H), generator=gen, device=dev) * 0.02
+        nw = 1.0 + 0.1 * torch.randn(H, generator=gen, device=dev)
+        layers.append((rw, nw, ExpertShard(mats[0], mats[1], mats[2], lo, n)))
+    x0 = torch.randn((1, H), generator=torch.Generator(device=dev).manual_seed(77 + rank), device=dev)
+
+    def step(x):
+        for rw, nw, shard in layers:
+            x = moe_layer(x, rw, shard, K_USED, E, norm_w=nw, norm_eps=1e-6)[0]
+        return x
+
+    xd = x0.clone()
+    # eager warm-up (sizes the workspace, checks the output), then the whole step (48
+    # layers, kernels and NCCL collectives) captured in one CUDA graph
+    for _ in range(2):
+        y = step(xd)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y).all()
+    dist.barrier()
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    cs.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cs):
+        step(xd)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=cs):
+            y_graph = step(xd)
+    torch.cuda.synchronize()
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.isfinite(y_graph).all()
+    dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        t0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        t1.record()
+        torch.cuda.synchronize()
+    ms_step = t0.elapsed_time(t1) / args.steps
+    # end to end: the rank's token from pinned host memory, the layer output back
+    x_host = torch.randn((1, H), generator=torch.Generator().manual_seed(5 + rank)).pin_memory()
+    y_host = torch.empty((1, H)).pin_memory()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps):
+        xd.copy_(x_host, non_blocking=True)
+        graph.replay()
+        y_host.copy_(y_graph, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    del graph
+    times = torch.tensor([ms_step, ms_e2e], device=dev)
+    dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms_step, ms_e2e = times.tolist()
+    hbm, kind = peaks()
+    if rank == 0:
+        cfg = workload_config(world, n_layers)
+        cfg["parallelism"] = f"ep{world}"
+        cfg["experts_per_gpu"] = n
+        print(json.dumps({
+            "metric": "decode_tokens_per_s", "value": world * 1000.0 / ms_step, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "q4_K/q6_K x q8_K -> f32", "data": "synthetic (seeded N(0,0.02) weights, ggml quantizer)",
+            "config": cfg,
+            "e2e": {"value": world * 1000.0 / ms_e2e, "unit": "tokens/s", "h2d_bytes_per_step": H * 4,
+                    "d2h_bytes_per_step": H * 4},
+            "collectives_per_step": 2 * n_layers,
+            "gpu_launches": args.steps * 11 * n_layers,
+            "roofline": {"bound": "latency", "kernel": "expert-parallel layer (collective-bound at batch 1)",
+                         "achieved": None, "peak": hbm, "peak_kind": kind, "unit": "GB/s", "frac": None,
+                         "traffic": None},
+            "clocks": clk.summary(),
+        }))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def workload_config(n, n_layers=LAYERS):
     return {"workload": "qwen3-30b-a3b MoE FFN stack, batch-1 decode", "layers": n_layers, "hidden": H,
             "experts": E, "top_k": K_USED, "expert_ffn": F, "gate_up": "Q4_K", "down": "Q6_K",
@@ -328,6 +442,7 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        return run_ep(args, world, rank, local)
     lib = q.lib()
 
     # ---------------------------------------------------------------- weights

@@ -40,6 +40,32 @@ __global__ void unpack_q80_kernel(const uint8_t *__restrict__ packed, int64_t n_
     for (int i = 0; i < QK8_0; ++i) dst[i] = (int8_t) src[2 + i];
 }
 
+// q8 planes -> packed ggml blocks (the exchange format)
+__global__ void pack_q8K_kernel(Q8Planes pl, int64_t n_rows, int64_t K, uint8_t *__restrict__ packed) {
+    const int64_t nb = K / QK_K;
+    const int64_t b = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // one block per warp
+    const int lane = threadIdx.x & 31;
+    if (b >= n_rows * nb) return;
+    const int64_t r = b / nb, c = b - r * nb;
+    uint8_t *dst = packed + b * Q8K_BYTES;  // 4-byte aligned only (292-byte blocks)
+    const uint2 q = *(const uint2 *) (pl.qs + r * K + c * QK_K + 8 * lane);
+    uint32_t *d32 = (uint32_t *) (dst + 4 + 8 * lane);
+    d32[0] = q.x;
+    d32[1] = q.y;
+    if (lane == 0) *(float *) dst = pl.d[r * plane_d_stride(K, QK_K) + c];
+    if (lane < 16) *(int16_t *) (dst + 4 + QK_K + 2 * lane) = pl.bsum[r * plane_bsum_stride(K) + c * 16 + lane];
+}
+__global__ void pack_q80_kernel(Q8Planes pl, int64_t n_rows, int64_t K, uint8_t *__restrict__ packed) {
+    const int64_t nb = K / QK8_0;
+    const int64_t b = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n_rows * nb) return;
+    const int64_t r = b / nb, c = b - r * nb;
+    uint8_t *dst = packed + b * Q80_BYTES;
+    *(uint16_t *) dst = f2h_rn(pl.d[r * plane_d_stride(K, QK8_0) + c]);  // exact: d came from an fp16
+    const int8_t *src = pl.qs + r * K + c * QK8_0;
+    for (int i = 0; i < QK8_0; ++i) dst[2 + i] = (uint8_t) src[i];
+}
+
 // local expert id of every (token, slot): id - lo when this GPU owns it, -1 otherwise;
 // ids outside [0, E) are reported and also skipped
 __global__ void local_ids_kernel(const int32_t *__restrict__ sel, int64_t P, int64_t lo, int64_t n_local, int64_t E,
@@ -73,8 +99,11 @@ namespace {
 bool ok_weight_type(int t) { return t == QWB_TYPE_Q4_K || t == QWB_TYPE_Q6_K || t == QWB_TYPE_Q8_0; }
 
 // ------------------------------------------------------------------ prepare
+// few tokens: the fused router kernel (H % 1024 == 0)
+bool fused_router(const qwb_moe_ep_prepare_desc *d) { return d->T <= kMaxRouterT && d->H % 1024 == 0; }
+
 struct PrepPlan {
-    size_t off_logits, off_xn, total;
+    size_t off_logits, off_xn, off_planes, total;
 };
 qwb_status plan_prep(const qwb_moe_ep_prepare_desc *d, PrepPlan &p) {
     if (!d) return QWB_ERR_INVALID_ARG;
@@ -87,6 +116,8 @@ qwb_status plan_prep(const qwb_moe_ep_prepare_desc *d, PrepPlan &p) {
     o += align_up((size_t) (d->T * d->E) * 4, 256);
     p.off_xn = o;
     if (d->norm_w) o += align_up((size_t) (d->T * d->H) * 4, 256);
+    p.off_planes = o;
+    if (fused_router(d)) o += planes_bytes(d->T, d->H, d->act_type == QWB_TYPE_Q8_K);
     p.total = o;
     return QWB_OK;
 }
@@ -144,6 +175,29 @@ extern "C" QWB_API qwb_status qwb_moe_ep_prepare(const qwb_moe_ep_prepare_desc *
     if (((uintptr_t) d->x | (uintptr_t) d->router_w | (uintptr_t) d->norm_w) % 16) return QWB_ERR_ALIGNMENT;
     cudaStream_t s = (cudaStream_t) stream;
     char *w = (char *) ws;
+    const bool kq = d->act_type == QWB_TYPE_Q8_K;
+    if (fused_router(d)) {
+        // few tokens: one fused launch (norm, router GEMV, top-k, Q8 planes), then pack
+        Q8Planes pl = planes_at(w + p.off_planes, d->T, d->H, kq);
+        RouterArgs r{};
+        r.x = d->x; r.router_w = d->router_w; r.mask = d->mask;
+        r.H = d->H; r.E = d->E; r.T = d->T; r.n_used = d->n_used;
+        r.logits = (float *) (w + p.off_logits);
+        r.counter = (unsigned *) w;
+        r.selected = d->selected; r.weights = d->weights;
+        r.xq = pl; r.kq = kq;
+        r.norm_w = d->norm_w; r.norm_eps = d->norm_eps;
+        cudaError_t e = launch_router_fused(r, s);
+        if (e != cudaSuccess) return QWB_ERR_CUDA;
+        if (kq) {
+            const int64_t blocks = d->T * (d->H / QK_K);
+            pack_q8K_kernel<<<(unsigned) ceil_div(blocks, 8), 256, 0, s>>>(pl, d->T, d->H, (uint8_t *) d->xq);
+        } else {
+            const int64_t blocks = d->T * (d->H / QK8_0);
+            pack_q80_kernel<<<(unsigned) ceil_div(blocks, 256), 256, 0, s>>>(pl, d->T, d->H, (uint8_t *) d->xq);
+        }
+        return cudaGetLastError() == cudaSuccess ? QWB_OK : QWB_ERR_CUDA;
+    }
     const float *xin = d->x;
     cudaError_t e = cudaSuccess;
     if (d->norm_w) {

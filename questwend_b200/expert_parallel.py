@@ -8,7 +8,8 @@ Per layer:
 
   1. prepare on the rank's own tokens (rms_norm * ffn_norm, router, top-k) and quantize
      the normalised rows to the gate/up weights' vec_dot type (qwb_moe_ep_prepare);
-  2. all-gather the packed rows, selected expert ids and routing weights;
+  2. all-gather the packed rows, selected expert ids and routing weights (one collective:
+     the three are laid side by side in one byte row per token);
   3. run the SwiGLU expert FFN of the rank's experts over all N*T tokens
      (qwb_moe_ep_experts), producing f32 partial sums;
   4. reduce-scatter (sum) the partial sums back to the token owners and add the residual.
@@ -84,6 +85,20 @@ def _reduce_scatter(t: torch.Tensor, group) -> torch.Tensor:
     return t[rank * rows:(rank + 1) * rows].clone()
 
 
+def _gather_routed(xq: torch.Tensor, sel: torch.Tensor, w: torch.Tensor, group):
+    """All-gather (xq, sel, w) of every rank as one byte tensor [T, xq bytes + 8 n_used]."""
+    T = xq.shape[0]
+    if dist.get_world_size(group) == 1:
+        return xq, sel, w
+    row = torch.cat([xq.reshape(T, -1).view(torch.uint8), sel.view(torch.uint8), w.view(torch.uint8)], 1)
+    allr = _all_gather(row, group)
+    nb = row.shape[1] - sel.shape[1] * 8
+    xq_all = allr[:, :nb].contiguous().view(xq.dtype).reshape((allr.shape[0],) + tuple(xq.shape[1:]))
+    sel_all = allr[:, nb:nb + 4 * sel.shape[1]].contiguous().view(torch.int32)
+    w_all = allr[:, nb + 4 * sel.shape[1]:].contiguous().view(torch.float32)
+    return xq_all, sel_all, w_all
+
+
 def moe_layer(x: torch.Tensor, router_w: torch.Tensor, shard: ExpertShard, n_used: int, n_expert: int,
               group=None, norm_w=None, norm_eps: float = 1e-6, residual: bool = True, act_type: int = ops.Q8_K,
               backend=None):
@@ -92,7 +107,7 @@ def moe_layer(x: torch.Tensor, router_w: torch.Tensor, shard: ExpertShard, n_use
     tokens; out = build_moe(rms_norm(x) * norm_w) (+ x when residual)."""
     backend = backend or CudaBackend()
     xq, sel, w = backend.prepare(x, router_w, n_used, norm_w, norm_eps, act_type)
-    xq_all, sel_all, w_all = _all_gather(xq, group), _all_gather(sel, group), _all_gather(w, group)
+    xq_all, sel_all, w_all = _gather_routed(xq, sel, w, group)
     part = backend.experts(xq_all, sel_all, w_all, shard, n_expert)
     out = _reduce_scatter(part, group)
     if residual:
