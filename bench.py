@@ -50,6 +50,9 @@ sys.path.insert(0, ROOT)
 import numpy as np  # noqa: E402
 
 H, F, E, K_USED, LAYERS = 2048, 768, 128, 8, 48
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate/up decode launch, from the ncu
+# capture summarised in profiles/decode_moe_layer_v2_ncu.md (same kernel, same shapes)
+GATEUP_TRAFFIC_BYTES = 14_179_840
 Q4_K, Q6_K = 12, 14
 ROW_GU = H // 256 * 144        # bytes per gate/up row
 ROW_D = F // 256 * 210         # bytes per down row
@@ -587,7 +590,8 @@ def main():
         "decode_hbm_frac": step_bytes / (ms_step * 1e-3) / 1e9 / hbm,
         "roofline": {"bound": "hbm", "kernel": "moe gate/up GEMV (GLU) per layer", "achieved": achieved,
                      "peak": hbm, "peak_kind": kind, "unit": "GB/s",
-                     "frac": achieved / hbm if achieved else None, "traffic": None,
+                     "frac": achieved / hbm if achieved else None, "traffic": GATEUP_TRAFFIC_BYTES,
+                     "traffic_source": "ncu capture, profiles/decode_moe_layer_v2_ncu.md",
                      "algorithmic_bytes": gu_bytes},
         "kernels_us": {"router": 1e3 * float(np.mean(per_kernel.get(1, [0]))), "gate_up": 1e3 * (gu_ms or 0),
                        "down": 1e3 * (dn_ms or 0)},

@@ -233,6 +233,25 @@ cudaError_t launch_router_fused(const RouterArgs &r, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// ------------------------------------------------------- logits, up to 512 tokens
+// One CTA per expert e: its router row staged in shared memory, one warp per token
+// (lanes stride over h, warp-shuffle sum), so E CTAs stream the router weights once.
+__global__ void __launch_bounds__(256) logits_rows_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                                                          float *__restrict__ out, int64_t T, int64_t E, int64_t H) {
+    extern __shared__ float ws_row[];
+    const int64_t e = blockIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int64_t h = tid; h < H; h += blockDim.x) ws_row[h] = w[e * H + h];
+    __syncthreads();
+    for (int64_t t = warp; t < T; t += blockDim.x >> 5) {
+        const float *xr = x + t * H;
+        float acc = 0.f;
+        for (int64_t h = lane; h < H; h += 32) acc = fmaf(xr[h], ws_row[h], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) out[t * E + e] = acc;
+    }
+}
+
 // ------------------------------------------------------- logits GEMM (large T)
 // logits[t][e] = sum_h x[t][h] * w[e][h]; 64x64 output tile per CTA, 256 threads, 4x4
 // outputs per thread, K chunks of 16 staged in shared memory.
@@ -275,6 +294,10 @@ __global__ void __launch_bounds__(256) logits_gemm_kernel(const float *__restric
 
 cudaError_t launch_logits_gemm(const float *x, const float *w, float *out, int64_t T, int64_t E, int64_t H,
                                cudaStream_t s) {
+    if (T <= 512 && H * 4 <= 48 * 1024) {
+        logits_rows_kernel<<<(unsigned) E, 256, (size_t) H * 4, s>>>(x, w, out, T, E, H);
+        return cudaGetLastError();
+    }
     dim3 grid((unsigned) ceil_div(E, 64), (unsigned) ceil_div(T, 64));
     logits_gemm_kernel<<<grid, 256, 0, s>>>(x, w, out, T, E, H);
     return cudaGetLastError();
