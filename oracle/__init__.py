@@ -107,8 +107,11 @@ def ref():
     if _ref is None:
         if not ref_available():
             return None
-        lib = C.CDLL(ref_path())
+        # global symbols: a ggml backend library loaded through ggml_backend_load resolves
+        # its ggml calls against this copy of ggml
+        lib = C.CDLL(ref_path(), mode=C.RTLD_GLOBAL)
         vp, i64, i32, f32, f64 = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_double
+        cp, ip = C.c_char_p, C.POINTER(C.c_int)
         lib.qref_set_threads.argtypes = [i32]
         lib.qref_quantize.restype = C.c_size_t
         lib.qref_quantize.argtypes = [i32, vp, vp, i64, i64]
@@ -123,6 +126,9 @@ def ref():
         lib.qref_moe_layer.restype = f64
         lib.qref_moe_layer.argtypes = [vp, i64, i64, vp, i64, i64, i32, vp, vp, i32, vp, i64, i64,
                                        vp, vp, vp, vp, vp, vp, i32, vp, f32]
+        lib.qref_backend_mul_mat_id.argtypes = [cp, i32, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, vp]
+        lib.qref_backend_get_rows.argtypes = [cp, i32, vp, i64, i64, vp, i64, vp]
+        lib.qref_backend_sched_mul_mat_id.argtypes = [cp, i32, vp, i64, i64, i64, vp, i64, vp, i64, f32, vp, ip, ip]
         _ref = lib
     return _ref
 
@@ -204,6 +210,46 @@ def get_rows(t: int, src: np.ndarray, ne0: int, nrows: int, idx: np.ndarray,
         return dst, ms
     rc = port().qo_get_rows(t, _p(src), ne0, nrows, _p(idx), idx.size, _p(dst))
     return dst, rc
+
+
+# ------------------------------------------------- a ggml backend loaded by ggml itself
+def backend_mul_mat_id(path: str, t: int, w: np.ndarray, K: int, M: int, n_as: int, b: np.ndarray,
+                       ids: np.ndarray, n_used: int | None = None):
+    """mul_mat_id computed by the ggml backend library at `path`, loaded with the
+    reference ggml's own ggml_backend_load and driven through ggml_backend_graph_compute.
+    ids [T, W]: the op uses its first n_used columns (a strided view when n_used < W).
+    Returns (dst [T, n_used, M], rc); rc 0 on success."""
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    T, n_b = b.shape[0], b.shape[1]
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    n_used = ids.shape[1] if n_used is None else n_used
+    dst = np.zeros((T, n_used, M), dtype=np.float32)
+    rc = ref().qref_backend_mul_mat_id(path.encode(), t, _p(w), K, M, n_as, _p(b), n_b, T, _p(ids), n_used,
+                                       ids.shape[1], _p(dst))
+    return dst, rc
+
+
+def backend_get_rows(path: str, t: int, src: np.ndarray, ne0: int, nrows: int, idx: np.ndarray):
+    """get_rows computed by the ggml backend library at `path`.  Returns (dst, rc)."""
+    idx = np.ascontiguousarray(idx, dtype=np.int32)
+    dst = np.zeros((idx.size, ne0), dtype=np.int32 if t == I32 else np.float32)
+    rc = ref().qref_backend_get_rows(path.encode(), t, _p(src), ne0, nrows, _p(idx), idx.size, _p(dst))
+    return dst, rc
+
+
+def backend_sched_mul_mat_id(path: str, t: int, w: np.ndarray, K: int, M: int, n_as: int, b: np.ndarray,
+                             ids: np.ndarray, scale: float):
+    """scale * mul_mat_id through ggml_backend_sched over [the backend at `path`, CPU], the
+    weights in the loaded backend's weight buffer.  Returns (dst, rc, n_splits,
+    mul_mat_id placed on the loaded backend)."""
+    b = np.ascontiguousarray(b, dtype=np.float32).reshape(b.shape[0], 1, K)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    T, n_used = ids.shape
+    dst = np.zeros((T, n_used, M), dtype=np.float32)
+    n_splits, on_backend = C.c_int(0), C.c_int(0)
+    rc = ref().qref_backend_sched_mul_mat_id(path.encode(), t, _p(w), K, M, n_as, _p(b), T, _p(ids), n_used,
+                                             scale, _p(dst), C.byref(n_splits), C.byref(on_backend))
+    return dst, rc, n_splits.value, bool(on_backend.value)
 
 
 def route(logits: np.ndarray, n_used: int, norm: bool = True, scale: float = 0.0,

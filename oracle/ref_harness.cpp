@@ -26,6 +26,8 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <map>
+#include <string>
 #include <vector>
 
 namespace {
@@ -277,6 +279,170 @@ double qref_moe_layer(const float * x, int64_t H, int64_t T,
     if (weights) ggml_backend_tensor_get(w, weights, 0, ggml_nbytes(w));
     if (act_out) ggml_backend_tensor_get(act, act_out, 0, ggml_nbytes(act));
     return ms;
+}
+
+// ------------------------------------------------------------------------------------
+// Drop-in checks: the same ggml graphs computed by a backend that ggml loads itself from
+// a shared library (ggml_backend_load, the path of ggml_backend_load_all()).  The tensors
+// are allocated in that backend's buffer type, exactly as a host application would.
+// Return 0 on success; -1 the library did not load, -2 it has no device, -3 the backend
+// did not initialise, -4 an allocation failed, -5 the graph failed to compute.
+
+static ggml_backend_reg_t load_backend_once(const char * path) {
+    static std::map<std::string, ggml_backend_reg_t> loaded;
+    auto it = loaded.find(path);
+    if (it != loaded.end()) return it->second;
+    ggml_backend_reg_t reg = ggml_backend_load(path);
+    loaded[path] = reg;
+    return reg;
+}
+
+static ggml_backend_t backend_open(const char * path, int * rc) {
+    ggml_backend_reg_t reg = load_backend_once(path);
+    if (!reg) { *rc = -1; return nullptr; }
+    if (ggml_backend_reg_dev_count(reg) == 0) { *rc = -2; return nullptr; }
+    ggml_backend_t be = ggml_backend_dev_init(ggml_backend_reg_dev_get(reg, 0), "workspace_mb=64");
+    *rc = be ? 0 : -3;
+    return be;
+}
+
+// Weights in one buffer marked as weights (the model loader marks expert buffers so,
+// core/model.cpp:244); everything else in a second buffer of the same backend.
+struct BackendGraph {
+    ggml_context * wctx = nullptr, * ctx = nullptr;
+    ggml_backend_buffer_t wbuf = nullptr, buf = nullptr;
+    ggml_cgraph * gf = nullptr;
+    BackendGraph() {
+        ggml_init_params wp = {ggml_tensor_overhead() * 4, nullptr, true};
+        wctx = ggml_init(wp);
+        ggml_init_params ip = {ggml_tensor_overhead() * 16 + ggml_graph_overhead(), nullptr, true};
+        ctx = ggml_init(ip);
+        gf = ggml_new_graph(ctx);
+    }
+    bool alloc(ggml_backend_t be) {
+        ggml_backend_buffer_type_t bt = ggml_backend_get_default_buffer_type(be);
+        wbuf = ggml_backend_alloc_ctx_tensors_from_buft(wctx, bt);
+        if (!wbuf) return false;
+        ggml_backend_buffer_set_usage(wbuf, GGML_BACKEND_BUFFER_USAGE_WEIGHTS);
+        buf = ggml_backend_alloc_ctx_tensors_from_buft(ctx, bt);
+        return buf != nullptr;
+    }
+    ~BackendGraph() {
+        if (buf) ggml_backend_buffer_free(buf);
+        if (wbuf) ggml_backend_buffer_free(wbuf);
+        ggml_free(ctx);
+        ggml_free(wctx);
+    }
+};
+
+// qref_mul_mat_id computed by the backend in `path`.
+int qref_backend_mul_mat_id(const char * path, int type, const void * as, int64_t K, int64_t M, int64_t n_as,
+                            const float * b, int64_t n_b, int64_t T, const int32_t * ids, int64_t n_used,
+                            int64_t ids_stride, float * dst) {
+    int rc = 0;
+    ggml_backend_t be = backend_open(path, &rc);
+    if (!be) return rc;
+    {
+        BackendGraph g;
+        ggml_tensor * tas  = ggml_new_tensor_3d(g.wctx, (ggml_type) type, K, M, n_as);
+        ggml_tensor * tb   = ggml_new_tensor_3d(g.ctx, GGML_TYPE_F32, K, n_b, T);
+        ggml_tensor * tidf = ggml_new_tensor_2d(g.ctx, GGML_TYPE_I32, ids_stride, T);
+        ggml_tensor * tid  = ggml_view_2d(g.ctx, tidf, n_used, T, tidf->nb[1], 0);
+        ggml_tensor * out  = ggml_mul_mat_id(g.ctx, tas, tb, tid);
+        ggml_build_forward_expand(g.gf, out);
+        if (!g.alloc(be)) {
+            rc = -4;
+        } else {
+            ggml_backend_tensor_set(tas, as, 0, ggml_nbytes(tas));
+            ggml_backend_tensor_set(tb, b, 0, ggml_nbytes(tb));
+            ggml_backend_tensor_set(tidf, ids, 0, ggml_nbytes(tidf));
+            if (ggml_backend_graph_compute(be, g.gf) != GGML_STATUS_SUCCESS) rc = -5;
+            else ggml_backend_tensor_get(out, dst, 0, ggml_nbytes(out));
+        }
+    }
+    ggml_backend_free(be);
+    return rc;
+}
+
+// qref_get_rows computed by the backend in `path`.
+int qref_backend_get_rows(const char * path, int type, const void * src, int64_t ne0, int64_t nrows,
+                          const int32_t * idx, int64_t n, void * dst) {
+    int rc = 0;
+    ggml_backend_t be = backend_open(path, &rc);
+    if (!be) return rc;
+    {
+        BackendGraph g;
+        ggml_tensor * ts = ggml_new_tensor_2d(g.wctx, (ggml_type) type, ne0, nrows);
+        ggml_tensor * ti = ggml_new_tensor_1d(g.ctx, GGML_TYPE_I32, n);
+        ggml_tensor * out = ggml_get_rows(g.ctx, ts, ti);
+        ggml_build_forward_expand(g.gf, out);
+        if (!g.alloc(be)) {
+            rc = -4;
+        } else {
+            ggml_backend_tensor_set(ts, src, 0, ggml_nbytes(ts));
+            ggml_backend_tensor_set(ti, idx, 0, ggml_nbytes(ti));
+            if (ggml_backend_graph_compute(be, g.gf) != GGML_STATUS_SUCCESS) rc = -5;
+            else ggml_backend_tensor_get(out, dst, 0, ggml_nbytes(out));
+        }
+    }
+    ggml_backend_free(be);
+    return rc;
+}
+
+// scale * mul_mat_id(as, b, ids) through ggml_backend_sched over [backend in `path`, CPU]:
+// the weights sit in the loaded backend's weight buffer, b and ids are CPU inputs, and
+// the scale is an op the loaded backend does not implement.  Reports the number of
+// splits and whether the scheduler put MUL_MAT_ID on the loaded backend.
+int qref_backend_sched_mul_mat_id(const char * path, int type, const void * as, int64_t K, int64_t M,
+                                  int64_t n_as, const float * b, int64_t T, const int32_t * ids, int64_t n_used,
+                                  float scale, float * dst, int * n_splits, int * mmid_on_backend) {
+    int rc = 0;
+    ggml_backend_t be = backend_open(path, &rc);
+    if (!be) return rc;
+    ggml_backend_t cb = ggml_backend_cpu_init();
+    ggml_init_params wp = {ggml_tensor_overhead() * 2, nullptr, true};
+    ggml_context * wctx = ggml_init(wp);
+    ggml_tensor * ta = ggml_new_tensor_3d(wctx, (ggml_type) type, K, M, n_as);
+    ggml_backend_buffer_t wbuf = ggml_backend_alloc_ctx_tensors_from_buft(wctx, ggml_backend_get_default_buffer_type(be));
+    ggml_context * ctx = nullptr;
+    ggml_backend_sched_t sched = nullptr;
+    if (!wbuf) {
+        rc = -4;
+    } else {
+        ggml_backend_buffer_set_usage(wbuf, GGML_BACKEND_BUFFER_USAGE_WEIGHTS);
+        ggml_backend_tensor_set(ta, as, 0, ggml_nbytes(ta));
+        ggml_init_params ip = {ggml_tensor_overhead() * 16 + ggml_graph_overhead(), nullptr, true};
+        ctx = ggml_init(ip);
+        ggml_tensor * tb = ggml_new_tensor_3d(ctx, GGML_TYPE_F32, K, 1, T);
+        ggml_tensor * tids = ggml_new_tensor_2d(ctx, GGML_TYPE_I32, n_used, T);
+        ggml_set_input(tb);
+        ggml_set_input(tids);
+        ggml_tensor * y = ggml_mul_mat_id(ctx, ta, tb, tids);
+        ggml_tensor * z = ggml_scale(ctx, y, scale);
+        ggml_set_output(z);
+        ggml_cgraph * gf = ggml_new_graph(ctx);
+        ggml_build_forward_expand(gf, z);
+        ggml_backend_t bes[2] = {be, cb};
+        sched = ggml_backend_sched_new(bes, nullptr, 2, GGML_DEFAULT_GRAPH_SIZE, false, true);
+        if (!ggml_backend_sched_alloc_graph(sched, gf)) {
+            rc = -4;
+        } else {
+            ggml_backend_tensor_set(tb, b, 0, ggml_nbytes(tb));
+            ggml_backend_tensor_set(tids, ids, 0, ggml_nbytes(tids));
+            if (ggml_backend_sched_graph_compute(sched, gf) != GGML_STATUS_SUCCESS) rc = -5;
+            ggml_backend_sched_synchronize(sched);
+            *n_splits = ggml_backend_sched_get_n_splits(sched);
+            *mmid_on_backend = ggml_backend_sched_get_tensor_backend(sched, y) == be;
+            if (rc == 0) ggml_backend_tensor_get(z, dst, 0, ggml_nbytes(z));
+        }
+    }
+    if (sched) ggml_backend_sched_free(sched);
+    if (ctx) ggml_free(ctx);
+    if (wbuf) ggml_backend_buffer_free(wbuf);
+    ggml_free(wctx);
+    ggml_backend_free(cb);
+    ggml_backend_free(be);
+    return rc;
 }
 
 }  // extern "C"
