@@ -16,6 +16,9 @@
 //   * in-graph slot remap  runtime.cpp:2769-2778  get_rows(g2s I32 table, selected)
 // Ops exercised: ggml_mul_mat_id (ggml.c:3413), ggml_get_rows (ggml.c:3975),
 // ggml_argsort_top_k (ggml.c:5462), ggml_swiglu_split (ggml.c:3082).
+// The qref_backend_* drivers run MUL_MAT_ID / GET_ROWS graphs on a ggml backend that this
+// ggml loads from a shared library (ggml_backend_load), directly and through
+// ggml_backend_sched, so the tests check a backend library as a host application uses it.
 #include "ggml.h"
 #include "ggml-alloc.h"
 #include "ggml-backend.h"
