@@ -273,6 +273,7 @@ QWB_API qwb_status qwb_moe_ep_experts(const qwb_moe_ep_experts_desc *desc, void 
 #define QWB_KERNEL_DOWN 3
 #define QWB_KERNEL_OTHER 4
 #define QWB_KERNEL_GROUPED_GEMM 5 /* tensor-core grouped expert GEMM (many tokens per expert) */
+#define QWB_KERNEL_EXPERT_GEMV 6  /* bandwidth-bound expert GEMV of qwb_mul_mat_id (few tokens per expert) */
 QWB_API qwb_status qwb_profile_enable(int max_marks); /* creates the events; 0 disables */
 QWB_API qwb_status qwb_profile_reset(void);           /* next mark is mark 0 */
 QWB_API int qwb_profile_count(void);                  /* marks recorded since reset */

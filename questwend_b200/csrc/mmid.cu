@@ -52,6 +52,7 @@ __global__ void __launch_bounds__(1024) mmid_index_kernel(const int32_t *__restr
             to += (cnt[e] + NT - 1) / NT;
         }
         *ix.n_tiles = to;
+        *ix.work = 0;
     }
     __syncthreads();
     for (int p = tid; p < P; p += nth) {
@@ -312,6 +313,7 @@ MmidIndex mmid_index_at(void *base, int64_t P, int64_t n_as, int NT) {
     MmidIndex ix;
     char *c = (char *) base;
     ix.n_tiles = (int *) c;
+    ix.work = ix.n_tiles + 1;
     c += 256;
     ix.pairs = (int *) c;
     c += align_up((size_t) P * 4, 256);
@@ -345,6 +347,7 @@ struct MmidPlan {
     int64_t K, M, n_as, n_b, T, n_used, P;
     int NT;
     bool pf;  // tensor-core grouped GEMM (many tokens per expert)
+    bool stream;  // weight-streaming kernel (one tile per expert)
     size_t planes, index, btiles, da, total;
 };
 
@@ -372,7 +375,8 @@ qwb_status plan_mmid(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor
     p.P = p.n_used * p.T;
     if (p.P > (1 << 24) || p.n_as > 16384 || p.K > (1 << 20) || p.M > (1 << 30)) return QWB_ERR_LIMIT;
     p.pf = allow_prefill && pf_eligible(p.type, p.K, p.M, p.P, p.n_as);
-    p.NT = p.pf ? kPfTileN : pick_nt(p.P, p.n_as);
+    p.stream = !p.pf && stream_fits(p.type, p.K, as->nb[1], as->nb[1], false);
+    p.NT = p.pf ? kPfTileN : p.stream ? (int) std::max<int64_t>(1, p.P) : pick_nt(p.P, p.n_as);
     p.planes = planes_bytes(p.n_b * p.T, p.K, p.vdt == QWB_TYPE_Q8_K);
     p.index = mmid_index_bytes(p.P, p.n_as, p.NT);
     p.btiles = p.da = 0;
@@ -466,6 +470,7 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
         profile_mark(s, QWB_KERNEL_GROUPED_GEMM);
         return e == cudaSuccess ? QWB_OK : QWB_ERR_CUDA;
     }
+    profile_mark(s, QWB_KERNEL_OTHER);
     GemvArgs a{};
     a.W = (const uint8_t *) as->data;
     a.nb1 = as->nb[1];
@@ -485,8 +490,17 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
     a.n_ids = p.n_as;
     a.n_slots = p.n_as;
     a.st = st;
-    gemv_geometry(a, p.NT, false);
-    e = launch_gemv(p.type, false, a, p.NT, ix.max_tiles, s);
+    if (p.stream) {
+        // experts with several tokens cost more than their bytes: balance dynamically
+        a.chunks_per_cta = 2 * p.P > 3 * std::min(p.P, p.n_as) ? 4 : 1;
+        a.work = ix.work;
+        if (!stream_geometry(a, p.type, false)) return QWB_ERR_LAYOUT;
+        e = launch_stream(p.type, false, a, s);
+    } else {
+        gemv_geometry(a, p.NT, false);
+        e = launch_gemv(p.type, false, a, p.NT, ix.max_tiles, s);
+    }
+    profile_mark(s, QWB_KERNEL_EXPERT_GEMV);
     return e == cudaSuccess ? QWB_OK : QWB_ERR_CUDA;
 }
 

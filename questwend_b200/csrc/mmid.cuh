@@ -8,6 +8,8 @@ namespace qwb {
 // Expert-sorted work description written by the index kernel into the workspace.
 struct MmidIndex {
     int *n_tiles;  // device scalar
+    int *work;     // device scalar next to n_tiles: chunk counter of the streaming kernel,
+                   // zeroed by the index kernel
     int *pairs;    // [P] pair ids p = t*n_used + j, grouped by expert
     int4 *tiles;   // [max_tiles] (expert, first pair, pair count, 0)
     int max_tiles; // host-side upper bound
@@ -29,6 +31,12 @@ struct GemvArgs {
     float *dst;              // dst[m, j, t] at dst + j*dnb1 + t*dnb2 (bytes) + 4m
     size_t dnb1, dnb2;
     int R, n_rb, wstage, stage_bytes;
+    // streaming kernel geometry (stream_geometry): lanes per row, rows per stage, slot
+    // bytes, ring slots, consumer warps, ring offset in shared memory, units per lane group
+    int lpr, rpw, slot, nslot, nwarps, ring_off, upg;
+    int tg, act_off;     // activation rows staged per pass, their shared-memory offset
+    int chunks_per_cta;  // > 1: rows are handed out in chunks from *work (load balance)
+    int *work;
     // optional expert -> slot remap (the in-graph get_rows of an I32 [1, E] table,
     // core/runtime.cpp:2769-2778); slot ids must lie in [0, n_slots)
     const int32_t *remap, *remap2;
@@ -40,6 +48,12 @@ struct GemvArgs {
 void gemv_geometry(GemvArgs &a, int NT, bool glu);
 cudaError_t launch_gemv(int type, bool glu, GemvArgs a, int NT, int max_tiles, cudaStream_t s);
 int pick_nt(int64_t pairs, int64_t n_as);
+// Weight-streaming MUL_MAT_ID kernel (mmid_stream.cu): one tile per used expert (index
+// built with NT >= pairs), every selected expert row read once.  stream_fits is false
+// when the rows are too long for its shared-memory stages.
+bool stream_fits(int type, int64_t K, size_t nb1, size_t nb1_2, bool glu);
+bool stream_geometry(GemvArgs &a, int type, bool glu);
+cudaError_t launch_stream(int type, bool glu, const GemvArgs &a, cudaStream_t s);
 int64_t mmid_max_tiles(int64_t P, int64_t n_as, int NT);
 size_t mmid_index_bytes(int64_t P, int64_t n_as, int NT);
 MmidIndex mmid_index_at(void *base, int64_t P, int64_t n_as, int NT);

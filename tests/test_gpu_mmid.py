@@ -51,6 +51,13 @@ CASES = [
     (O.Q6_K, 1024, 128, 8, 33, 4, 4),
     (O.Q8_0, 512, 96, 8, 64, 8, 8),
     (O.Q4_K, 768, 2048, 8, 64, 8, 8),
+    # weight-streaming kernel edges
+    (O.Q6_K, 768, 2048, 4, 40, 2, 1),      # 20 tokens per expert: three token passes
+    (O.Q8_0, 2048, 300, 16, 7, 4, 2),      # rows not a multiple of the stage rows
+    (O.Q8_0, 96, 40, 3, 5, 2, 1),          # 3 blocks per row: a partial lane group
+    (O.Q4_K, 256, 33, 5, 3, 5, 1),         # one superblock per row: 32 rows per stage
+    (O.Q4_K, 256, 8, 2, 1, 2, 1),          # 16 rows in total: most CTAs idle
+    (O.Q4_K, 16384, 64, 4, 2, 2, 1),       # long rows: fewer consumer warps
 ]
 
 
