@@ -33,10 +33,18 @@ qwb_mul_mat_id call (activation quantisation, expert sort, B-tile gather, GEMM),
 for the tensor-core kernel alone (event marks around it).  The weights of all 128 experts
 (453 MB per matrix) exceed L2.  Its `roofline` compares the GEMM kernel with the measured
 dense bf16 peak; its `cpu_baseline` times the reference CPU backend on T = 512, gate shape.
+
+`decode_mmid` (rank 0): BASELINE config 4's expert shape (hidden 4096 -> expert FFN 1536,
+128 Q4_K experts, top-8) as a decode-batch MUL_MAT_ID at T = 1, 8, 64 tokens, the path a
+ggml backend takes for a decode graph's MUL_MAT_ID nodes (weight streaming: each selected
+expert row read once for all its tokens).  GB/s counts the distinct expert weights per
+call; `frac` is against the measured HBM copy bandwidth, for the whole call (`us`) and for
+the streaming kernel alone (`kernel_us`).
 """
 from __future__ import annotations
 
 import argparse
+import functools
 import json
 import os
 import subprocess
@@ -204,6 +212,7 @@ def zipf_ids(T, n_exp, n_used, seed, s=1.1):
     return np.argsort(-logits, axis=1, kind="stable")[:, :n_used].astype(np.int32)
 
 
+@functools.lru_cache(maxsize=1)
 def prefill_experts(seed=7):
     """PF_UNIQUE distinct Q4_K experts for the gate/up shape [PF_H -> PF_F] and the down
     shape [PF_F -> PF_H]: N(0, 0.02) weights quantized with the reference quantizer."""
@@ -221,6 +230,92 @@ def prefill_experts(seed=7):
     with cf.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as ex:
         out = list(ex.map(one, [(r, i) for r in range(2) for i in range(PF_UNIQUE)]))
     return [np.concatenate(out[r * PF_UNIQUE:(r + 1) * PF_UNIQUE]) for r in range(2)]
+
+
+MMID_TOKENS = (1, 8, 64)  # BASELINE config 4 decode batches
+
+
+def decode_mmid_sweep(q, lib, dev):
+    """Decode-batch MUL_MAT_ID (BASELINE config 4 shape: hidden 4096 -> expert FFN 1536,
+    128 Q4_K experts, top-8 of uniform random routing) at T = 1, 8, 64 tokens: the
+    weight-streaming path qwb_mul_mat_id takes for few tokens per expert.  Timed from CUDA
+    graph replays of 8 calls; call i reads pool i of 8 identical expert pools, so the
+    bytes touched between two reads of a pool exceed L2 (and the calls are not L2 hits).
+    GB/s counts the distinct expert weights a call streams (experts touched x 3.54 MB)."""
+    import ctypes as C
+
+    import torch
+
+    from questwend_b200 import _lib as L
+    experts = prefill_experts()[0]  # gate/up shape [PF_H -> PF_F], PF_UNIQUE distinct matrices
+    reps = E // PF_UNIQUE
+    per = experts.size // PF_UNIQUE
+    base = torch.from_numpy(experts).to(dev)
+    n_pools, n_call = 8, 8
+    pools = []
+    for _ in range(n_pools):
+        buf = torch.empty(base.numel() * reps, dtype=torch.uint8, device=dev)
+        buf.view(reps, -1).copy_(base.expand(reps, -1))
+        pools.append(q.QTensor(buf, Q4_K, (PF_H, PF_F, E, 1)))
+    hbm, kind = peaks()
+    rng = np.random.default_rng(11)
+    s = torch.cuda.Stream()
+    points = []
+    for T in MMID_TOKENS:
+        ids_np = np.stack([rng.permutation(E)[:K_USED] for _ in range(T)]).astype(np.int32)
+        ids = torch.from_numpy(ids_np).to(dev)
+        b = torch.randn((T, 1, PF_H), device=dev)
+        out = torch.empty((T, K_USED, PF_F), device=dev)
+        for i in range(3):
+            q.mul_mat_id(pools[i], b, ids, out)
+        torch.cuda.synchronize()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+            for i in range(n_call):
+                q.mul_mat_id(pools[i % n_pools], b, ids, out)
+        # per-kernel marks: a one-call graph with event records around the kernels
+        L.check("qwb_profile_enable", lib.qwb_profile_enable(8))
+        g1 = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s), torch.cuda.graph(g1, stream=s):
+            lib.qwb_profile_reset()
+            q.mul_mat_id(pools[0], b, ids, out)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        calls, kern = [], []
+        for _ in range(10):
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            calls.append(e0.elapsed_time(e1) / n_call)
+            for p_ in pools[1:4]:  # evict pool 0 before the marked call
+                p_.data[: 64 << 20].add_(0)
+            g1.replay()
+            torch.cuda.synchronize()
+            n = lib.qwb_profile_count() - 1
+            ms = (C.c_float * max(n, 1))()
+            tg = (C.c_int32 * max(n, 1))()
+            L.check("qwb_profile_read", lib.qwb_profile_read(ms, tg, n))
+            kern.append(sum(m for m, t in zip(ms[:n], tg[:n]) if t == 6))
+        L.check("qwb_profile_enable", lib.qwb_profile_enable(0))
+        del g, g1
+        assert torch.isfinite(out).all()
+        wbytes = len(np.unique(ids_np)) * per
+        c_ms, k_ms = float(np.median(calls)), float(np.median(kern))
+        points.append({"tokens": T, "experts_touched": int(len(np.unique(ids_np))), "weight_mb": wbytes / 1e6,
+                       "us": 1e3 * c_ms, "gbs": wbytes / (c_ms * 1e-3) / 1e9, "frac": wbytes / (c_ms * 1e-3) / 1e9 / hbm,
+                       "kernel_us": 1e3 * k_ms,
+                       "kernel_gbs": wbytes / (k_ms * 1e-3) / 1e9 if k_ms > 0 else None,
+                       "kernel_frac": wbytes / (k_ms * 1e-3) / 1e9 / hbm if k_ms > 0 else None})
+    del pools
+    torch.cuda.empty_cache()
+    return {"config": {"workload": "C4 decode-batch MUL_MAT_ID, Q4_K x Q8_K, weight streaming", "hidden": PF_H,
+                       "expert_ffn": PF_F, "experts": E, "top_k": K_USED, "routing": "uniform random",
+                       "tokens": list(MMID_TOKENS), "l2": "8 pools of all 128 experts, call i reads pool i"},
+            "peak": hbm, "peak_kind": kind, "points": points}
 
 
 def prefill_sweep(q, lib, dev, warmup, iters, cpu):
@@ -428,6 +523,7 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="MoE layers per step (default 48; fewer only for profiling captures)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (config 3) sweep")
+    ap.add_argument("--no-mmid", action="store_true", help="skip the decode-batch MUL_MAT_ID (config 4) sweep")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -612,6 +708,8 @@ def main():
     del graph, pgraph
     if rank == 0 and not args.no_prefill:
         result["prefill"] = prefill_sweep(q, lib, dev, args.warmup, 10, cpu=(world == 1 and not args.no_cpu))
+    if rank == 0 and not args.no_mmid:
+        result["decode_mmid"] = decode_mmid_sweep(q, lib, dev)
     if rank == 0:
         print(json.dumps(result))
     if world > 1:

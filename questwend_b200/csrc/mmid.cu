@@ -29,6 +29,9 @@ __global__ void __launch_bounds__(1024) mmid_index_kernel(const int32_t *__restr
                                                           int64_t ids_s1, int n_used, int T, int n_as, int NT,
                                                           MmidIndex ix, float *dst, size_t dnb1, size_t dnb2,
                                                           int64_t M, qwb_status_block *st, int skip_neg) {
+    // a kernel launched after this one with programmatic dependent launch may start its
+    // prologue now; it reads this kernel's output only after griddepcontrol.wait
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     extern __shared__ int sh[];
     int *cnt = sh;              // [n_as]
     int *off = sh + n_as;       // [n_as] pair offset, later running cursor
@@ -43,16 +46,61 @@ __global__ void __launch_bounds__(1024) mmid_index_kernel(const int32_t *__restr
         if (e >= 0 && e < n_as) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
-    if (tid == 0) {  // serial scan over experts (n_as <= a few thousand)
-        int po = 0, to = 0;
-        for (int e = 0; e < n_as; ++e) {
+    {
+        // exclusive prefix sums of the pair and tile counts over experts: each thread
+        // scans its own contiguous range of experts, then the per-thread totals are
+        // scanned across the block (warp shuffles + one value per warp)
+        __shared__ int wsum_p[32], wsum_t[32];
+        const int per = (n_as + nth - 1) / nth;
+        const int e0 = min(n_as, tid * per), e1 = min(n_as, e0 + per);
+        int sp = 0, st_ = 0;
+        for (int e = e0; e < e1; ++e) {
+            sp += cnt[e];
+            st_ += (cnt[e] + NT - 1) / NT;
+        }
+        const int lane = tid & 31, wid = tid >> 5;
+        int ip = sp, it = st_;  // inclusive scan within the warp
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int xp = __shfl_up_sync(0xffffffffu, ip, o), xt = __shfl_up_sync(0xffffffffu, it, o);
+            if (lane >= o) {
+                ip += xp;
+                it += xt;
+            }
+        }
+        if (lane == 31) {
+            wsum_p[wid] = ip;
+            wsum_t[wid] = it;
+        }
+        __syncthreads();
+        if (wid == 0) {
+            const int nw = (nth + 31) >> 5;
+            int vp = lane < nw ? wsum_p[lane] : 0, vt = lane < nw ? wsum_t[lane] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int xp = __shfl_up_sync(0xffffffffu, vp, o), xt = __shfl_up_sync(0xffffffffu, vt, o);
+                if (lane >= o) {
+                    vp += xp;
+                    vt += xt;
+                }
+            }
+            if (lane < nw) {
+                wsum_p[lane] = vp;  // inclusive totals per warp
+                wsum_t[lane] = vt;
+            }
+            if (lane == nw - 1) {
+                *ix.n_tiles = vt;
+                *ix.work = 0;
+            }
+        }
+        __syncthreads();
+        int po = ip - sp + (wid ? wsum_p[wid - 1] : 0), to = it - st_ + (wid ? wsum_t[wid - 1] : 0);
+        for (int e = e0; e < e1; ++e) {
             off[e] = po;
             toff[e] = to;
             po += cnt[e];
             to += (cnt[e] + NT - 1) / NT;
         }
-        *ix.n_tiles = to;
-        *ix.work = 0;
     }
     __syncthreads();
     for (int p = tid; p < P; p += nth) {

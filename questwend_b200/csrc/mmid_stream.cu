@@ -75,6 +75,27 @@ __device__ __forceinline__ void mbar_arrive_relaxed(uint64_t *bar) {
     asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Weight rows are read exactly once: copy them with an L2 evict-first policy so they do
+// not displace the activations, the expert index and the kernel's code from L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void bulk_span_issue_ef(void *dst, const void *src, size_t bytes, uint64_t *bar,
+                                                   uint64_t pol) {
+    const uintptr_t a = (uintptr_t) src & ~(uintptr_t) 15;
+    const uint32_t total = bulk_span_bytes(src, bytes);
+    for (uint32_t off = 0; off < total; off += 65536u) {
+        const uint32_t n = total - off < 65536u ? total - off : 65536u;
+        asm volatile(
+            "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+                smem_u32((char *) dst + off)),
+            "l"((const void *) (a + off)), "r"(n), "r"(smem_u32(bar)), "l"(pol)
+            : "memory");
+    }
+}
+
 // Bounded wait that also gives up as soon as another warp has aborted the CTA.
 __device__ __forceinline__ bool stream_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
     if (mbar_try_wait_fast(bar, parity)) return true;
@@ -98,6 +119,12 @@ template <int TYPE, bool GLU, int NT>
 __device__ __noinline__ void stream_pass(const uint8_t *row1, const uint8_t *row2, const ActStage &A, int ng,
                                             bool live, bool bad, int LPR, int sl, int n_sb, int units, int UPG,
                                             bool row_ok, const long long *tok_o, float *dst, int row) {
+    // every pointer below is into this CTA's shared memory: let the compiler use shared
+    // loads (this function is not inlined, so it cannot see where they come from)
+    __builtin_assume(__isShared(row1));
+    if (GLU) __builtin_assume(__isShared(row2));
+    __builtin_assume(__isShared(A.base));
+    __builtin_assume(__isShared(tok_o));
     float acc[NT], acc2[NT];
 #pragma unroll
     for (int k = 0; k < NT; ++k) {
@@ -159,6 +186,9 @@ __global__ void __launch_bounds__(32 * (kStreamMaxWarps + 1), 1) mmid_stream_ker
         *abort_flag = 0;
     }
     __syncthreads();  // barriers are CTA-local: the block barrier publishes their init
+    // launched with programmatic dependent launch: everything above overlapped the index
+    // kernel; its output (and the quantized activations before it) is read only below
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (tid == 0) ST_TRACE(1);
     const int64_t total = (int64_t) (*a.n_tiles) * a.M;
@@ -169,6 +199,7 @@ __global__ void __launch_bounds__(32 * (kStreamMaxWarps + 1), 1) mmid_stream_ker
     if (warp == NWC) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
             const int64_t n_chunks = (int64_t) gridDim.x * a.chunks_per_cta;
             const int64_t CH = align_up((size_t) ceil_div(max(total, (int64_t) 1), n_chunks), (size_t) SR);
             int64_t chunk = blockIdx.x;
@@ -231,8 +262,8 @@ __global__ void __launch_bounds__(32 * (kStreamMaxWarps + 1), 1) mmid_stream_ker
                 mbar_arrive_expect_tx(&full[slot], bytes);
                 if (bytes) {
                     uint8_t *dst = ring + (size_t) slot * a.slot;
-                    bulk_span_issue(dst, src1, span1, &full[slot]);
-                    if (GLU) bulk_span_issue(dst + half, src2, span2, &full[slot]);
+                    bulk_span_issue_ef(dst, src1, span1, &full[slot], pol);
+                    if (GLU) bulk_span_issue_ef(dst + half, src2, span2, &full[slot], pol);
                 }
                 issued = s + 1;
                 if (s < 6) ST_TRACE(3 + s);
@@ -313,11 +344,13 @@ __global__ void __launch_bounds__(32 * (kStreamMaxWarps + 1), 1) mmid_stream_ker
                 }
                 // one pass over the staged tokens, instantiated for the pass width
                 const bool live = row_ok && !d.bad;
+                if (s == 1 && g0 == 0 && warp == 0 && lane == 0) ST_TRACE(28);
                 if (ng == 1) stream_pass<TYPE, GLU, 1>(row1, row2, A, ng, live, d.bad, LPR, sl, n_sb, units, UPG, row_ok, tok_o, a.dst, d.r0 + rr);
                 else if (ng == 2) stream_pass<TYPE, GLU, 2>(row1, row2, A, ng, live, d.bad, LPR, sl, n_sb, units, UPG, row_ok, tok_o, a.dst, d.r0 + rr);
                 else if (ng <= 4) stream_pass<TYPE, GLU, 4>(row1, row2, A, ng, live, d.bad, LPR, sl, n_sb, units, UPG, row_ok, tok_o, a.dst, d.r0 + rr);
                 else stream_pass<TYPE, GLU, 8>(row1, row2, A, ng, live, d.bad, LPR, sl, n_sb, units, UPG, row_ok, tok_o, a.dst, d.r0 + rr);
                 if (s == 0 && g0 == 0 && warp == 0 && lane == 0) ST_TRACE(23);
+                if (s == 1 && g0 == 0 && warp == 0 && lane == 0) ST_TRACE(29);
             }
             if (d.bad && d.r0 == 0 && warp == 0 && lane == 0) report(a.st, QWB_DEVERR_ID_RANGE, t.x);
             __syncwarp();
@@ -347,8 +380,17 @@ cudaError_t launch_stream_t(const GemvArgs &a, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured = smem;
     }
-    kern<<<num_sms(), 32 * (a.nwarps + 1), smem, s>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_sms());
+    cfg.blockDim = dim3(32 * (a.nwarps + 1));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 }  // namespace
