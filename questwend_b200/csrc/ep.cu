@@ -126,6 +126,7 @@ qwb_status plan_prep(const qwb_moe_ep_prepare_desc *d, PrepPlan &p) {
 struct ExpPlan {
     bool kq_gu, kq_d;
     int NT;
+    bool stream;  // expert GEMVs on the streaming kernel (index: one tile per expert)
     int64_t P, n_local;
     size_t off_xq, off_lid, off_index, off_act, off_actq, off_ex, total;
 };
@@ -144,7 +145,8 @@ qwb_status plan_exp(const qwb_moe_ep_experts_desc *d, ExpPlan &p) {
     p.kq_gu = tg != QWB_TYPE_Q8_0;
     p.kq_d = td != QWB_TYPE_Q8_0;
     p.P = d->n_used * d->T;
-    p.NT = pick_nt(std::max<int64_t>(1, p.P * p.n_local / d->E), p.n_local);
+    p.stream = stream_fits_ffn(tg, d->H, d->gate.nb[1], d->up.nb[1], td, d->F, d->down.nb[1]);
+    p.NT = p.stream ? (int) std::max<int64_t>(1, p.P) : pick_nt(std::max<int64_t>(1, p.P * p.n_local / d->E), p.n_local);
     size_t o = kCtrlBytes;
     p.off_xq = o; o += planes_bytes(d->T, d->H, p.kq_gu);
     p.off_lid = o; o += align_up((size_t) p.P * 4, 256);
@@ -273,8 +275,7 @@ extern "C" QWB_API qwb_status qwb_moe_ep_experts(const qwb_moe_ep_experts_desc *
         a.dst = act; a.dnb1 = (size_t) F * 4; a.dnb2 = (size_t) K * F * 4;
         a.n_ids = NL; a.n_slots = NL;
         a.st = st;
-        gemv_geometry(a, p.NT, true);
-        e = launch_gemv(d->gate.type, true, a, p.NT, ix.max_tiles, s);
+        e = launch_expert_gemv(d->gate.type, true, a, p.stream, p.NT, ix.max_tiles, P, NL, ix.work, s);
         if (e != cudaSuccess) return QWB_ERR_CUDA;
         profile_mark(s, QWB_KERNEL_GATE_UP);
     }
@@ -292,8 +293,7 @@ extern "C" QWB_API qwb_status qwb_moe_ep_experts(const qwb_moe_ep_experts_desc *
         a.dst = ex; a.dnb1 = (size_t) H * 4; a.dnb2 = (size_t) K * H * 4;
         a.n_ids = NL; a.n_slots = NL;
         a.st = st;
-        gemv_geometry(a, p.NT, false);
-        e = launch_gemv(d->down.type, false, a, p.NT, ix.max_tiles, s);
+        e = launch_expert_gemv(d->down.type, false, a, p.stream, p.NT, ix.max_tiles, P, NL, ix.work + 1, s);
         if (e != cudaSuccess) return QWB_ERR_CUDA;
         profile_mark(s, QWB_KERNEL_DOWN);
     }

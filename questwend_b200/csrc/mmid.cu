@@ -88,10 +88,8 @@ __global__ void __launch_bounds__(1024) mmid_index_kernel(const int32_t *__restr
                 wsum_p[lane] = vp;  // inclusive totals per warp
                 wsum_t[lane] = vt;
             }
-            if (lane == nw - 1) {
-                *ix.n_tiles = vt;
-                *ix.work = 0;
-            }
+            if (lane == nw - 1) *ix.n_tiles = vt;
+            if (lane < kIndexCounters) ix.work[lane] = 0;
         }
         __syncthreads();
         int po = ip - sp + (wid ? wsum_p[wid - 1] : 0), to = it - st_ + (wid ? wsum_t[wid - 1] : 0);

@@ -6,10 +6,13 @@
 namespace qwb {
 
 // Expert-sorted work description written by the index kernel into the workspace.
+constexpr int kIndexCounters = 4;
+
 struct MmidIndex {
     int *n_tiles;  // device scalar
-    int *work;     // device scalar next to n_tiles: chunk counter of the streaming kernel,
-                   // zeroed by the index kernel
+    int *work;     // [kIndexCounters] device counters next to n_tiles, zeroed by the index
+                   // kernel: chunk counters of the streaming kernels run on this index (one
+                   // per kernel: gate/up uses work[0], down work[1])
     int *pairs;    // [P] pair ids p = t*n_used + j, grouped by expert
     int4 *tiles;   // [max_tiles] (expert, first pair, pair count, 0)
     int max_tiles; // host-side upper bound
@@ -54,6 +57,12 @@ int pick_nt(int64_t pairs, int64_t n_as);
 bool stream_fits(int type, int64_t K, size_t nb1, size_t nb1_2, bool glu);
 bool stream_geometry(GemvArgs &a, int type, bool glu);
 cudaError_t launch_stream(int type, bool glu, const GemvArgs &a, cudaStream_t s);
+// An expert FFN (gate/up GLU GEMV, then down GEMV) can use the streaming kernel for both.
+bool stream_fits_ffn(int type_gu, int64_t H, size_t nb_g, size_t nb_u, int type_d, int64_t F, size_t nb_d);
+// Expert GEMV over the index's tiles: the streaming kernel when `stream` (index built with
+// one tile per expert), else the staged GEMV with tiles of <= NT pairs.
+cudaError_t launch_expert_gemv(int type, bool glu, GemvArgs a, bool stream, int NT, int max_tiles, int64_t pairs,
+                               int64_t n_experts, int *work, cudaStream_t s);
 int64_t mmid_max_tiles(int64_t P, int64_t n_as, int NT);
 size_t mmid_index_bytes(int64_t P, int64_t n_as, int NT);
 MmidIndex mmid_index_at(void *base, int64_t P, int64_t n_as, int NT);

@@ -455,6 +455,24 @@ bool stream_fits(int type, int64_t K, size_t nb1, size_t nb1_2, bool glu) {
     return stream_geometry(a, type, glu);
 }
 
+bool stream_fits_ffn(int type_gu, int64_t H, size_t nb_g, size_t nb_u, int type_d, int64_t F, size_t nb_d) {
+    // the Q6_K gate/up (GLU) variant does not fit the register budget: staged GEMV there
+    return type_gu != QWB_TYPE_Q6_K && stream_fits(type_gu, H, nb_g, nb_u, true) &&
+           stream_fits(type_d, F, nb_d, nb_d, false);
+}
+
+cudaError_t launch_expert_gemv(int type, bool glu, GemvArgs a, bool stream, int NT, int max_tiles, int64_t pairs,
+                               int64_t n_experts, int *work, cudaStream_t s) {
+    if (stream) {
+        a.chunks_per_cta = 2 * pairs > 3 * std::min(pairs, n_experts) ? 4 : 1;
+        a.work = work;
+        if (!stream_geometry(a, type, glu)) return cudaErrorInvalidValue;
+        return launch_stream(type, glu, a, s);
+    }
+    gemv_geometry(a, NT, glu);
+    return launch_gemv(type, glu, a, NT, max_tiles, s);
+}
+
 cudaError_t launch_stream(int type, bool glu, const GemvArgs &a, cudaStream_t s) {
     if (a.nwarps < 1 || a.nwarps > kStreamMaxWarps) return cudaErrorInvalidConfiguration;
     if (glu) {

@@ -189,6 +189,7 @@ static cudaError_t launch_down(int type, DownArgs d, cudaStream_t s) {
 struct FfnPlan {
     bool kq_gu, kq_d;
     int NT;
+    bool stream;  // batched expert GEMVs on the streaming kernel (index: one tile per expert)
     int64_t P;
     size_t off_logits, off_sel, off_w, off_slots, off_xq, off_index, off_act, off_xn, off_actq, off_experts, total;
 };
@@ -209,7 +210,9 @@ static qwb_status plan_ffn(const qwb_moe_ffn_desc *d, FfnPlan &p) {
     p.kq_gu = tg != QWB_TYPE_Q8_0;
     p.kq_d = td != QWB_TYPE_Q8_0;
     p.P = d->n_used * d->T;
-    p.NT = pick_nt(p.P, d->E);
+    // batched (T > 1): the streaming kernel when it fits, with one index tile per expert
+    p.stream = d->T > 1 && stream_fits_ffn(tg, d->H, d->gate.nb[1], d->up.nb[1], td, d->F, d->down.nb[1]);
+    p.NT = p.stream ? (int) std::max<int64_t>(1, p.P) : pick_nt(p.P, d->E);
     size_t o = kCtrlBytes;
     p.off_logits = o; o += align_up((size_t) (d->T * d->E) * 4, 256);
     p.off_sel = o; o += align_up((size_t) p.P * 4, 256);
@@ -351,8 +354,8 @@ extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, s
         a.remap = g2s_g; a.remap2 = g2s_u; a.n_ids = E; a.n_slots = n_mat;
         a.st = st;
         const int NT = decode ? 1 : p.NT;
-        gemv_geometry(a, NT, true);
-        e = launch_gemv(d->gate.type, true, a, NT, decode ? (int) K : ix.max_tiles, s);
+        e = launch_expert_gemv(d->gate.type, true, a, !decode && p.stream, NT, decode ? (int) K : ix.max_tiles, p.P,
+                               E, ix.work, s);
         if (e != cudaSuccess) return QWB_ERR_CUDA;
         profile_mark(s, QWB_KERNEL_GATE_UP);
     }
@@ -386,8 +389,7 @@ extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, s
         a.dst = experts; a.dnb1 = (size_t) H * 4; a.dnb2 = (size_t) K * H * 4;
         a.remap = g2s_d; a.n_ids = E; a.n_slots = n_mat;
         a.st = st;
-        gemv_geometry(a, p.NT, false);
-        e = launch_gemv(d->down.type, false, a, p.NT, ix.max_tiles, s);
+        e = launch_expert_gemv(d->down.type, false, a, p.stream, p.NT, ix.max_tiles, p.P, E, ix.work + 1, s);
         if (e != cudaSuccess) return QWB_ERR_CUDA;
         profile_mark(s, QWB_KERNEL_DOWN);
     }
