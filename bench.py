@@ -235,7 +235,7 @@ def prefill_experts(seed=7):
 MMID_TOKENS = (1, 8, 64)  # BASELINE config 4 decode batches
 
 
-def decode_mmid_sweep(q, lib, dev):
+def decode_mmid_sweep(q, lib, dev, tokens=MMID_TOKENS, n_pools=8):
     """Decode-batch MUL_MAT_ID (BASELINE config 4 shape: hidden 4096 -> expert FFN 1536,
     128 Q4_K experts, top-8 of uniform random routing) at T = 1, 8, 64 tokens: the
     weight-streaming path qwb_mul_mat_id takes for few tokens per expert.  Timed from CUDA
@@ -251,7 +251,7 @@ def decode_mmid_sweep(q, lib, dev):
     reps = E // PF_UNIQUE
     per = experts.size // PF_UNIQUE
     base = torch.from_numpy(experts).to(dev)
-    n_pools, n_call = 8, 8
+    n_call = 8
     pools = []
     for _ in range(n_pools):
         buf = torch.empty(base.numel() * reps, dtype=torch.uint8, device=dev)
@@ -261,13 +261,13 @@ def decode_mmid_sweep(q, lib, dev):
     rng = np.random.default_rng(11)
     s = torch.cuda.Stream()
     points = []
-    for T in MMID_TOKENS:
+    for T in tokens:
         ids_np = np.stack([rng.permutation(E)[:K_USED] for _ in range(T)]).astype(np.int32)
         ids = torch.from_numpy(ids_np).to(dev)
         b = torch.randn((T, 1, PF_H), device=dev)
         out = torch.empty((T, K_USED, PF_F), device=dev)
         for i in range(3):
-            q.mul_mat_id(pools[i], b, ids, out)
+            q.mul_mat_id(pools[i % n_pools], b, ids, out)
         torch.cuda.synchronize()
         s.wait_stream(torch.cuda.current_stream())
         g = torch.cuda.CUDAGraph()
@@ -314,7 +314,8 @@ def decode_mmid_sweep(q, lib, dev):
     torch.cuda.empty_cache()
     return {"config": {"workload": "C4 decode-batch MUL_MAT_ID, Q4_K x Q8_K, weight streaming", "hidden": PF_H,
                        "expert_ffn": PF_F, "experts": E, "top_k": K_USED, "routing": "uniform random",
-                       "tokens": list(MMID_TOKENS), "l2": "8 pools of all 128 experts, call i reads pool i"},
+                       "tokens": list(tokens),
+                       "l2": f"{n_pools} pools of all 128 experts, call i reads pool i mod {n_pools}"},
             "peak": hbm, "peak_kind": kind, "points": points}
 
 
@@ -524,6 +525,12 @@ def main():
                     help="MoE layers per step (default 48; fewer only for profiling captures)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (config 3) sweep")
     ap.add_argument("--no-mmid", action="store_true", help="skip the decode-batch MUL_MAT_ID (config 4) sweep")
+    ap.add_argument("--only-mmid", action="store_true",
+                    help="run only the decode-batch MUL_MAT_ID sweep and print its JSON (profiling runs)")
+    ap.add_argument("--mmid-tokens", default=",".join(str(t) for t in MMID_TOKENS),
+                    help="comma-separated token counts of the decode-batch MUL_MAT_ID sweep")
+    ap.add_argument("--mmid-pools", type=int, default=8,
+                    help="expert pools (453 MB each) the sweep rotates through between calls")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -543,6 +550,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         return run_ep(args, world, rank, local)
     lib = q.lib()
+    mmid_tokens = tuple(int(t) for t in args.mmid_tokens.split(","))
+    if args.only_mmid:
+        print(json.dumps({"decode_mmid": decode_mmid_sweep(q, lib, torch.device("cuda", local), mmid_tokens, args.mmid_pools)}))
+        return
 
     # ---------------------------------------------------------------- weights
     g, u, d = quantized_experts(seed=0)
@@ -709,7 +720,7 @@ def main():
     if rank == 0 and not args.no_prefill:
         result["prefill"] = prefill_sweep(q, lib, dev, args.warmup, 10, cpu=(world == 1 and not args.no_cpu))
     if rank == 0 and not args.no_mmid:
-        result["decode_mmid"] = decode_mmid_sweep(q, lib, dev)
+        result["decode_mmid"] = decode_mmid_sweep(q, lib, dev, mmid_tokens, args.mmid_pools)
     if rank == 0:
         print(json.dumps(result))
     if world > 1:

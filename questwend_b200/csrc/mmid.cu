@@ -537,8 +537,8 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
     a.n_slots = p.n_as;
     a.st = st;
     if (p.stream) {
-        // experts with several tokens cost more than their bytes: balance dynamically
-        a.chunks_per_cta = 2 * p.P > 3 * std::min(p.P, p.n_as) ? 4 : 1;
+        // rows cost more with more tokens on their expert: hand out chunks dynamically
+        a.chunks_per_cta = 2 * p.P > 3 * std::min(p.P, p.n_as) ? 8 : 4;
         a.work = ix.work;
         if (!stream_geometry(a, p.type, false)) return QWB_ERR_LAYOUT;
         e = launch_stream(p.type, false, a, s);

@@ -464,7 +464,7 @@ bool stream_fits_ffn(int type_gu, int64_t H, size_t nb_g, size_t nb_u, int type_
 cudaError_t launch_expert_gemv(int type, bool glu, GemvArgs a, bool stream, int NT, int max_tiles, int64_t pairs,
                                int64_t n_experts, int *work, cudaStream_t s) {
     if (stream) {
-        a.chunks_per_cta = 2 * pairs > 3 * std::min(pairs, n_experts) ? 4 : 1;
+        a.chunks_per_cta = 2 * pairs > 3 * std::min(pairs, n_experts) ? 8 : 4;
         a.work = work;
         if (!stream_geometry(a, type, glu)) return cudaErrorInvalidValue;
         return launch_stream(type, glu, a, s);
