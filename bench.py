@@ -40,6 +40,11 @@ ggml backend takes for a decode graph's MUL_MAT_ID nodes (weight streaming: each
 expert row read once for all its tokens).  GB/s counts the distinct expert weights per
 call; `frac` is against the measured HBM copy bandwidth, for the whole call (`us`) and for
 the streaming kernel alone (`kernel_us`).
+
+`gathers` (rank 0): BASELINE config 5 part 1 - GET_ROWS on a 151936 x 4096 table stored as
+Q4_K / Q6_K / Q8_0 with index streams of n = 1, 512, 8192 (uniform, 50 % repeats; bytes =
+n x (row + 16 KB f32 written + index)) - and config 2's Q6_K output head [2048 -> 151936]
+(255 MB) as quantized MUL_MAT at T = 1 and 8 tokens.
 """
 from __future__ import annotations
 
@@ -78,25 +83,42 @@ def peaks():
         return 6650.0, "fallback"
 
 
+Q8_0 = 8
+
+
+def synth_blocks(t, n_rows, K, rng):
+    """n_rows rows of K weights as valid ggml blocks of type t: uniformly random quantized
+    codes with fp16 scales sized so the dequantized weights are of the magnitude of a
+    quantized N(0, 0.02) matrix (|w| <~ 0.02-0.04).  The kernels' work and bytes do not
+    depend on the values; these only keep every output finite."""
+    def f16(lo, hi, n):
+        return rng.uniform(lo, hi, n).astype(np.float16).view(np.uint8).reshape(n, 2)
+    if t == Q4_K:  # d, dmin fp16 | 12 packed 6-bit scales / mins | 128 B nibbles
+        nb = n_rows * (K // 256)
+        b = rng.integers(0, 256, (nb, 144), dtype=np.uint8)
+        b[:, 0:2] = f16(1.5e-5, 2.5e-5, nb)
+        b[:, 2:4] = f16(1.5e-4, 2.5e-4, nb)
+    elif t == Q6_K:  # 128 B low bits | 64 B high bits | 16 int8 scales | d fp16
+        nb = n_rows * (K // 256)
+        b = rng.integers(0, 256, (nb, 210), dtype=np.uint8)
+        b[:, 192:208] = rng.integers(-64, 64, (nb, 16), dtype=np.int8).view(np.uint8)
+        b[:, 208:210] = f16(0.8e-5, 1.2e-5, nb)
+    else:  # Q8_0: d fp16 | 32 int8
+        nb = n_rows * (K // 32)
+        b = rng.integers(0, 256, (nb, 34), dtype=np.uint8)
+        b[:, 0:2] = f16(1.2e-4, 1.8e-4, nb)
+    return b.reshape(-1)
+
+
 def quantized_experts(seed=0):
-    """UNIQUE distinct expert matrices per role: N(0, 0.02) weights quantized with the
-    reference quantizer restatement (ggml_quantize_chunk semantics), built in threads."""
-    import concurrent.futures as cf
-
-    import oracle as O
-
-    def one(args):
-        role, i = args
-        rng = np.random.default_rng(seed * 1000 + role * 100 + i)
-        if role < 2:
-            x = (rng.standard_normal((F, H), dtype=np.float32) * 0.02).astype(np.float32)
-            return O.quantize_weights(Q4_K, x)
-        x = (rng.standard_normal((H, F), dtype=np.float32) * 0.02).astype(np.float32)
-        return O.quantize_weights(Q6_K, x)
-
-    with cf.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as ex:
-        out = list(ex.map(one, [(r, i) for r in range(3) for i in range(UNIQUE)]))
-    return [np.concatenate(out[r * UNIQUE:(r + 1) * UNIQUE]) for r in range(3)]
+    """UNIQUE distinct expert matrices per role (gate/up Q4_K [H -> F], down Q6_K [F -> H])
+    of synthetic quantized blocks (synth_blocks)."""
+    out = []
+    for role in range(3):
+        rng = np.random.default_rng(seed * 1000 + role)
+        t, rows, K = (Q4_K, F, H) if role < 2 else (Q6_K, H, F)
+        out.append(synth_blocks(t, UNIQUE * rows, K, rng))
+    return out
 
 
 class ClockSampler:
@@ -215,21 +237,13 @@ def zipf_ids(T, n_exp, n_used, seed, s=1.1):
 @functools.lru_cache(maxsize=1)
 def prefill_experts(seed=7):
     """PF_UNIQUE distinct Q4_K experts for the gate/up shape [PF_H -> PF_F] and the down
-    shape [PF_F -> PF_H]: N(0, 0.02) weights quantized with the reference quantizer."""
-    import concurrent.futures as cf
-
-    import oracle as O
-
-    def one(args):
-        role, i = args
-        rng = np.random.default_rng(seed * 1000 + role * 100 + i)
+    shape [PF_F -> PF_H] of synthetic quantized blocks (synth_blocks)."""
+    out = []
+    for role in range(2):
+        rng = np.random.default_rng(seed * 1000 + role)
         rows, k = (PF_F, PF_H) if role == 0 else (PF_H, PF_F)
-        x = (rng.standard_normal((rows, k), dtype=np.float32) * 0.02).astype(np.float32)
-        return O.quantize_weights(Q4_K, x)
-
-    with cf.ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as ex:
-        out = list(ex.map(one, [(r, i) for r in range(2) for i in range(PF_UNIQUE)]))
-    return [np.concatenate(out[r * PF_UNIQUE:(r + 1) * PF_UNIQUE]) for r in range(2)]
+        out.append(synth_blocks(Q4_K, PF_UNIQUE * rows, k, rng))
+    return out
 
 
 MMID_TOKENS = (1, 8, 64)  # BASELINE config 4 decode batches
@@ -317,6 +331,87 @@ def decode_mmid_sweep(q, lib, dev, tokens=MMID_TOKENS, n_pools=8):
                        "tokens": list(tokens),
                        "l2": f"{n_pools} pools of all 128 experts, call i reads pool i mod {n_pools}"},
             "peak": hbm, "peak_kind": kind, "points": points}
+
+
+VOCAB, EMB = 151936, 4096  # BASELINE config 5 embedding table; config 2 output head is VOCAB x H
+GATHER_N = (1, 512, 8192)
+
+
+def _graph_time(fn, n_call=8, reps=10):
+    """Median ms per call of fn(i), i = 0..n_call-1, from CUDA graph replays."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+        for i in range(n_call):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ts = []
+    for _ in range(reps):
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) / n_call)
+    del g
+    return float(np.median(ts))
+
+
+def gathers_sweep(q, dev):
+    """BASELINE config 5 part 1 and config 2's output head.
+    GET_ROWS on a 151936 x 4096 table stored as Q4_K / Q6_K / Q8_0 (350 / 510 / 661 MB)
+    with index streams of n = 1, 512, 8192 rows, uniform random with 50 % repeats; 8 index
+    sets rotate between calls so the rows read are not L2 hits.  Bytes = n x (row bytes +
+    16,384 B written + 4 B index).  Output head: qwb_mul_mat of the Q6_K [2048 -> 151936]
+    matrix (255 MB) at T = 1 and 8 tokens.  Tables: 512 distinct synthetic rows tiled."""
+    import torch
+    hbm, kind = peaks()
+    rng = np.random.default_rng(5)
+    out = {"peak": hbm, "peak_kind": kind, "get_rows": [], "output_head": []}
+    for t in (Q4_K, Q6_K, Q8_0):
+        rows = synth_blocks(t, 512, EMB, rng)
+        rb = rows.size // 512
+        tab = torch.empty(VOCAB * rb, dtype=torch.uint8, device=dev)
+        reps = -(-VOCAB // 512)
+        src = torch.from_numpy(rows).to(dev).view(1, -1).expand(reps, -1).reshape(-1)
+        tab.copy_(src[:VOCAB * rb])
+        T = q.QTensor(tab, t, (EMB, VOCAB, 1, 1))
+        for n in GATHER_N:
+            sets = []
+            for _ in range(8):
+                base = rng.integers(0, VOCAB, max(1, (n + 1) // 2))
+                idx = np.concatenate([base, rng.choice(base, n - base.size)]) if n > 1 else base
+                sets.append(torch.from_numpy(rng.permutation(idx).astype(np.int32)).to(dev))
+            dst = torch.empty((1, 1, n, EMB), device=dev)
+            ms = _graph_time(lambda i: q.get_rows(T, sets[i % 8], dst))
+            nbytes = n * (rb + EMB * 4 + 4)
+            out["get_rows"].append({"type": {12: "Q4_K", 14: "Q6_K", 8: "Q8_0"}[t], "n": n, "us": 1e3 * ms,
+                                    "gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / hbm})
+        del tab, T
+    # output head (config 2): Q6_K [H = 2048 -> VOCAB]
+    rows = synth_blocks(Q6_K, 512, H, rng)
+    rb = rows.size // 512
+    heads = []
+    for _ in range(2):  # two copies: consecutive calls read different 255 MB matrices
+        w = torch.empty(VOCAB * rb, dtype=torch.uint8, device=dev)
+        w.copy_(torch.from_numpy(rows).to(dev).view(1, -1).expand(-(-VOCAB // 512), -1).reshape(-1)[:VOCAB * rb])
+        heads.append(q.QTensor(w, Q6_K, (H, VOCAB, 1, 1)))
+    for Tt in (1, 8):
+        x = torch.randn((Tt, H), device=dev)
+        y = torch.empty((Tt, VOCAB), device=dev)
+        ms = _graph_time(lambda i: q.mul_mat(heads[i % 2], x, y))
+        nbytes = VOCAB * rb
+        out["output_head"].append({"tokens": Tt, "weight_mb": nbytes / 1e6, "us": 1e3 * ms,
+                                   "gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / hbm})
+    del heads
+    torch.cuda.empty_cache()
+    return out
 
 
 def prefill_sweep(q, lib, dev, warmup, iters, cpu):
@@ -492,7 +587,7 @@ def run_ep(args, world, rank, local):
             "metric": "decode_tokens_per_s", "value": world * 1000.0 / ms_step, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "q4_K/q6_K x q8_K -> f32", "data": "synthetic (seeded N(0,0.02) weights, ggml quantizer)",
+            "dtype": "q4_K/q6_K x q8_K -> f32", "data": "synthetic (seeded quantized blocks: random codes, scales sized like quantized N(0,0.02))",
             "config": cfg,
             "e2e": {"value": world * 1000.0 / ms_e2e, "unit": "tokens/s", "h2d_bytes_per_step": H * 4,
                     "d2h_bytes_per_step": H * 4},
@@ -525,6 +620,8 @@ def main():
                     help="MoE layers per step (default 48; fewer only for profiling captures)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (config 3) sweep")
     ap.add_argument("--no-mmid", action="store_true", help="skip the decode-batch MUL_MAT_ID (config 4) sweep")
+    ap.add_argument("--no-gathers", action="store_true",
+                    help="skip the GET_ROWS (config 5) and output-head (config 2) measurements")
     ap.add_argument("--only-mmid", action="store_true",
                     help="run only the decode-batch MUL_MAT_ID sweep and print its JSON (profiling runs)")
     ap.add_argument("--mmid-tokens", default=",".join(str(t) for t in MMID_TOKENS),
@@ -691,7 +788,7 @@ def main():
         "metric": "decode_tokens_per_s", "value": world * 1000.0 / ms_step, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "q4_K/q6_K x q8_K -> f32", "data": "synthetic (seeded N(0,0.02) weights, ggml quantizer)",
+        "dtype": "q4_K/q6_K x q8_K -> f32", "data": "synthetic (seeded quantized blocks: random codes, scales sized like quantized N(0,0.02))",
         "config": workload_config(world, n_layers),
         "decode_hbm_gbs": step_bytes / (ms_step * 1e-3) / 1e9,
         "decode_hbm_frac": step_bytes / (ms_step * 1e-3) / 1e9 / hbm,
@@ -721,6 +818,8 @@ def main():
         result["prefill"] = prefill_sweep(q, lib, dev, args.warmup, 10, cpu=(world == 1 and not args.no_cpu))
     if rank == 0 and not args.no_mmid:
         result["decode_mmid"] = decode_mmid_sweep(q, lib, dev, mmid_tokens, args.mmid_pools)
+    if rank == 0 and not args.no_gathers:
+        result["gathers"] = gathers_sweep(q, dev)
     if rank == 0:
         print(json.dumps(result))
     if world > 1:

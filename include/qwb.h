@@ -156,6 +156,20 @@ QWB_API qwb_status qwb_mul_mat_id_noalloc(const qwb_tensor *as, const qwb_tensor
                                           const qwb_tensor *ids, const qwb_tensor *dst,
                                           qwb_status_block *d_status, qwb_stream_t stream);
 
+/* ------------------------------------------------------------------ MUL_MAT
+ * replaces ggml_compute_forward_mul_mat (ggml-cpu/ggml-cpu.c:1255-1470) for quantized
+ * weights; op contract ggml_mul_mat (ggml.c:3362-3377).  The shared expert and dense FFN
+ * matrices (core/runtime.cpp:2825-2833) and the output head (runtime.cpp:3037):
+ *   a   [K, M]   Q4_K | Q6_K | Q8_0 (rows contiguous blocks, no batch dimensions)
+ *   b   [K, T]   F32 (rows contiguous)
+ *   dst [M, T]   F32
+ * dst[:, t] = a . b[:, t], b quantized exactly as the CPU backend does (Q8_K / Q8_0-cpu).
+ * Same kernels and tolerance as qwb_mul_mat_id (one expert that every token selects). */
+QWB_API size_t qwb_mul_mat_workspace_size(const qwb_tensor *a, const qwb_tensor *b);
+QWB_API qwb_status qwb_mul_mat(const qwb_tensor *a, const qwb_tensor *b, const qwb_tensor *dst,
+                               void *workspace, size_t workspace_bytes, qwb_status_block *d_status,
+                               qwb_stream_t stream);
+
 /* ------------------------------------------------------------ small MoE ops */
 /* replaces the route_experts subgraph (core/runtime.cpp:2693-2734): soft_max
  * (ops.cpp:5813) -> argsort_top_k (ggml.c:5462) -> get_rows of probs -> sum_rows ->

@@ -7,6 +7,7 @@
  * (interface version 3: buffer type :17-39, buffer :50-79, backend :122-164, device
  * :177-225, registry :231-247).  It computes
  *   GGML_OP_MUL_MAT_ID  on Q4_K / Q6_K / Q8_0 expert tensors      -> qwb_mul_mat_id
+ *   GGML_OP_MUL_MAT     on 2-D Q4_K / Q6_K / Q8_0 weights          -> qwb_mul_mat
  *   GGML_OP_GET_ROWS    on Q4_K / Q6_K / Q8_0 / F16 / F32 / I32     -> qwb_get_rows
  * and reports every other compute op unsupported, so the scheduler places those on
  * ggml-cuda or the CPU backend.  Tensors live in the device's buffer type (cudaMalloc'd

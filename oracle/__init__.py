@@ -128,6 +128,9 @@ def ref():
                                        vp, vp, vp, vp, vp, vp, i32, vp, f32]
         lib.qref_backend_mul_mat_id.argtypes = [cp, i32, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, vp]
         lib.qref_backend_get_rows.argtypes = [cp, i32, vp, i64, i64, vp, i64, vp]
+        lib.qref_mul_mat.restype = f64
+        lib.qref_mul_mat.argtypes = [i32, vp, i64, i64, vp, i64, vp, i32]
+        lib.qref_backend_mul_mat.argtypes = [cp, i32, vp, i64, i64, vp, i64, vp]
         lib.qref_backend_sched_mul_mat_id.argtypes = [cp, i32, vp, i64, i64, i64, vp, i64, vp, i64, f32, vp, ip, ip]
         _ref = lib
     return _ref
@@ -200,6 +203,20 @@ def mul_mat_id(t: int, w: np.ndarray, K: int, M: int, n_as: int, b: np.ndarray,
     return dst, rc
 
 
+def mul_mat(t: int, w: np.ndarray, K: int, M: int, b: np.ndarray, impl: str = "port", iters: int = 0):
+    """dst[T, M] = ggml_mul_mat(a[M, K] quantized, b[T, K]).  impl="ref": the reference's
+    ggml CPU backend (returns (dst, ms_per_iter)); "port": the restatement's mul_mat_id
+    with one expert that every token selects (the same dots; returns (dst, rc))."""
+    b = np.ascontiguousarray(b, dtype=np.float32).reshape(-1, K)
+    T = b.shape[0]
+    if impl == "ref":
+        dst = np.zeros((T, M), dtype=np.float32)
+        ms = ref().qref_mul_mat(t, _p(w), K, M, _p(b), T, _p(dst), iters)
+        return dst, ms
+    dst, rc = mul_mat_id(t, w, K, M, 1, b.reshape(T, 1, K), np.zeros((T, 1), dtype=np.int32))
+    return dst.reshape(T, M), rc
+
+
 def get_rows(t: int, src: np.ndarray, ne0: int, nrows: int, idx: np.ndarray,
              impl: str = "port", iters: int = 0):
     idx = np.ascontiguousarray(idx, dtype=np.int32)
@@ -234,6 +251,14 @@ def backend_get_rows(path: str, t: int, src: np.ndarray, ne0: int, nrows: int, i
     idx = np.ascontiguousarray(idx, dtype=np.int32)
     dst = np.zeros((idx.size, ne0), dtype=np.int32 if t == I32 else np.float32)
     rc = ref().qref_backend_get_rows(path.encode(), t, _p(src), ne0, nrows, _p(idx), idx.size, _p(dst))
+    return dst, rc
+
+
+def backend_mul_mat(path: str, t: int, w: np.ndarray, K: int, M: int, b: np.ndarray):
+    """mul_mat computed by the ggml backend library at `path`.  Returns (dst [T, M], rc)."""
+    b = np.ascontiguousarray(b, dtype=np.float32).reshape(-1, K)
+    dst = np.zeros((b.shape[0], M), dtype=np.float32)
+    rc = ref().qref_backend_mul_mat(path.encode(), t, _p(w), K, M, _p(b), b.shape[0], _p(dst))
     return dst, rc
 
 

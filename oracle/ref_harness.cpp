@@ -162,6 +162,23 @@ double qref_get_rows(int type, const void * src, int64_t ne0, int64_t nrows,
     return ms;
 }
 
+// dst[M, T] = mul_mat(a[K, M] of `type`, b[K, T] f32): ggml_mul_mat (ggml.c:3362) on the
+// CPU backend, as the dense FFN / shared expert / output head (runtime.cpp:2825-2833, 3037)
+double qref_mul_mat(int type, const void * a, int64_t K, int64_t M, const float * b, int64_t T,
+                    float * dst, int iters) {
+    Graph g;
+    ggml_tensor * ta  = ggml_new_tensor_2d(g.ctx, (ggml_type) type, K, M);
+    ggml_tensor * tb  = ggml_new_tensor_2d(g.ctx, GGML_TYPE_F32, K, T);
+    ggml_tensor * out = ggml_mul_mat(g.ctx, ta, tb);
+    ggml_build_forward_expand(g.gf, out);
+    g.bind(ta, a);
+    g.alloc_rest();
+    ggml_backend_tensor_set(tb, b, 0, ggml_nbytes(tb));
+    double ms = g.compute(iters);
+    ggml_backend_tensor_get(out, dst, 0, ggml_nbytes(out));
+    return ms;
+}
+
 // route_experts (runtime.cpp:2693-2734) on given logits [E, T]:
 // selected[n_used, T] i32, weights[n_used, T] f32 (renormalised when norm != 0).
 double qref_route(const float * logits, int64_t E, int64_t T, int64_t n_used, int norm,
@@ -359,6 +376,31 @@ int qref_backend_mul_mat_id(const char * path, int type, const void * as, int64_
             ggml_backend_tensor_set(tas, as, 0, ggml_nbytes(tas));
             ggml_backend_tensor_set(tb, b, 0, ggml_nbytes(tb));
             ggml_backend_tensor_set(tidf, ids, 0, ggml_nbytes(tidf));
+            if (ggml_backend_graph_compute(be, g.gf) != GGML_STATUS_SUCCESS) rc = -5;
+            else ggml_backend_tensor_get(out, dst, 0, ggml_nbytes(out));
+        }
+    }
+    ggml_backend_free(be);
+    return rc;
+}
+
+// qref_mul_mat computed by the backend in `path`.
+int qref_backend_mul_mat(const char * path, int type, const void * a, int64_t K, int64_t M, const float * b,
+                         int64_t T, float * dst) {
+    int rc = 0;
+    ggml_backend_t be = backend_open(path, &rc);
+    if (!be) return rc;
+    {
+        BackendGraph g;
+        ggml_tensor * ta  = ggml_new_tensor_2d(g.wctx, (ggml_type) type, K, M);
+        ggml_tensor * tb  = ggml_new_tensor_2d(g.ctx, GGML_TYPE_F32, K, T);
+        ggml_tensor * out = ggml_mul_mat(g.ctx, ta, tb);
+        ggml_build_forward_expand(g.gf, out);
+        if (!g.alloc(be)) {
+            rc = -4;
+        } else {
+            ggml_backend_tensor_set(ta, a, 0, ggml_nbytes(ta));
+            ggml_backend_tensor_set(tb, b, 0, ggml_nbytes(tb));
             if (ggml_backend_graph_compute(be, g.gf) != GGML_STATUS_SUCCESS) rc = -5;
             else ggml_backend_tensor_get(out, dst, 0, ggml_nbytes(out));
         }

@@ -79,6 +79,8 @@ SIGNATURES = [
     ("qwb_get_rows", C.c_int, [_TP, _TP, _TP, _P, _P]),
     ("qwb_mul_mat_id_workspace_size", C.c_size_t, [_TP, _TP, _TP]),
     ("qwb_mul_mat_id", C.c_int, [_TP, _TP, _TP, _TP, _P, C.c_size_t, _P, _P]),
+    ("qwb_mul_mat_workspace_size", C.c_size_t, [_TP, _TP]),
+    ("qwb_mul_mat", C.c_int, [_TP, _TP, _TP, _P, C.c_size_t, _P, _P]),
     ("qwb_mul_mat_id_noalloc", C.c_int, [_TP, _TP, _TP, _TP, _P, _P]),
     ("qwb_moe_route", C.c_int, [_P, _P, C.c_int64, C.c_int64, C.c_int64, C.c_int, C.c_float, _P, _P, _P]),
     ("qwb_swiglu", C.c_int, [_P, _P, _P, C.c_int64, _P]),

@@ -1,7 +1,8 @@
 // ggml-qwb.cpp - a ggml backend (interface version 3) for B200 that runs QuestWend's MoE
 // hot path through libqwb.so: GGML_OP_MUL_MAT_ID on Q4_K / Q6_K / Q8_0 expert tensors
-// (slot-pool tensors with slot ids included) and GGML_OP_GET_ROWS on Q4_K / Q6_K / Q8_0 /
-// F16 / F32 / I32 rows.  Every other compute op is reported unsupported, so ggml's
+// (slot-pool tensors with slot ids included), GGML_OP_MUL_MAT on 2-D Q4_K / Q6_K / Q8_0
+// weights (shared expert, dense FFN, output head) and GGML_OP_GET_ROWS on Q4_K / Q6_K /
+// Q8_0 / F16 / F32 / I32 rows.  Every other compute op is reported unsupported, so ggml's
 // scheduler places it on another backend (ggml-cuda or the CPU).
 //
 // The vtables are the ones of ggml-backend-impl.h (buffer type / buffer :17-85, backend
@@ -178,6 +179,14 @@ bool supported(const ggml_tensor *op) {
             qwb_tensor qa = view_of(a), qb = view_of(b), qi = view_of(ids);
             return qwb_mul_mat_id_workspace_size(&qa, &qb, &qi) > 0;
         }
+        case GGML_OP_MUL_MAT: {
+            const ggml_tensor *a = op->src[0], *b = op->src[1];
+            if (!weight_type(a->type) || b->type != GGML_TYPE_F32 || op->type != GGML_TYPE_F32) return false;
+            if (b->nb[0] != sizeof(float) || op->nb[0] != sizeof(float) || a->nb[0] != ggml_type_size(a->type))
+                return false;
+            qwb_tensor qa = view_of(a), qb = view_of(b);
+            return qwb_mul_mat_workspace_size(&qa, &qb) > 0;
+        }
         case GGML_OP_GET_ROWS: {
             const ggml_tensor *s = op->src[0], *i = op->src[1];
             const bool rows = weight_type(s->type) || s->type == GGML_TYPE_F16 || s->type == GGML_TYPE_F32 ||
@@ -276,6 +285,12 @@ ggml_status be_compute(ggml_backend_t be, ggml_cgraph *g) {
                 qwb_tensor a = view_of(t->src[0]), b = view_of(t->src[1]), ids = view_of(t->src[2]), d = view_of(t);
                 if (!reserve_workspace(c, qwb_mul_mat_id_workspace_size(&a, &b, &ids))) return GGML_STATUS_ALLOC_FAILED;
                 rc = qwb_mul_mat_id(&a, &b, &ids, &d, c->ws, c->ws_bytes, c->status, (qwb_stream_t) c->stream);
+                break;
+            }
+            case GGML_OP_MUL_MAT: {
+                qwb_tensor a = view_of(t->src[0]), b = view_of(t->src[1]), d = view_of(t);
+                if (!reserve_workspace(c, qwb_mul_mat_workspace_size(&a, &b))) return GGML_STATUS_ALLOC_FAILED;
+                rc = qwb_mul_mat(&a, &b, &d, c->ws, c->ws_bytes, c->status, (qwb_stream_t) c->stream);
                 break;
             }
             case GGML_OP_GET_ROWS: {

@@ -197,6 +197,24 @@ def mul_mat_id(as_: QTensor, b: torch.Tensor, ids: torch.Tensor, out: torch.Tens
     return out
 
 
+# ------------------------------------------------------------------ MUL_MAT
+def mul_mat(a: QTensor, b: torch.Tensor, out: torch.Tensor | None = None):
+    """ggml_mul_mat(a [K, M] quantized, b [K, T] f32) -> [M, T] (dense FFN / shared expert /
+    output head).  Torch shapes: b (T, K) f32, result (T, M) f32."""
+    T, M = b.shape[0], a.ne[1]
+    if out is None:
+        out = torch.empty((T, M), dtype=torch.float32, device=b.device)
+    ad, bd, od = desc(a), desc(b), desc(out)
+    lib = L.lib()
+    need = lib.qwb_mul_mat_workspace_size(C.byref(ad), C.byref(bd))
+    if need == 0 and T > 0:
+        raise L.QwbError("qwb_mul_mat_workspace_size", 3)
+    ws = workspace(need)
+    L.check("qwb_mul_mat", lib.qwb_mul_mat(C.byref(ad), C.byref(bd), C.byref(od), _ws_ptr(ws), ws.numel(),
+                                           status_block().data_ptr(), _stream()))
+    return out
+
+
 # ------------------------------------------------------------------ small MoE ops
 def moe_route(logits: torch.Tensor, n_used: int, norm: bool = True, scale: float = 0.0,
               mask: torch.Tensor | None = None):

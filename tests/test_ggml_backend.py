@@ -57,3 +57,17 @@ def test_no_b200_means_score_0_and_no_device(shim):
     _, rc = O.backend_mul_mat_id(SHIM, O.Q8_0, w, 64, 2, 2, np.zeros((1, 1, 64), np.float32),
                                  np.zeros((1, 2), np.int32))
     assert rc == -1
+
+
+def test_mul_mat_reference_driver_matches_restatement():
+    # the reference's own ggml_mul_mat (CPU backend) and the restatement agree; the GPU
+    # tests hold qwb_mul_mat to the former
+    if not O.ref_available():
+        pytest.skip("the reference ggml (oracle/_ref) is not built")
+    import _data as D
+    for t, K, M, T in ((O.Q4_K, 512, 96, 5), (O.Q6_K, 768, 64, 9), (O.Q8_0, 256, 40, 3)):
+        w = D.weights(t, 1, M, K, seed=K)
+        b = D.acts((T, K), seed=T)
+        r, _ = O.mul_mat(t, w, K, M, b, impl="ref")
+        p, rc = O.mul_mat(t, w, K, M, b)
+        assert rc == 0 and O.nrmse(p, r) <= 1e-6
