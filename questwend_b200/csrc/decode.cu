@@ -43,9 +43,17 @@ namespace qwb {
 // global timer at numbered points of each kernel.
 #ifdef QWB_DECODE_TRACE
 __device__ unsigned long long g_decode_trace[3][160][8];
+__device__ unsigned int g_decode_smid[3][160];
 #define QWB_TRACE(k, p)                                                                   \
     do {                                                                                 \
-        if (threadIdx.x == 0 && blockIdx.x < 160) g_decode_trace[k][blockIdx.x][p] = globaltimer_ns(); \
+        if (threadIdx.x == 0 && blockIdx.x < 160) {                                      \
+            g_decode_trace[k][blockIdx.x][p] = globaltimer_ns();                         \
+            if (p == 0) {                                                                \
+                unsigned int sm;                                                         \
+                asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));                          \
+                g_decode_smid[k][blockIdx.x] = sm;                                       \
+            }                                                                            \
+        }                                                                                \
     } while (0)
 #else
 #define QWB_TRACE(k, p) \
@@ -319,7 +327,6 @@ __global__ void __launch_bounds__(kRouterThreads) router_decode_kernel(const Rou
         if (rbytes) bulk_span_issue(rows, r.router_w + (int64_t) e0 * H, rbytes, &bar[0]);
         if (r.norm_w) bulk_span_issue(gw, r.norm_w, gbytes, &bar[0]);
     }
-    pdl_trigger();
     pdl_wait();  // x is the previous layer's output
     QWB_TRACE(0, 1);
 
@@ -386,6 +393,11 @@ __global__ void __launch_bounds__(kRouterThreads) router_decode_kernel(const Rou
     }
     cluster.sync();  // every logit is in CTA 0's shared memory
     QWB_TRACE(0, 4);
+    // Let the gate/up kernel launch now, while CTA 0 routes: its launch overlaps the
+    // routing, and by now the previous layer's down kernel has completed (pdl_wait
+    // above), so its CTAs find a free slot on every SM.  Triggering at entry launched it
+    // while that down kernel still held every SM, and its CTAs doubled up on some SMs.
+    pdl_trigger();
     if (rank_in_cluster != 0) {
         // side work of CTAs 1..: Q8 of the normed x, one 256-chunk per warp (needed by the
         // next kernel, which waits for this grid to complete)
@@ -639,7 +651,14 @@ static cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cud
 
 template <typename Kern>
 static cudaError_t set_smem(Kern kern, size_t smem) {
-    if (smem <= 48 * 1024) return cudaSuccess;
+    // The three decode kernels overlap on every SM under programmatic dependent launch.
+    // An SM's L1 / shared-memory split is set for the kernels resident on it and changes
+    // only when it drains; with every kernel asking for the largest shared carveout, a CTA
+    // fits wherever the shared memory it needs is free (otherwise some CTAs doubled up on
+    // other SMs and finished microseconds after the rest).
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         (int) cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess || smem <= 48 * 1024) return e;
     return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
 }
 
@@ -725,6 +744,9 @@ cudaError_t launch_down_decode(int type, const DownDecodeArgs &a, cudaStream_t s
 }  // namespace qwb
 
 #ifdef QWB_DECODE_TRACE
+extern "C" QWB_API int qwb_debug_decode_smid(void *host, size_t bytes) {
+    return cudaMemcpyFromSymbol(host, qwb::g_decode_smid, bytes) == cudaSuccess ? 0 : 1;
+}
 extern "C" QWB_API int qwb_debug_decode_trace(void *host, size_t bytes) {
     return cudaMemcpyFromSymbol(host, qwb::g_decode_trace, bytes) == cudaSuccess ? 0 : 1;
 }

@@ -1,0 +1,114 @@
+"""GPU parity: MUL_MAT_ID on Q8_0 experts with many tokens per expert, the integer
+tensor-core kernel (mma.sync s8 x s8 -> s32, one MMA per 32-element block, fp32 block
+scaling in block order), against the oracle's Q8_0 x Q8_0 dots (activations quantized
+with the CPU backend's Q8_0 variant), against the reference's own ggml CPU backend under
+skewed routing, and against the weight-streaming path on the same inputs.
+Bar: nRMS <= 1e-4 (max abs-rel error in the message)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+import _data as D
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+
+@pytest.fixture(scope="module")
+def qwb():
+    import questwend_b200 as q
+    q.lib()
+    return q
+
+
+def cu(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _run(q, W, b, ids, profile=False):
+    from questwend_b200 import _lib as L
+    lib = L.lib()
+    if profile:
+        L.check("qwb_profile_enable", lib.qwb_profile_enable(8))
+        lib.qwb_profile_reset()
+    out = q.mul_mat_id(W, b, ids)
+    torch.cuda.synchronize()
+    tags = []
+    if profile:
+        n = lib.qwb_profile_count() - 1
+        ms = (C.c_float * max(n, 1))()
+        tg = (C.c_int32 * max(n, 1))()
+        L.check("qwb_profile_read", lib.qwb_profile_read(ms, tg, n))
+        tags = list(tg[:n])
+        L.check("qwb_profile_enable", lib.qwb_profile_enable(0))
+    return out, tags
+
+
+def _stream(q, W, b, ids):
+    # qwb_mul_mat_id_noalloc never takes a tensor-core path: the weight-streaming kernel
+    from questwend_b200 import _lib as L
+    T, n_used, M = ids.shape[0], ids.shape[1], W.ne[1]
+    out = torch.empty((T, n_used, M), dtype=torch.float32, device="cuda")
+    ad, bd, idd, od = q.ops.desc(W), q.ops.desc(b), q.ops.desc(ids), q.ops.desc(out)
+    rc = L.lib().qwb_mul_mat_id_noalloc(C.byref(ad), C.byref(bd), C.byref(idd), C.byref(od),
+                                       q.ops.status_block().data_ptr(),
+                                       C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    return out
+
+
+CASES = [
+    # K, M, n_as, T, n_used, n_b
+    (1024, 300, 8, 256, 4, 1),      # rows not a multiple of 128, partial token tiles
+    (2048, 768, 16, 512, 8, 1),     # gate/up-like
+    (512, 2048, 8, 128, 4, 4),      # down-like: one activation row per (token, slot)
+    (4096, 128, 8, 64, 8, 8),       # long K, one activation row per (token, slot)
+]
+
+
+@pytest.mark.parametrize("K,M,n_as,T,n_used,n_b", CASES)
+def test_uniform_routing(qwb, K, M, n_as, T, n_used, n_b):
+    w = D.weights(O.Q8_0, n_as, M, K, seed=K + M + T)
+    b = D.acts((T, n_b, K), seed=T + 5)
+    ids = np.stack([D.rng(200 + i).permutation(n_as)[:n_used] for i in range(T)]).astype(np.int32)
+    W = qwb.QTensor.from_bytes(w, O.Q8_0, (K, M, n_as))
+    got, tags = _run(qwb, W, cu(b), cu(ids), profile=True)
+    assert 5 in tags  # the tensor-core kernel ran (QWB_KERNEL_GROUPED_GEMM)
+    flags, _, _ = qwb.read_status()
+    assert flags == 0
+    want, rc = O.mul_mat_id(O.Q8_0, w, K, M, n_as, b, ids)
+    assert rc == 0
+    got = got.cpu().numpy()
+    e = O.nrmse(got, want)
+    assert e <= TOL, (e, O.max_abs_rel(got, want))
+
+
+def test_zipf_routing_against_reference_build(qwb):
+    K, M, n_as, T, n_used = 1024, 256, 64, 512, 8
+    w = D.weights(O.Q8_0, n_as, M, K, seed=31)
+    b = D.acts((T, 1, K), seed=32)
+    ids = D.zipf_ids(T, n_as, n_used, seed=33)
+    W = qwb.QTensor.from_bytes(w, O.Q8_0, (K, M, n_as))
+    got = _run(qwb, W, cu(b), cu(ids))[0].cpu().numpy()
+    if O.ref_available():
+        O.set_ref_threads(8)
+        want, _ = O.mul_mat_id(O.Q8_0, w, K, M, n_as, b, ids, impl="ref")
+    else:
+        want, _ = O.mul_mat_id(O.Q8_0, w, K, M, n_as, b, ids)
+    e = O.nrmse(got, want)
+    assert e <= TOL, (e, O.max_abs_rel(got, want))
+
+
+def test_matches_streaming_path(qwb):
+    K, M, n_as, T, n_used = 1024, 384, 8, 160, 8
+    w = D.weights(O.Q8_0, n_as, M, K, seed=51)
+    b = cu(D.acts((T, 1, K), seed=52))
+    ids = cu(np.stack([D.rng(53 + i).permutation(n_as)[:n_used] for i in range(T)]).astype(np.int32))
+    W = qwb.QTensor.from_bytes(w, O.Q8_0, (K, M, n_as))
+    tc = _run(qwb, W, b, ids)[0]
+    st = _stream(qwb, W, b, ids)
+    # the same per-block fp32 products; only the summation order of blocks vs passes differs
+    assert O.nrmse(tc.cpu().numpy(), st.cpu().numpy()) <= 1e-5
