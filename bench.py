@@ -461,8 +461,8 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu):
             points.append({"tokens": T, "shape": name, "ms": t_ms, "tflops": fl / (t_ms * 1e-3) / 1e12,
                            "gemm_ms": g_ms, "gemm_tflops": fl / (g_ms * 1e-3) / 1e12 if g_ms > 0 else None})
     L.check("qwb_profile_enable", lib.qwb_profile_enable(0))
-    # Q8_0 experts (config 3's second weight type), gate/up shape: no tensor-core path
-    # yet, the weight-streaming kernel runs every token of an expert in passes of <= 8
+    # Q8_0 experts (config 3's second weight type), gate/up shape, and Q6_K experts, down
+    # shape: the integer tensor-core kernel
     q8_points = []
     rng = np.random.default_rng(17)
     q8base = torch.from_numpy(synth_blocks(Q8_0, PF_UNIQUE * PF_F, PF_H, rng)).to(dev)
@@ -487,8 +487,33 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu):
         fl = 2.0 * T * K_USED * PF_H * PF_F
         t_ms = float(np.median(tot))
         q8_points.append({"tokens": T, "shape": "gate_up", "type": "Q8_0", "ms": t_ms,
-                          "tflops": fl / (t_ms * 1e-3) / 1e12, "path": "weight streaming (dp4a)"})
+                          "tflops": fl / (t_ms * 1e-3) / 1e12, "path": "int8 tensor cores (mma.sync)"})
     del W8, q8buf, q8base
+    # Q6_K experts, down shape [PF_F -> PF_H] (the Q4_K_M mix's down projections)
+    q6base = torch.from_numpy(synth_blocks(Q6_K, PF_UNIQUE * PF_H, PF_F, rng)).to(dev)
+    q6buf = torch.empty(q6base.numel() * reps, dtype=torch.uint8, device=dev)
+    q6buf.view(reps, -1).copy_(q6base.expand(reps, -1))
+    W6 = q.QTensor(q6buf, Q6_K, (PF_F, PF_H, E, 1))
+    for T in PF_TOKENS:
+        ids = torch.from_numpy(zipf_ids(T, E, K_USED, seed=T)).to(dev)
+        b = torch.randn((T, K_USED, PF_F), generator=gen, device=dev)
+        out = torch.empty((T, K_USED, PF_H), device=dev)
+        q.mul_mat_id(W6, b, ids, out)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        tot = []
+        for _ in range(3):
+            e0.record()
+            q.mul_mat_id(W6, b, ids, out)
+            e1.record()
+            torch.cuda.synchronize()
+            tot.append(e0.elapsed_time(e1))
+        assert torch.isfinite(out).all()
+        fl = 2.0 * T * K_USED * PF_H * PF_F
+        t_ms = float(np.median(tot))
+        q8_points.append({"tokens": T, "shape": "down", "type": "Q6_K", "ms": t_ms,
+                          "tflops": fl / (t_ms * 1e-3) / 1e12, "path": "int8 tensor cores (mma.sync)"})
+    del W6, q6buf, q6base
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             peak, pkind = json.load(f)["bf16_tflops"], "measured bf16 burst"
@@ -498,7 +523,7 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu):
     res = {"config": {"workload": "C3 prefill grouped GEMM, MUL_MAT_ID Q4_K x Q8_K", "hidden": PF_H,
                       "expert_ffn": PF_F, "experts": E, "top_k": K_USED, "routing": "Zipf(1.1) + Gumbel",
                       "tokens": list(PF_TOKENS), "l2": "weights 453 MB per matrix > L2"},
-           "points": points, "q8_0_points": q8_points,
+           "points": points, "int8_points": q8_points,
            "roofline": {"bound": "tensor", "kernel": f"grouped GEMM, gate/up shape, T={PF_TOKENS[-1]}",
                         "achieved": top["gemm_tflops"], "peak": peak, "peak_kind": pkind, "unit": "TFLOP/s",
                         "frac": top["gemm_tflops"] / peak if top["gemm_tflops"] else None, "traffic": None}}

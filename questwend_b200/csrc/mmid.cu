@@ -394,7 +394,7 @@ struct MmidPlan {
     int NT;
     bool pf;  // tensor-core grouped GEMM (many tokens per expert)
     bool stream;  // weight-streaming kernel (one tile per expert)
-    bool pf8;     // Q8_0 integer tensor-core kernel (many tokens per expert)
+    bool pf8;     // Q8_0 / Q6_K integer tensor-core kernel (many tokens per expert)
     size_t planes, index, btiles, da, total;
 };
 
@@ -422,10 +422,10 @@ qwb_status plan_mmid(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor
     p.P = p.n_used * p.T;
     if (p.P > (1 << 24) || p.n_as > 16384 || p.K > (1 << 20) || p.M > (1 << 30)) return QWB_ERR_LIMIT;
     p.pf = allow_prefill && pf_eligible(p.type, p.K, p.M, p.P, p.n_as);
-    p.pf8 = allow_prefill && pf_q80_eligible(p.type, p.K, p.M, p.P, p.n_as, as->data, as->nb[1], as->nb[2]);
+    p.pf8 = allow_prefill && pf_i8_eligible(p.type, p.K, p.M, p.P, p.n_as, as->data, as->nb[1], as->nb[2]);
     p.stream = !p.pf && !p.pf8 && stream_fits(p.type, p.K, as->nb[1], as->nb[1], false);
     p.NT = p.pf    ? kPfTileN
-           : p.pf8 ? pf_q80_tile_tokens()
+           : p.pf8 ? pf_i8_tile_tokens()
            : p.stream ? (int) std::max<int64_t>(1, p.P)
                       : pick_nt(p.P, p.n_as);
     p.planes = planes_bytes(p.n_b * p.T, p.K, p.vdt == QWB_TYPE_Q8_K);
@@ -523,7 +523,7 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
     }
     profile_mark(s, QWB_KERNEL_OTHER);
     if (p.pf8) {
-        Q8PrefillArgs q{};
+        I8PrefillArgs q{};
         q.W = (const uint8_t *) as->data;
         q.nb1 = as->nb[1];
         q.nb2 = as->nb[2];
@@ -531,7 +531,7 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
         q.K = p.K;
         q.n_as = p.n_as;
         q.act = pl;
-        q.act_dstride = (int) plane_d_stride(p.K, QK8_0);
+        q.act_dstride = (int) plane_d_stride(p.K, kq ? QK_K : QK8_0);
         q.tiles = ix.tiles;
         q.n_tiles = ix.n_tiles;
         q.pairs = ix.pairs;
@@ -542,7 +542,7 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
         q.dnb2 = dst->nb[2];
         q.work = ix.work + 2;
         q.st = st;
-        e = launch_pf_q80(q, s);
+        e = launch_pf_i8(p.type, q, s);
         profile_mark(s, QWB_KERNEL_GROUPED_GEMM);
         return e == cudaSuccess ? QWB_OK : QWB_ERR_CUDA;
     }

@@ -1,8 +1,9 @@
-"""GPU parity: MUL_MAT_ID on Q8_0 experts with many tokens per expert, the integer
-tensor-core kernel (mma.sync s8 x s8 -> s32, one MMA per 32-element block, fp32 block
-scaling in block order), against the oracle's Q8_0 x Q8_0 dots (activations quantized
-with the CPU backend's Q8_0 variant), against the reference's own ggml CPU backend under
-skewed routing, and against the weight-streaming path on the same inputs.
+"""GPU parity: MUL_MAT_ID on Q8_0 and Q6_K experts with many tokens per expert, the
+integer tensor-core kernel (mma.sync s8 x s8 -> s32: one m16n8k32 per Q8_0 block with fp32
+block scaling in block order; one m16n8k16 per Q6_K sub-block with its int8 scale in
+int32 and fp32 scaling per superblock), against the oracle's dots (activations quantized
+as the CPU backend does: Q8_0 CPU variant / Q8_K), against the reference's own ggml CPU
+backend under skewed routing, and against the weight-streaming path on the same inputs.
 Bar: nRMS <= 1e-4 (max abs-rel error in the message)."""
 import ctypes as C
 
@@ -61,53 +62,58 @@ def _stream(q, W, b, ids):
 
 
 CASES = [
-    # K, M, n_as, T, n_used, n_b
-    (1024, 300, 8, 256, 4, 1),      # rows not a multiple of 128, partial token tiles
-    (2048, 768, 16, 512, 8, 1),     # gate/up-like
-    (512, 2048, 8, 128, 4, 4),      # down-like: one activation row per (token, slot)
-    (4096, 128, 8, 64, 8, 8),       # long K, one activation row per (token, slot)
+    # type, K, M, n_as, T, n_used, n_b
+    (O.Q8_0, 1024, 300, 8, 256, 4, 1),      # rows not a multiple of 128, partial token tiles
+    (O.Q8_0, 2048, 768, 16, 512, 8, 1),     # gate/up-like
+    (O.Q8_0, 512, 2048, 8, 128, 4, 4),      # down-like: one activation row per (token, slot)
+    (O.Q8_0, 4096, 128, 8, 64, 8, 8),       # long K, one activation row per (token, slot)
+    (O.Q6_K, 768, 2048, 8, 128, 4, 4),      # config-2 down shape
+    (O.Q6_K, 1024, 300, 8, 256, 4, 1),
+    (O.Q6_K, 2048, 128, 8, 64, 8, 8),
 ]
 
 
-@pytest.mark.parametrize("K,M,n_as,T,n_used,n_b", CASES)
-def test_uniform_routing(qwb, K, M, n_as, T, n_used, n_b):
-    w = D.weights(O.Q8_0, n_as, M, K, seed=K + M + T)
+@pytest.mark.parametrize("t,K,M,n_as,T,n_used,n_b", CASES)
+def test_uniform_routing(qwb, t, K, M, n_as, T, n_used, n_b):
+    w = D.weights(t, n_as, M, K, seed=K + M + T)
     b = D.acts((T, n_b, K), seed=T + 5)
     ids = np.stack([D.rng(200 + i).permutation(n_as)[:n_used] for i in range(T)]).astype(np.int32)
-    W = qwb.QTensor.from_bytes(w, O.Q8_0, (K, M, n_as))
+    W = qwb.QTensor.from_bytes(w, t, (K, M, n_as))
     got, tags = _run(qwb, W, cu(b), cu(ids), profile=True)
     assert 5 in tags  # the tensor-core kernel ran (QWB_KERNEL_GROUPED_GEMM)
     flags, _, _ = qwb.read_status()
     assert flags == 0
-    want, rc = O.mul_mat_id(O.Q8_0, w, K, M, n_as, b, ids)
+    want, rc = O.mul_mat_id(t, w, K, M, n_as, b, ids)
     assert rc == 0
     got = got.cpu().numpy()
     e = O.nrmse(got, want)
     assert e <= TOL, (e, O.max_abs_rel(got, want))
 
 
-def test_zipf_routing_against_reference_build(qwb):
+@pytest.mark.parametrize("t", [O.Q8_0, O.Q6_K])
+def test_zipf_routing_against_reference_build(qwb, t):
     K, M, n_as, T, n_used = 1024, 256, 64, 512, 8
-    w = D.weights(O.Q8_0, n_as, M, K, seed=31)
+    w = D.weights(t, n_as, M, K, seed=31)
     b = D.acts((T, 1, K), seed=32)
     ids = D.zipf_ids(T, n_as, n_used, seed=33)
-    W = qwb.QTensor.from_bytes(w, O.Q8_0, (K, M, n_as))
+    W = qwb.QTensor.from_bytes(w, t, (K, M, n_as))
     got = _run(qwb, W, cu(b), cu(ids))[0].cpu().numpy()
     if O.ref_available():
         O.set_ref_threads(8)
-        want, _ = O.mul_mat_id(O.Q8_0, w, K, M, n_as, b, ids, impl="ref")
+        want, _ = O.mul_mat_id(t, w, K, M, n_as, b, ids, impl="ref")
     else:
-        want, _ = O.mul_mat_id(O.Q8_0, w, K, M, n_as, b, ids)
+        want, _ = O.mul_mat_id(t, w, K, M, n_as, b, ids)
     e = O.nrmse(got, want)
     assert e <= TOL, (e, O.max_abs_rel(got, want))
 
 
-def test_matches_streaming_path(qwb):
+@pytest.mark.parametrize("t", [O.Q8_0, O.Q6_K])
+def test_matches_streaming_path(qwb, t):
     K, M, n_as, T, n_used = 1024, 384, 8, 160, 8
-    w = D.weights(O.Q8_0, n_as, M, K, seed=51)
+    w = D.weights(t, n_as, M, K, seed=51)
     b = cu(D.acts((T, 1, K), seed=52))
     ids = cu(np.stack([D.rng(53 + i).permutation(n_as)[:n_used] for i in range(T)]).astype(np.int32))
-    W = qwb.QTensor.from_bytes(w, O.Q8_0, (K, M, n_as))
+    W = qwb.QTensor.from_bytes(w, t, (K, M, n_as))
     tc = _run(qwb, W, b, ids)[0]
     st = _stream(qwb, W, b, ids)
     # the same per-block fp32 products; only the summation order of blocks vs passes differs
