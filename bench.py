@@ -675,6 +675,8 @@ def main():
     ap.add_argument("--no-mmid", action="store_true", help="skip the decode-batch MUL_MAT_ID (config 4) sweep")
     ap.add_argument("--no-gathers", action="store_true",
                     help="skip the GET_ROWS (config 5) and output-head (config 2) measurements")
+    ap.add_argument("--only-prefill", action="store_true",
+                    help="run only the prefill (config 3) sweep, without its CPU baseline (profiling runs)")
     ap.add_argument("--only-mmid", action="store_true",
                     help="run only the decode-batch MUL_MAT_ID sweep and print its JSON (profiling runs)")
     ap.add_argument("--mmid-tokens", default=",".join(str(t) for t in MMID_TOKENS),
@@ -703,6 +705,9 @@ def main():
     mmid_tokens = tuple(int(t) for t in args.mmid_tokens.split(","))
     if args.only_mmid:
         print(json.dumps({"decode_mmid": decode_mmid_sweep(q, lib, torch.device("cuda", local), mmid_tokens, args.mmid_pools)}))
+        return
+    if args.only_prefill:
+        print(json.dumps({"prefill": prefill_sweep(q, lib, torch.device("cuda", local), args.warmup, 10, cpu=False)}))
         return
 
     # ---------------------------------------------------------------- weights
