@@ -21,6 +21,13 @@
 //   * the raw blocks are repacked into int8 codes in a bank-padded layout (272-byte row
 //     stride) for ldmatrix, with fp32 (and, for Q6_K, int8 sub-block) scales;
 //   * the MMAs of the step, each followed by its scale epilogue.
+// Q8_0 block scaling without an int -> float conversion instruction: each MMA adds the
+// integer dot to the accumulator input 0x4B400000, the bit pattern of 1.5 * 2^23, so the
+// int32 result read as a float is exactly 12582912 + isum (|isum| <= 32 * 128 * 127 <
+// 2^22 keeps it in [2^23, 2^24), where floats are the consecutive integers).  Then
+// t = fma(y, d_a, -12582912 * d_a) = round(isum * d_a): y * d_a is exact inside the fma
+// and 12582912 * d_a is exact in fp32 (d_a comes from fp16: 11 significant bits, times
+// the 2 bits of 3 * 2^22), and acc = fma(t, d_w, acc).
 #include <algorithm>
 
 #include "common.cuh"
@@ -42,9 +49,13 @@ template <int TYPE>
 struct I8Geo {
     static constexpr bool q6 = TYPE == QWB_TYPE_Q6_K;
     static constexpr int raw = q6 ? 240 : 272;  // raw bytes staged per row per step
-    static constexpr int ndw = q6 ? 1 : 8;      // fp32 weight scales per row per step
+    static constexpr int ndw = 1;               // Q6_K: fp32 weight scale per row per step
     static constexpr int nda = q6 ? 4 : 8;      // activation scale floats staged per token per step
+    static constexpr int nj = q6 ? 1 : 8;       // Q8_0: blocks per row per step (repacked scales)
 };
+
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23, bit pattern 0x4B400000
+constexpr int kMagicBits = 0x4B400000;
 
 template <int TYPE>
 struct I8Smem {
@@ -52,6 +63,11 @@ struct I8Smem {
     uint8_t wq[kI8TM][kI8Row];                // repacked int8 codes
     uint8_t aq[2][kI8TN][kI8Row];             // activation codes (cp.async from the planes)
     float dw[kI8TM][I8Geo<TYPE>::ndw];        // weight scales of the step
+    // Q8_0: weight scales of block j for the rows one lane reads, (g, g+8, g+16, g+24) of its
+    // warp's 32 rows; and activation scales of token pair k (tokens 2k, 2k+1) of block j as
+    // {d(2k), d(2k+1), -kMagic d(2k), -kMagic d(2k+1)} (stride 33 pairs: no bank conflicts)
+    float dwp[I8Geo<TYPE>::nj][4][8][4];
+    float dap[I8Geo<TYPE>::nj][I8Geo<TYPE>::q6 ? 1 : kI8TN / 2 + 1][4];
     int sc[I8Geo<TYPE>::q6 ? kI8TM : 1][16];  // Q6_K sub-block scales of the step
     float da[2][kI8TN][I8Geo<TYPE>::nda];     // activation scales (cp.async)
     int off[2][kI8TM];                        // Q6_K: offset of the superblock in its raw row
@@ -75,13 +91,13 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r
                  : "r"(addr));
 }
 
-// one 32-element block (m16n8k32) of A = {a0..a3} and B = {b0, b1}
-__device__ __forceinline__ void mma_k32(int *c, const uint32_t *a, uint32_t b0, uint32_t b1) {
+// one 32-element block (m16n8k32) of A = {a0..a3} and B = {b0, b1}, added to `bias`
+__device__ __forceinline__ void mma_k32(int *c, const uint32_t *a, uint32_t b0, uint32_t b1, int bias) {
     asm volatile(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%11,%12,%13};"
+        "{%10,%10,%10,%10};"
         : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(bias));
 }
 // one 16-element sub-block (m16n8k16) of A = {a0, a1} and B = {b0}
 __device__ __forceinline__ void mma_k16(int *c, uint32_t a0, uint32_t a1, uint32_t b0) {
@@ -141,14 +157,22 @@ __device__ __forceinline__ void i8_repack(I8Smem<TYPE> &S, int buf, int tid) {
         const uint8_t *src = S.raw[buf][r] + 136 * half;  // 4 blocks of 34 B
         uint8_t *dst = S.wq[r] + 128 * half;
 #pragma unroll
+        // row r = 32 wm + 16 mi + 8 h + g is slot 2 mi + h of lane group g in warp row wm
+        const int wm = r >> 5, g = r & 7, slot = ((r >> 3) & 3);
         for (int b = 0; b < 4; ++b) {
             const uint8_t *blk = src + 34 * b;  // 2-byte aligned
-            S.dw[r][4 * half + b] = h2f(*(const uint16_t *) blk);
+            S.dwp[4 * half + b][wm][g][slot] = h2f(*(const uint16_t *) blk);
             uint32_t w[8];
             lds_words8_a2(blk + 2, w);
             uint4 *d4 = (uint4 *) (dst + 32 * b);
             d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
             d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+        // activation scales of token pair k, block j (8 threads per pair)
+        {
+            const int k = tid >> 3, j = tid & 7;
+            const float d0 = S.da[buf][2 * k][j], d1 = S.da[buf][2 * k + 1][j];
+            *(float4 *) &S.dap[j][k][0] = make_float4(d0, d1, -kMagic * d0, -kMagic * d1);
         }
     } else {
         // Q6_K superblock: ql[128] qh[64] sc[16] d; element 128*hf + 32*i + l has ql nibble
@@ -273,30 +297,24 @@ __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArg
                             bf[2 * np + 1][1]);
                 }
                 if constexpr (TYPE == QWB_TYPE_Q8_0) {
-                    float dwr[2][2], dat[4][2];
+                    // {row g, g+8} of mi 0, then of mi 1; per ni {d(tok), d(tok+1), -M d(tok), -M d(tok+1)}
+                    const float4 dw4 = *(const float4 *) &S.dwp[j][wm][lane >> 2][0];
+                    float4 da4[4];
+#pragma unroll
+                    for (int ni = 0; ni < 4; ++ni) da4[ni] = *(const float4 *) &S.dap[j][16 * wn + 4 * ni + (lane & 3)][0];
 #pragma unroll
                     for (int mi = 0; mi < 2; ++mi) {
-                        const int row = 32 * wm + 16 * mi + (lane >> 2);
-                        dwr[mi][0] = S.dw[row][j];
-                        dwr[mi][1] = S.dw[row + 8][j];
-                    }
-#pragma unroll
-                    for (int ni = 0; ni < 4; ++ni) {
-                        const int tok = 32 * wn + 8 * ni + 2 * (lane & 3);
-                        dat[ni][0] = S.da[buf][tok][j];
-                        dat[ni][1] = S.da[buf][tok + 1][j];
-                    }
-#pragma unroll
-                    for (int mi = 0; mi < 2; ++mi) {
+                        const float w0 = mi ? dw4.z : dw4.x, w1 = mi ? dw4.w : dw4.y;
 #pragma unroll
                         for (int ni = 0; ni < 4; ++ni) {
                             int c[4];
-                            mma_k32(c, af[mi], bf[ni][0], bf[ni][1]);
+                            mma_k32(c, af[mi], bf[ni][0], bf[ni][1], kMagicBits);
                             // c0: (row g, tok 2q), c1: (g, 2q+1), c2: (g+8, 2q), c3: (g+8, 2q+1)
-                            acc[mi][ni][0] += (float) c[0] * __fmul_rn(dwr[mi][0], dat[ni][0]);
-                            acc[mi][ni][1] += (float) c[1] * __fmul_rn(dwr[mi][0], dat[ni][1]);
-                            acc[mi][ni][2] += (float) c[2] * __fmul_rn(dwr[mi][1], dat[ni][0]);
-                            acc[mi][ni][3] += (float) c[3] * __fmul_rn(dwr[mi][1], dat[ni][1]);
+                            const float4 d = da4[ni];
+                            acc[mi][ni][0] = __fmaf_rn(__fmaf_rn(__int_as_float(c[0]), d.x, d.z), w0, acc[mi][ni][0]);
+                            acc[mi][ni][1] = __fmaf_rn(__fmaf_rn(__int_as_float(c[1]), d.y, d.w), w0, acc[mi][ni][1]);
+                            acc[mi][ni][2] = __fmaf_rn(__fmaf_rn(__int_as_float(c[2]), d.x, d.z), w1, acc[mi][ni][2]);
+                            acc[mi][ni][3] = __fmaf_rn(__fmaf_rn(__int_as_float(c[3]), d.y, d.w), w1, acc[mi][ni][3]);
                         }
                     }
                 } else {
