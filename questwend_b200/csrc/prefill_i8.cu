@@ -57,24 +57,30 @@ struct I8Geo {
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23, bit pattern 0x4B400000
 constexpr int kMagicBits = 0x4B400000;
 
+// Pipeline slots of K step ks: copies land in raw / off [ks & 1] and aq / da [ks % 3]; the
+// repack writes wq / dw / dwp / dap / sc [ks & 1].  In the iteration of step ks the MMAs
+// read step ks while the repack writes step ks + 1 and the copies of step ks + 2 land.
 template <int TYPE>
 struct I8Smem {
     uint8_t raw[2][kI8TM][I8Geo<TYPE>::raw];  // raw weight bytes (cp.async)
-    uint8_t wq[kI8TM][kI8Row];                // repacked int8 codes
-    uint8_t aq[2][kI8TN][kI8Row];             // activation codes (cp.async from the planes)
-    float dw[kI8TM][I8Geo<TYPE>::ndw];        // weight scales of the step
+    uint8_t wq[2][kI8TM][kI8Row];             // repacked int8 codes
+    uint8_t aq[3][kI8TN][kI8Row];             // activation codes (cp.async from the planes)
+    float dw[2][kI8TM][I8Geo<TYPE>::ndw];     // Q6_K: weight scale of the step
     // Q8_0: weight scales of block j for the rows one lane reads, (g, g+8, g+16, g+24) of its
     // warp's 32 rows; and activation scales of token pair k (tokens 2k, 2k+1) of block j as
     // {d(2k), d(2k+1), -kMagic d(2k), -kMagic d(2k+1)} (stride 33 pairs: no bank conflicts)
-    float dwp[I8Geo<TYPE>::nj][4][8][4];
-    float dap[I8Geo<TYPE>::nj][I8Geo<TYPE>::q6 ? 1 : kI8TN / 2 + 1][4];
-    int sc[I8Geo<TYPE>::q6 ? kI8TM : 1][16];  // Q6_K sub-block scales of the step
-    float da[2][kI8TN][I8Geo<TYPE>::nda];     // activation scales (cp.async)
-    int off[2][kI8TM];                        // Q6_K: offset of the superblock in its raw row
+    float dwp[2][I8Geo<TYPE>::nj][4][8][4];
+    float dap[2][I8Geo<TYPE>::nj][I8Geo<TYPE>::q6 ? 1 : kI8TN / 2 + 1][4];
+    int sc[2][I8Geo<TYPE>::q6 ? kI8TM : 1][16];  // Q6_K sub-block scales of the step
+    float da[3][kI8TN][I8Geo<TYPE>::nda];        // activation scales (cp.async)
+    int off[2][kI8TM];                           // Q6_K: offset of the superblock in its raw row
     long long tok_o[kI8TN];                   // output byte offset of each pair
     int tok_ar[kI8TN];                        // activation plane row of each pair
     int item;
 };
+
+static_assert(sizeof(I8Smem<QWB_TYPE_Q8_0>) <= 232448 && sizeof(I8Smem<QWB_TYPE_Q6_K>) <= 232448,
+              "one CTA per SM: at most 227 KB of shared memory");
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
@@ -107,12 +113,13 @@ __device__ __forceinline__ void mma_k16(int *c, uint32_t a0, uint32_t a1, uint32
         : "r"(a0), "r"(a1), "r"(b0), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
-// Issue the copies of K step `ks` of the current item into buffer `buf`.
+// Issue the copies of K step `ks` of the current item into its slots.
 template <int TYPE>
-__device__ __forceinline__ void i8_issue(const I8PrefillArgs &a, I8Smem<TYPE> &S, int buf, int ks,
-                                         const uint8_t *wbase, int nrows, int ntok) {
+__device__ __forceinline__ void i8_issue(const I8PrefillArgs &a, I8Smem<TYPE> &S, int ks, const uint8_t *wbase,
+                                         int nrows, int ntok) {
     using G = I8Geo<TYPE>;
     const int tid = threadIdx.x;
+    const int buf = ks & 1, b3 = ks % 3;
     constexpr int pieces = G::raw / 16;
     for (int i = tid; i < kI8TM * pieces; i += kI8Threads) {
         const int r = i / pieces, c = i - r * pieces;
@@ -138,30 +145,31 @@ __device__ __forceinline__ void i8_issue(const I8PrefillArgs &a, I8Smem<TYPE> &S
         const bool ok = k < ntok;
         const int64_t ar = ok ? S.tok_ar[k] : 0;
         if (c < 16) {
-            cp_async16(&S.aq[buf][k][16 * c], a.act.qs + ar * a.K + (int64_t) ks * kI8KS + 16 * c, ok);
+            cp_async16(&S.aq[b3][k][16 * c], a.act.qs + ar * a.K + (int64_t) ks * kI8KS + 16 * c, ok);
         } else if constexpr (G::q6) {
             // one scale per superblock: the 16-byte group of 4 holding it
-            cp_async16(&S.da[buf][k][0], a.act.d + ar * a.act_dstride + (ks & ~3), ok);
+            cp_async16(&S.da[b3][k][0], a.act.d + ar * a.act_dstride + (ks & ~3), ok);
         } else {
-            cp_async16(&S.da[buf][k][4 * (c - 16)], a.act.d + ar * a.act_dstride + (int64_t) ks * 8 + 4 * (c - 16), ok);
+            cp_async16(&S.da[b3][k][4 * (c - 16)], a.act.d + ar * a.act_dstride + (int64_t) ks * 8 + 4 * (c - 16), ok);
         }
     }
     cp_async_commit();
 }
 
-// Repack row r's raw step bytes (two threads per row) into int8 codes + scales.
+// Repack row r's raw bytes of step ks (two threads per row) into int8 codes + scales.
 template <int TYPE>
-__device__ __forceinline__ void i8_repack(I8Smem<TYPE> &S, int buf, int tid) {
+__device__ __forceinline__ void i8_repack(I8Smem<TYPE> &S, int ks, int tid) {
     const int r = tid >> 1, half = tid & 1;
+    const int buf = ks & 1, b3 = ks % 3;
     if constexpr (TYPE == QWB_TYPE_Q8_0) {
         const uint8_t *src = S.raw[buf][r] + 136 * half;  // 4 blocks of 34 B
-        uint8_t *dst = S.wq[r] + 128 * half;
-#pragma unroll
+        uint8_t *dst = S.wq[buf][r] + 128 * half;
         // row r = 32 wm + 16 mi + 8 h + g is slot 2 mi + h of lane group g in warp row wm
         const int wm = r >> 5, g = r & 7, slot = ((r >> 3) & 3);
+#pragma unroll
         for (int b = 0; b < 4; ++b) {
             const uint8_t *blk = src + 34 * b;  // 2-byte aligned
-            S.dwp[4 * half + b][wm][g][slot] = h2f(*(const uint16_t *) blk);
+            S.dwp[buf][4 * half + b][wm][g][slot] = h2f(*(const uint16_t *) blk);
             uint32_t w[8];
             lds_words8_a2(blk + 2, w);
             uint4 *d4 = (uint4 *) (dst + 32 * b);
@@ -171,8 +179,8 @@ __device__ __forceinline__ void i8_repack(I8Smem<TYPE> &S, int buf, int tid) {
         // activation scales of token pair k, block j (8 threads per pair)
         {
             const int k = tid >> 3, j = tid & 7;
-            const float d0 = S.da[buf][2 * k][j], d1 = S.da[buf][2 * k + 1][j];
-            *(float4 *) &S.dap[j][k][0] = make_float4(d0, d1, -kMagic * d0, -kMagic * d1);
+            const float d0 = S.da[b3][2 * k][j], d1 = S.da[b3][2 * k + 1][j];
+            *(float4 *) &S.dap[buf][j][k][0] = make_float4(d0, d1, -kMagic * d0, -kMagic * d1);
         }
     } else {
         // Q6_K superblock: ql[128] qh[64] sc[16] d; element 128*hf + 32*i + l has ql nibble
@@ -183,7 +191,7 @@ __device__ __forceinline__ void i8_repack(I8Smem<TYPE> &S, int buf, int tid) {
         lds_words8_a2(sb + 64 * hf, qa);
         lds_words8_a2(sb + 64 * hf + 32, qb);
         lds_words8_a2(sb + 128 + 32 * hf, qh);
-        uint8_t *dst = S.wq[r] + 128 * hf;
+        uint8_t *dst = S.wq[buf][r] + 128 * hf;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             uint32_t w[8];
@@ -199,8 +207,8 @@ __device__ __forceinline__ void i8_repack(I8Smem<TYPE> &S, int buf, int tid) {
         }
         const int8_t *scp = (const int8_t *) (sb + 192) + 8 * hf;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) S.sc[r][8 * hf + j] = scp[j];
-        if (hf == 0) S.dw[r][0] = h2f(*(const uint16_t *) (sb + 208));
+        for (int j = 0; j < 8; ++j) S.sc[buf][r][8 * hf + j] = scp[j];
+        if (hf == 0) S.dw[buf][r][0] = h2f(*(const uint16_t *) (sb + 208));
     }
 }
 
@@ -259,19 +267,25 @@ __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArg
 #pragma unroll
                 for (int v = 0; v < 4; ++v) acc[mi][ni][v] = 0.f;
 
-        i8_issue<TYPE>(a, S, 0, 0, wbase, nrows, ntok);
+        // prologue: steps 0 and 1 in flight, step 0 repacked
+        i8_issue<TYPE>(a, S, 0, wbase, nrows, ntok);
+        if (nks > 1) {
+            i8_issue<TYPE>(a, S, 1, wbase, nrows, ntok);
+            cp_async_wait1();
+        } else {
+            cp_async_wait0();
+        }
+        __syncthreads();  // step 0 has landed for every thread
+        i8_repack<TYPE>(S, 0, tid);
         for (int ks = 0; ks < nks; ++ks) {
-            const int buf = ks & 1;
-            if (ks + 1 < nks) {
-                i8_issue<TYPE>(a, S, buf ^ 1, ks + 1, wbase, nrows, ntok);
-                cp_async_wait1();
-            } else {
-                cp_async_wait0();
-            }
-            __syncthreads();  // step ks has landed for every thread
-            i8_repack<TYPE>(S, buf, tid);
+            const int buf = ks & 1, b3 = ks % 3;
+            if (ks + 1 < nks) cp_async_wait0();  // this thread's copies of step ks + 1
+            // One barrier per step: step ks + 1 has landed, step ks is repacked, and the
+            // MMAs of step ks - 1 are done, so its slots may be refilled / rewritten.
             __syncthreads();
-            const uint32_t wq_base = smem_u32(&S.wq[0][0]), aq_base = smem_u32(&S.aq[buf][0][0]);
+            if (ks + 2 < nks) i8_issue<TYPE>(a, S, ks + 2, wbase, nrows, ntok);
+            if (ks + 1 < nks) i8_repack<TYPE>(S, ks + 1, tid);
+            const uint32_t wq_base = smem_u32(&S.wq[buf][0][0]), aq_base = smem_u32(&S.aq[b3][0][0]);
             int isum[2][4][4];  // Q6_K: integer sum of the superblock (sub-block scales applied)
 #pragma unroll
             for (int mi = 0; mi < 2; ++mi)
@@ -298,10 +312,10 @@ __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArg
                 }
                 if constexpr (TYPE == QWB_TYPE_Q8_0) {
                     // {row g, g+8} of mi 0, then of mi 1; per ni {d(tok), d(tok+1), -M d(tok), -M d(tok+1)}
-                    const float4 dw4 = *(const float4 *) &S.dwp[j][wm][lane >> 2][0];
+                    const float4 dw4 = *(const float4 *) &S.dwp[buf][j][wm][lane >> 2][0];
                     float4 da4[4];
 #pragma unroll
-                    for (int ni = 0; ni < 4; ++ni) da4[ni] = *(const float4 *) &S.dap[j][16 * wn + 4 * ni + (lane & 3)][0];
+                    for (int ni = 0; ni < 4; ++ni) da4[ni] = *(const float4 *) &S.dap[buf][j][16 * wn + 4 * ni + (lane & 3)][0];
 #pragma unroll
                     for (int mi = 0; mi < 2; ++mi) {
                         const float w0 = mi ? dw4.z : dw4.x, w1 = mi ? dw4.w : dw4.y;
@@ -323,10 +337,10 @@ __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArg
 #pragma unroll
                     for (int mi = 0; mi < 2; ++mi) {
                         const int row = 32 * wm + 16 * mi + (lane >> 2);
-                        scr[mi][0][0] = S.sc[row][2 * j];
-                        scr[mi][0][1] = S.sc[row][2 * j + 1];
-                        scr[mi][1][0] = S.sc[row + 8][2 * j];
-                        scr[mi][1][1] = S.sc[row + 8][2 * j + 1];
+                        scr[mi][0][0] = S.sc[buf][row][2 * j];
+                        scr[mi][0][1] = S.sc[buf][row][2 * j + 1];
+                        scr[mi][1][0] = S.sc[buf][row + 8][2 * j];
+                        scr[mi][1][1] = S.sc[buf][row + 8][2 * j + 1];
                     }
 #pragma unroll
                     for (int mi = 0; mi < 2; ++mi) {
@@ -350,11 +364,11 @@ __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArg
 #pragma unroll
                 for (int mi = 0; mi < 2; ++mi) {
                     const int row = 32 * wm + 16 * mi + (lane >> 2);
-                    const float dw0 = S.dw[row][0], dw1 = S.dw[row + 8][0];
+                    const float dw0 = S.dw[buf][row][0], dw1 = S.dw[buf][row + 8][0];
 #pragma unroll
                     for (int ni = 0; ni < 4; ++ni) {
                         const int tok = 32 * wn + 8 * ni + 2 * (lane & 3);
-                        const float da0 = S.da[buf][tok][ks & 3], da1 = S.da[buf][tok + 1][ks & 3];
+                        const float da0 = S.da[b3][tok][ks & 3], da1 = S.da[b3][tok + 1][ks & 3];
                         acc[mi][ni][0] += __fmul_rn(dw0, da0) * (float) isum[mi][ni][0];
                         acc[mi][ni][1] += __fmul_rn(dw0, da1) * (float) isum[mi][ni][1];
                         acc[mi][ni][2] += __fmul_rn(dw1, da0) * (float) isum[mi][ni][2];
@@ -362,7 +376,6 @@ __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArg
                     }
                 }
             }
-            __syncthreads();  // wq and this step's buffers are free again
         }
         // outputs: dst[row] of each (token, slot) pair
 #pragma unroll
