@@ -414,6 +414,95 @@ def gathers_sweep(q, dev):
     return out
 
 
+def slab_sweep(q, dev, iters=20):
+    """Expert pool writes: the expert cache's slab uploads (core/expert_cache.cpp:637-723,
+    :1357-1377) for one config-2 layer group, 8 experts x (gate, up: 884,736 B Q4_K; down:
+    1,290,240 B Q6_K) = 24 slabs of 24.5 MB, from one page-locked staging buffer into random
+    slots of three 64-slot pools (qwb_pool_write_slabs, one call per pool).  GB/s of slab
+    bytes, against one plain host-to-device copy of the same staging buffer measured in the
+    same run (the host link's copy rate).  Then the device byte audit of the 24 slots
+    (qwb_pool_audit_slabs), compare only and with the FNV-1a 64 checksums (a diagnostic
+    whose serial chains take milliseconds).  The audit times include the ctypes calls."""
+    import ctypes as C
+
+    import torch
+
+    from questwend_b200 import _lib as L
+    lib = q.lib()
+    rng = np.random.default_rng(11)
+    roles = ((Q4_K, H, F), (Q4_K, H, F), (Q6_K, F, H))
+    slab = [q.ops.row_size(t, k) * m for t, k, m in roles]
+    n_slots, n_exp = 64, K_USED
+    pools = [q.QTensor(torch.zeros(n_slots * sb, dtype=torch.uint8, device=dev), t, (k, m, n_slots, 1))
+             for (t, k, m), sb in zip(roles, slab)]
+    group = sum(slab) * n_exp
+    stage = torch.from_numpy(np.concatenate([synth_blocks(t, m, k, rng) for t, k, m in roles] * n_exp)).pin_memory()
+    assert stage.numel() == group
+    # staging order: expert-major (gate, up, down of expert 0, then expert 1, ...)
+    offs = np.cumsum([0] + [sb for _ in range(n_exp) for sb in slab])[:-1].reshape(n_exp, 3)
+    descs = [p.desc() for p in pools]
+    calls = []
+    for it in range(iters + 3):
+        per_pool = []
+        for r in range(3):
+            slots = rng.choice(n_slots, n_exp, replace=False)
+            arr = (L.SlabCopy * n_exp)()
+            for e in range(n_exp):
+                arr[e].src = stage.data_ptr() + int(offs[e, r])
+                arr[e].slot = int(slots[e])
+            per_pool.append((arr, slots))
+        calls.append(per_pool)
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def upload(i):
+        for r in range(3):
+            L.check("qwb_pool_write_slabs", lib.qwb_pool_write_slabs(C.byref(descs[r]), slab[r], calls[i][r][0],
+                                                                     n_exp, stream))
+    for i in range(3):
+        upload(i)
+    dst = torch.empty(group, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        dst.copy_(stage, non_blocking=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(3, iters + 3):
+        upload(i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    e0.record()
+    for _ in range(iters):
+        dst.copy_(stage, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    ms_link = e0.elapsed_time(e1) / iters
+    # every written slot holds its staged slab (last iteration)
+    last = calls[iters + 2]
+    for r in range(3):
+        got = pools[r].data.view(n_slots, slab[r])[torch.from_numpy(last[r][1]).to(dev)]
+        want = torch.stack([stage[int(offs[e, r]):int(offs[e, r]) + slab[r]] for e in range(n_exp)]).to(dev)
+        assert torch.equal(got, want)
+    # device byte audit of the 24 slots against the staging buffer (page-locked host memory):
+    # compare only, then with both FNV-1a 64 checksums
+    audit_ms = []
+    for sums in (False, True):
+        e0.record()
+        audits = [q.pool_audit_slabs(pools[r], [stage.data_ptr() + int(offs[e, r]) for e in range(n_exp)],
+                                     last[r][1], checksums=sums) for r in range(3)]
+        e1.record()
+        torch.cuda.synchronize()
+        assert all(a["equal"] for rec in audits for a in rec)
+        audit_ms.append(e0.elapsed_time(e1))
+    link = group / (ms_link * 1e-3) / 1e9
+    return {"config": {"workload": "C2 layer group: 8 experts x (gate, up Q4_K, down Q6_K) slabs",
+                       "slabs": 3 * n_exp, "bytes": group, "pool_slots": n_slots,
+                       "source": "one page-locked staging buffer"},
+            "ms": ms, "gbs": group / (ms * 1e-3) / 1e9, "link_gbs": link,
+            "frac_of_link": (group / (ms * 1e-3) / 1e9) / link,
+            "audit_compare_ms": audit_ms[0], "audit_checksums_ms": audit_ms[1], "audit_equal": True}
+
+
 def prefill_sweep(q, lib, dev, warmup, iters, cpu):
     import ctypes as C
 
@@ -675,6 +764,7 @@ def main():
     ap.add_argument("--no-mmid", action="store_true", help="skip the decode-batch MUL_MAT_ID (config 4) sweep")
     ap.add_argument("--no-gathers", action="store_true",
                     help="skip the GET_ROWS (config 5) and output-head (config 2) measurements")
+    ap.add_argument("--no-slabs", action="store_true", help="skip the expert pool write (slab upload) measurement")
     ap.add_argument("--only-prefill", action="store_true",
                     help="run only the prefill (config 3) sweep, without its CPU baseline (profiling runs)")
     ap.add_argument("--only-mmid", action="store_true",
@@ -878,6 +968,8 @@ def main():
         result["decode_mmid"] = decode_mmid_sweep(q, lib, dev, mmid_tokens, args.mmid_pools)
     if rank == 0 and not args.no_gathers:
         result["gathers"] = gathers_sweep(q, dev)
+    if rank == 0 and not args.no_slabs:
+        result["slab_upload"] = slab_sweep(q, dev)
     if rank == 0:
         print(json.dumps(result))
     if world > 1:

@@ -273,6 +273,60 @@ QWB_API size_t qwb_moe_ep_experts_workspace_size(const qwb_moe_ep_experts_desc *
 QWB_API qwb_status qwb_moe_ep_experts(const qwb_moe_ep_experts_desc *desc, void *workspace, size_t workspace_bytes,
                                       qwb_status_block *d_status, qwb_stream_t stream);
 
+/* ------------------------------------------------------------- expert pool writes
+ * The expert cache keeps each role's experts in a pool tensor [ne0, ne1, n_slots] (one
+ * slab of nb[2] bytes per slot; the kernels above read it through slot ids).  A miss
+ * copies one expert's slab from host memory into a slot:
+ * ExpertCache::fetch_slab (core/expert_cache.cpp:637-723) and the group upload of
+ * fetch_parallel (:1357-1377, from a page-locked staging buffer) call
+ * ggml_backend_tensor_set(_async)(pool, src, slot * nb2, nb2) once per (role, expert),
+ * after checking that the source's nb2 equals the pool's (:643-645, "slab size mismatch").
+ *
+ * qwb_pool_write_slabs issues those copies on `stream` for n slabs of one pool: copy i
+ * writes pool->nb[2] bytes from copies[i].src into slot copies[i].slot, in array order
+ * (a slot named twice ends with the later source), one asynchronous copy per slab; odd
+ * slots are copied on a second stream of the library's, forked from `stream` and joined
+ * back into it with events, so work queued on `stream` after the call sees every slab.
+ * Sources in page-locked host memory
+ * (cudaHostAlloc / cudaHostRegister) give asynchronous DMA copies; pageable sources work
+ * but the copy is staged by the driver; device sources are device-to-device copies.
+ * Arguments are checked before the first copy is issued: src_slab_bytes must equal
+ * pool->nb[2] (QWB_ERR_SHAPE), every slot must lie in [0, pool->ne[2])
+ * (QWB_ERR_INVALID_ARG), so an error writes nothing. */
+typedef struct qwb_slab_copy {
+    const void *src; /* the slab's bytes (host or device memory) */
+    int64_t slot;    /* destination slot in the pool */
+} qwb_slab_copy;
+
+QWB_API qwb_status qwb_pool_write_slabs(const qwb_tensor *pool, size_t src_slab_bytes,
+                                        const qwb_slab_copy *copies, int n, qwb_stream_t stream);
+
+/* Byte audit of pool slots, on the device.  The reference's audit
+ * (core/expert_weight_audit.h:56-66 and :106-125, driven from
+ * core/expert_cache.cpp:1712-1731) synchronises, reads every selected slot back to the
+ * host and compares it with the authoritative bytes: equal flag, first differing byte
+ * and the FNV-1a 64 checksums of both (:82-86).  qwb_pool_audit_slabs computes the same
+ * record for n slots on the GPU, without reading the slabs back: expected[i].src holds
+ * the bytes slot expected[i].slot should contain, in device memory or page-locked host
+ * memory (read by the kernel over the host link; pageable host memory is rejected with
+ * QWB_ERR_INVALID_ARG).  results[i] (device memory, n records) is written in stream
+ * order; read it back after the stream.  checksums != 0 also computes both FNV-1a 64
+ * sums, a serial chain over every byte (milliseconds per megabyte, a diagnostic);
+ * checksums == 0 leaves them 0 and only compares, which runs at memory / host-link speed
+ * and stops at the first difference. */
+typedef struct qwb_slab_audit {
+    int32_t equal;             /* 1 when the slot holds exactly the expected bytes */
+    int32_t reserved;
+    uint64_t first_difference; /* index of the first differing byte; the slab size when equal */
+    uint32_t expected_byte;    /* the two bytes at first_difference (0 when equal) */
+    uint32_t actual_byte;
+    uint64_t expected_fnv1a64; /* FNV-1a 64 of the expected bytes (0 without checksums) */
+    uint64_t actual_fnv1a64;   /* FNV-1a 64 of the slot's bytes (0 without checksums) */
+} qwb_slab_audit;
+
+QWB_API qwb_status qwb_pool_audit_slabs(const qwb_tensor *pool, const qwb_slab_copy *expected, int n,
+                                        int checksums, qwb_slab_audit *results, qwb_stream_t stream);
+
 /* ------------------------------------------------------------- profiling hook
  * Optional per-kernel timing for benchmarks (no counterpart in the reference, whose
  * QWEN_PROF timers are host wall-clock, core/runtime.cpp:3720).  While enabled,

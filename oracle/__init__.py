@@ -80,6 +80,9 @@ def port():
         lib.qo_rms_norm_mul.argtypes = [vp, vp, f32, i64, i64, vp]
         lib.qo_fp32_to_fp16.restype = C.c_uint16
         lib.qo_fp32_to_fp16.argtypes = [f32]
+        lib.qo_fnv1a64.restype = C.c_uint64
+        lib.qo_fnv1a64.argtypes = [vp, C.c_size_t]
+        lib.qo_slab_audit.argtypes = [vp, vp, C.c_size_t] + [vp] * 6
         _port = lib
     return _port
 
@@ -348,3 +351,22 @@ def max_abs_rel(got: np.ndarray, want: np.ndarray) -> float:
     want = np.asarray(want, dtype=np.float64).ravel()
     den = np.max(np.abs(want)) if want.size else 1.0
     return float(np.max(np.abs(got - want)) / (den if den > 0 else 1.0)) if want.size else 0.0
+
+
+def fnv1a64(data: bytes | np.ndarray) -> int:
+    """FNV-1a 64 of a byte string (core/expert_weight_audit.h:83-87), C restatement."""
+    a = np.frombuffer(bytes(data), dtype=np.uint8) if not isinstance(data, np.ndarray) else np.ascontiguousarray(data, dtype=np.uint8)
+    return int(port().qo_fnv1a64(_p(a) if a.size else None, a.size))
+
+
+def slab_audit(expected: np.ndarray, actual: np.ndarray) -> dict:
+    """The byte audit record of ExpertWeightAudit::compare (core/expert_weight_audit.h:
+    106-125) for one slab, C restatement."""
+    e = np.ascontiguousarray(expected, dtype=np.uint8)
+    a = np.ascontiguousarray(actual, dtype=np.uint8)
+    assert e.size == a.size
+    eq, fd, eb, ab, fe, fa = (C.c_int32(), C.c_uint64(), C.c_uint32(), C.c_uint32(), C.c_uint64(), C.c_uint64())
+    port().qo_slab_audit(_p(e), _p(a), e.size, C.byref(eq), C.byref(fd), C.byref(eb), C.byref(ab),
+                         C.byref(fe), C.byref(fa))
+    return {"equal": eq.value, "first_difference": fd.value, "expected_byte": eb.value,
+            "actual_byte": ab.value, "expected_fnv1a64": fe.value, "actual_fnv1a64": fa.value}

@@ -734,3 +734,31 @@ void qo_rms_norm_mul(const float *x, const float *w, float eps, int64_t T, int64
         for (int64_t i = 0; i < H; ++i) y[t * H + i] = xr[i] * scale * w[i];
     }
 }
+
+/* ------------------------------------------------------------ expert pool byte audit */
+
+/* FNV-1a 64 over n bytes: core/expert_weight_audit.h:83-87 (offset basis, then per byte
+ * xor and multiply by the FNV prime, modulo 2^64). */
+uint64_t qo_fnv1a64(const uint8_t *p, size_t n) {
+    uint64_t h = 14695981039346656037ull;
+    for (size_t i = 0; i < n; ++i) {
+        h ^= p[i];
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+/* ExpertWeightAudit::compare (core/expert_weight_audit.h:106-125): memcmp equality, the
+ * first index where the bytes differ and the two bytes there, both checksums. */
+void qo_slab_audit(const uint8_t *expected, const uint8_t *actual, size_t n, int32_t *equal,
+                   uint64_t *first_difference, uint32_t *expected_byte, uint32_t *actual_byte,
+                   uint64_t *expected_fnv, uint64_t *actual_fnv) {
+    size_t first = 0;
+    while (first < n && actual[first] == expected[first]) ++first;
+    *equal = first == n;
+    *first_difference = first;
+    *expected_byte = first < n ? expected[first] : 0u;
+    *actual_byte = first < n ? actual[first] : 0u;
+    *expected_fnv = qo_fnv1a64(expected, n);
+    *actual_fnv = qo_fnv1a64(actual, n);
+}

@@ -79,6 +79,14 @@ int qo_moe_layer(const float *x, int64_t H, int64_t T,
 /* ggml_rms_norm(x, eps) * w per row of H (ggml-cpu/ops.cpp:4107-4162) */
 void qo_rms_norm_mul(const float *x, const float *w, float eps, int64_t T, int64_t H, float *y);
 
+/* Expert pool byte audit: FNV-1a 64 (core/expert_weight_audit.h:83-87) and the audit
+ * record of ExpertWeightAudit::compare (:106-125): equal flag, first differing byte (n
+ * when equal), the two bytes there, both checksums. */
+uint64_t qo_fnv1a64(const uint8_t *p, size_t n);
+void qo_slab_audit(const uint8_t *expected, const uint8_t *actual, size_t n, int32_t *equal,
+                   uint64_t *first_difference, uint32_t *expected_byte, uint32_t *actual_byte,
+                   uint64_t *expected_fnv, uint64_t *actual_fnv);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,4 +8,4 @@ if it is missing.
 from . import ops  # noqa: F401
 from ._lib import LIB_PATH, QwbError, lib  # noqa: F401
 from .ops import (QTensor, get_rows, moe_ffn, moe_route, moe_weighted_sum, mul_mat, mul_mat_id,  # noqa: F401
-                  quantize_q8_0, quantize_q8_K, read_status, swiglu)
+                  pool_audit_slabs, pool_write_slabs, quantize_q8_0, quantize_q8_K, read_status, swiglu)

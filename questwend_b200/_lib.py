@@ -70,6 +70,18 @@ _lib = None
 
 # (name, restype, argtypes) for every QWB_API symbol of include/qwb.h
 _P, _TP = C.c_void_p, C.POINTER(Tensor)
+class SlabCopy(C.Structure):
+    """struct qwb_slab_copy: a slab's bytes and its pool slot."""
+    _fields_ = [("src", C.c_void_p), ("slot", C.c_int64)]
+
+
+class SlabAudit(C.Structure):
+    """struct qwb_slab_audit: the byte audit record of one pool slot."""
+    _fields_ = [("equal", C.c_int32), ("reserved", C.c_int32), ("first_difference", C.c_uint64),
+                ("expected_byte", C.c_uint32), ("actual_byte", C.c_uint32),
+                ("expected_fnv1a64", C.c_uint64), ("actual_fnv1a64", C.c_uint64)]
+
+
 SIGNATURES = [
     ("qwb_abi_version", C.c_int, []),
     ("qwb_status_string", C.c_char_p, [C.c_int]),
@@ -91,6 +103,8 @@ SIGNATURES = [
     ("qwb_moe_ep_prepare", C.c_int, [C.POINTER(MoeEpPrepareDesc), _P, C.c_size_t, _P, _P]),
     ("qwb_moe_ep_experts_workspace_size", C.c_size_t, [C.POINTER(MoeEpExpertsDesc)]),
     ("qwb_moe_ep_experts", C.c_int, [C.POINTER(MoeEpExpertsDesc), _P, C.c_size_t, _P, _P]),
+    ("qwb_pool_write_slabs", C.c_int, [_TP, C.c_size_t, C.POINTER(SlabCopy), C.c_int, _P]),
+    ("qwb_pool_audit_slabs", C.c_int, [_TP, C.POINTER(SlabCopy), C.c_int, C.c_int, _P, _P]),
     ("qwb_profile_enable", C.c_int, [C.c_int]),
     ("qwb_profile_reset", C.c_int, []),
     ("qwb_profile_count", C.c_int, []),

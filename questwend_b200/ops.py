@@ -341,3 +341,58 @@ def moe_ep_experts(xq, selected, weights, gate: QTensor, up: QTensor, down: QTen
     L.check("qwb_moe_ep_experts", lib.qwb_moe_ep_experts(C.byref(d), _ws_ptr(ws), ws.numel(),
                                                          status_block().data_ptr(), _stream()))
     return out
+
+
+# ------------------------------------------------------------------ expert pool writes
+def _slab_ptr(x) -> int:
+    if isinstance(x, torch.Tensor):
+        if not x.is_contiguous():
+            raise ValueError("slab sources must be contiguous")
+        return x.data_ptr()
+    return int(x)
+
+
+def _slab_copies(srcs, slots):
+    if len(srcs) != len(slots):
+        raise ValueError("one slot per slab")
+    arr = (L.SlabCopy * max(len(srcs), 1))()
+    for i, (src, slot) in enumerate(zip(srcs, slots)):
+        arr[i].src = _slab_ptr(src)
+        arr[i].slot = int(slot)
+    return arr
+
+
+def pool_write_slabs(pool: QTensor, srcs, slots, src_slab_bytes: int | None = None):
+    """Copy expert slabs into pool slots on the current stream, like the expert cache's
+    ``ggml_backend_tensor_set_async(pool, src, slot * nb2, nb2)`` per (role, expert)
+    (core/expert_cache.cpp:637-723, :1357-1377).  ``srcs``: tensors (page-locked host
+    memory for asynchronous copies, or device memory) or raw pointers of one slab each;
+    ``slots``: their slots in ``pool`` (a [ne0, ne1, n_slots] QTensor)."""
+    nb2 = pool.nb[2]
+    for x in srcs:
+        if isinstance(x, torch.Tensor) and x.numel() * x.element_size() != nb2:
+            raise ValueError(f"slab of {x.numel() * x.element_size()} bytes, pool slot holds {nb2}")
+    arr = _slab_copies(srcs, slots)
+    d = pool.desc()
+    L.check("qwb_pool_write_slabs", L.lib().qwb_pool_write_slabs(
+        C.byref(d), nb2 if src_slab_bytes is None else src_slab_bytes, arr, len(srcs), _stream()))
+
+
+def pool_audit_slabs(pool: QTensor, expected, slots, checksums: bool = True):
+    """Byte audit of pool slots on the GPU (core/expert_weight_audit.h:56-66, :106-125):
+    one record per slot (equal, first_difference, expected_byte, actual_byte,
+    expected_fnv1a64, actual_fnv1a64) as a list of dicts.  ``expected``: the bytes each
+    slot should hold, in device or page-locked host memory.  ``checksums=False`` skips the
+    serial FNV-1a chains (both sums read 0) and only compares."""
+    n = len(expected)
+    res = torch.zeros((max(n, 1), C.sizeof(L.SlabAudit)), dtype=torch.uint8, device=pool.data.device)
+    arr = _slab_copies(expected, slots)
+    d = pool.desc()
+    L.check("qwb_pool_audit_slabs", L.lib().qwb_pool_audit_slabs(C.byref(d), arr, n, int(checksums), res.data_ptr(),
+                                                                 _stream()))
+    host = res.cpu().numpy()
+    out = []
+    for i in range(n):
+        r = L.SlabAudit.from_buffer_copy(host[i].tobytes())
+        out.append({k: int(getattr(r, k)) for k, _ in L.SlabAudit._fields_ if k != "reserved"})
+    return out

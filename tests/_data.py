@@ -33,3 +33,35 @@ def zipf_ids(T, E, n_used, seed, s=1.1):
     pop = 1.0 / np.arange(1, E + 1, dtype=np.float64) ** s
     logits = np.log(pop[r.permutation(E)])[None, :] + r.gumbel(size=(T, E))
     return np.argsort(-logits, axis=1, kind="stable")[:, :n_used].astype(np.int32)
+
+
+def slab_bytes(size: int, seed: int) -> np.ndarray:
+    """Deterministic pseudo-random slab bytes (splitmix64 of the byte index), defined by
+    this formula rather than by a library generator so fixtures never depend on numpy's
+    stream versions."""
+    with np.errstate(over="ignore"):
+        z = np.arange(size, dtype=np.uint64) + np.uint64(seed) * np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        z = z ^ (z >> np.uint64(31))
+    return (z & np.uint64(0xFF)).astype(np.uint8)
+
+
+# Byte-audit cases: (slab bytes, seed, [(position, xor mask), ...] planted in the actual
+# bytes).  Sizes cover one partial chunk, exact multiples and non-multiples of the
+# device's 8 KB staging chunk and of 16 bytes, and a C1 Q4_K expert slab (884,736 B).
+AUDIT_CASES = [
+    (1, 1, []), (1, 2, [(0, 0x80)]), (15, 3, [(14, 1)]), (16, 4, []),
+    (8191, 5, [(8190, 0xff)]), (8192, 6, [(0, 1), (100, 2)]), (8193, 7, [(8192, 4)]),
+    (70001, 8, [(40000, 0x10), (40001, 0x10)]), (65536, 9, [(8191, 1), (8192, 1)]),
+    (884736, 10, []), (884736, 11, [(884735, 0x01)]), (884736, 12, [(123457, 0x5a), (700000, 3)]),
+]
+
+
+def audit_pair(size, seed, flips):
+    """(expected, actual) bytes of one audit case."""
+    exp = slab_bytes(size, seed)
+    act = exp.copy()
+    for pos, mask in flips:
+        act[pos] ^= mask
+    return exp, act
