@@ -284,12 +284,13 @@ QWB_API qwb_status qwb_moe_ep_experts(const qwb_moe_ep_experts_desc *desc, void 
  *
  * qwb_pool_write_slabs issues those copies on `stream` for n slabs of one pool: copy i
  * writes pool->nb[2] bytes from copies[i].src into slot copies[i].slot, in array order
- * (a slot named twice ends with the later source), one asynchronous copy per slab; odd
- * slots are copied on a second stream of the library's, forked from `stream` and joined
- * back into it with events, so work queued on `stream` after the call sees every slab.
- * Sources in page-locked host memory
- * (cudaHostAlloc / cudaHostRegister) give asynchronous DMA copies; pageable sources work
- * but the copy is staged by the driver; device sources are device-to-device copies.
+ * (a slot named twice ends with the later source).  When every source is readable by the
+ * device (page-locked host memory from cudaHostAlloc / cudaHostRegister, or this device's
+ * memory) and 16-byte aligned, one kernel launch gathers the whole group, reading the
+ * sources directly; otherwise one cudaMemcpyAsync per slab (pageable sources are staged
+ * by the driver), the odd slots on a second stream of the library's, forked from
+ * `stream` and joined back into it with events.  Either way, work queued on `stream`
+ * after the call sees every slab.
  * Arguments are checked before the first copy is issued: src_slab_bytes must equal
  * pool->nb[2] (QWB_ERR_SHAPE), every slot must lie in [0, pool->ne[2])
  * (QWB_ERR_INVALID_ARG), so an error writes nothing. */

@@ -8,11 +8,15 @@
 // arguments are checked first (nothing is written on an error), then one asynchronous
 // copy per slab.  Slabs are not merged into larger copies even when their addresses
 // line up: adjacent addresses may belong to two separate page-locked allocations, and
-// one copy may not span both.  Copies in one stream run back to back with a fixed
-// set-up gap each (~7 us per 1 MB slab on the B200 boxes' host link, 0.82 of one large
-// copy's rate); the odd slots go to a second stream of the library's, forked from and
-// joined back into the caller's stream with events, so one copy's set-up overlaps the
-// other's transfer.  A slot's copies all go to the same stream, in array order.
+// one copy may not span both.  Copy-engine copies queued back to back leave a set-up gap
+// each (0.67-0.84 of one large copy's rate for 24 slabs of ~1 MB), so when every source
+// is readable by the device (page-locked host memory or this device's memory) and
+// 16-byte aligned, one gather kernel moves the whole group: each CTA copies a 64 KB chunk
+// of one slab with 16-byte loads straight from the source (over the host link for host
+// memory) and stores into the slot.  A slot named twice keeps only its last source (the
+// one a sequence of copies would leave).  Otherwise (pageable or unaligned sources) one
+// cudaMemcpyAsync per slab, the odd slots on a second stream of the library's, forked
+// from and joined back into the caller's stream with events.
 //
 // Byte audit: ExpertWeightAudit::destination / compare (core/expert_weight_audit.h:62-66,
 // :106-125) read each slot back to the host and compare it with the authoritative bytes,
@@ -28,6 +32,8 @@
 
 #include <algorithm>
 #include <mutex>
+#include <unordered_set>
+#include <vector>
 
 #include "common.cuh"
 
@@ -156,6 +162,35 @@ bool side_ready(SideStream &ss) {
     return true;
 }
 
+constexpr int kGatherThreads = 256;
+constexpr int kGatherChunk = 65536;  // bytes of one slab per CTA
+constexpr int kGatherBatch = 128;    // slabs per launch (pointer table in the kernel parameters)
+
+struct GatherBatch {
+    const uint4 *src[kGatherBatch];
+    uint4 *dst[kGatherBatch];
+};
+
+// CTA (slab i, chunk c) copies bytes [c * 64 KB, (c + 1) * 64 KB) of slab i; every thread
+// keeps four 16-byte loads in flight before it stores them.
+__global__ void __launch_bounds__(kGatherThreads) pool_gather_kernel(const __grid_constant__ GatherBatch b,
+                                                                     int chunks, long long words) {
+    const int i = blockIdx.x / chunks, c = blockIdx.x - i * chunks;
+    const uint4 *src = b.src[i];
+    uint4 *dst = b.dst[i];
+    constexpr int kw = kGatherChunk / 16;
+    const long long w0 = (long long) c * kw, w1 = min(w0 + kw, words);
+    long long w = w0 + threadIdx.x;
+    for (; w + 3 * kGatherThreads < w1; w += 4 * kGatherThreads) {
+        uint4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = src[w + k * kGatherThreads];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[w + k * kGatherThreads] = v[k];
+    }
+    for (; w < w1; w += kGatherThreads) dst[w] = src[w];
+}
+
 bool pool_ok(const qwb_tensor *pool) { return pool && pool->data && pool->ne[2] >= 1 && pool->nb[2] > 0; }
 
 // A pointer the current device can dereference: device memory of this device, managed
@@ -189,12 +224,44 @@ extern "C" QWB_API qwb_status qwb_pool_write_slabs(const qwb_tensor *pool, size_
     if (n == 0) return QWB_OK;
     cudaStream_t s = (cudaStream_t) stream;
     char *base = (char *) pool->data;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= qwb::kMaxDevices) return QWB_ERR_CUDA;
+    {
+        // gather kernel: every source device-readable and 16-byte aligned, the slots too
+        std::vector<const void *> view(n, nullptr);
+        bool gather = nb2 % 16 == 0 && (uintptr_t) base % 16 == 0 && qwb::device_view(base, dev) == base;
+        for (int i = 0; i < n && gather; ++i) {
+            view[i] = qwb::device_view(copies[i].src, dev);
+            gather = view[i] && (uintptr_t) view[i] % 16 == 0;
+        }
+        if (gather) {
+            // the last entry of each slot wins; the others would be overwritten
+            std::vector<int> keep;
+            keep.reserve(n);
+            std::unordered_set<int64_t> seen;
+            for (int i = n - 1; i >= 0; --i)
+                if (seen.insert(copies[i].slot).second) keep.push_back(i);
+            const int chunks = (int) ((nb2 + qwb::kGatherChunk - 1) / qwb::kGatherChunk);
+            for (size_t k0 = 0; k0 < keep.size(); k0 += qwb::kGatherBatch) {
+                const int cnt = (int) std::min(keep.size() - k0, (size_t) qwb::kGatherBatch);
+                qwb::GatherBatch b{};
+                for (int k = 0; k < cnt; ++k) {
+                    const int i = keep[k0 + k];
+                    b.src[k] = (const uint4 *) view[i];
+                    b.dst[k] = (uint4 *) (base + (size_t) copies[i].slot * nb2);
+                }
+                qwb::pool_gather_kernel<<<cnt * chunks, qwb::kGatherThreads, 0, s>>>(b, chunks,
+                                                                                   (long long) (nb2 / 16));
+                if (cudaGetLastError() != cudaSuccess) return QWB_ERR_CUDA;
+            }
+            return QWB_OK;
+        }
+        (void) cudaGetLastError();
+    }
     auto issue = [&](int i, cudaStream_t st) {
         return cudaMemcpyAsync(base + (size_t) copies[i].slot * nb2, copies[i].src, nb2, cudaMemcpyDefault, st) ==
                cudaSuccess;
     };
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= qwb::kMaxDevices) return QWB_ERR_CUDA;
     std::lock_guard<std::mutex> lk(qwb::g_side_mu);
     qwb::SideStream &ss = qwb::g_side[dev];
     bool ok;
