@@ -394,7 +394,7 @@ struct MmidPlan {
     int NT;
     bool pf;  // tensor-core grouped GEMM (many tokens per expert)
     bool stream;  // weight-streaming kernel (one tile per expert)
-    bool pf8;     // Q8_0 / Q6_K integer tensor-core kernel (many tokens per expert)
+    bool pf8;     // Q8_0 / Q6_K integer tensor-core kernel (8 or more tokens per expert)
     size_t planes, index, btiles, da, total;
 };
 
@@ -425,7 +425,7 @@ qwb_status plan_mmid(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor
     p.pf8 = allow_prefill && pf_i8_eligible(p.type, p.K, p.M, p.P, p.n_as, as->data, as->nb[1], as->nb[2]);
     p.stream = !p.pf && !p.pf8 && stream_fits(p.type, p.K, as->nb[1], as->nb[1], false);
     p.NT = p.pf    ? kPfTileN
-           : p.pf8 ? pf_i8_tile_tokens()
+           : p.pf8 ? pf_i8_tile_tokens(p.P, p.n_as)
            : p.stream ? (int) std::max<int64_t>(1, p.P)
                       : pick_nt(p.P, p.n_as);
     p.planes = planes_bytes(p.n_b * p.T, p.K, p.vdt == QWB_TYPE_Q8_K);
@@ -542,7 +542,7 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
         q.dnb2 = dst->nb[2];
         q.work = ix.work + 2;
         q.st = st;
-        e = launch_pf_i8(p.type, q, s);
+        e = launch_pf_i8(p.type, p.NT, q, s);
         profile_mark(s, QWB_KERNEL_GROUPED_GEMM);
         return e == cudaSuccess ? QWB_OK : QWB_ERR_CUDA;
     }

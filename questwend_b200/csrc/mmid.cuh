@@ -48,14 +48,14 @@ struct GemvArgs {
     qwb_status_block *st;
 };
 
-// Q8_0 / Q6_K experts with many tokens per expert: integer tensor-core kernel (prefill_i8.cu).
+// Q8_0 / Q6_K experts with 8 or more tokens per expert: integer tensor-core kernel (prefill_i8.cu).
 struct I8PrefillArgs {
     const uint8_t *W;        // expert weights [K, M, n_as] (16-byte aligned)
     size_t nb1, nb2;
     int64_t M, K, n_as;
     Q8Planes act;            // activation planes (Q8_0 for Q8_0 weights, Q8_K for Q6_K)
     int act_dstride;
-    const int4 *tiles;       // index tiles of <= pf_i8_tile_tokens() pairs
+    const int4 *tiles;       // index tiles of <= pf_i8_tile_tokens(P, n_as) pairs
     const int *n_tiles;
     const int *pairs;
     int n_used, n_b;
@@ -65,8 +65,8 @@ struct I8PrefillArgs {
     qwb_status_block *st;
 };
 bool pf_i8_eligible(int type, int64_t K, int64_t M, int64_t P, int64_t n_as, const void *W, size_t nb1, size_t nb2);
-int pf_i8_tile_tokens();
-cudaError_t launch_pf_i8(int type, const I8PrefillArgs &a, cudaStream_t s);
+int pf_i8_tile_tokens(int64_t P, int64_t n_as);
+cudaError_t launch_pf_i8(int type, int tile_tokens, const I8PrefillArgs &a, cudaStream_t s);
 
 void gemv_geometry(GemvArgs &a, int NT, bool glu);
 cudaError_t launch_gemv(int type, bool glu, GemvArgs a, int NT, int max_tiles, cudaStream_t s);

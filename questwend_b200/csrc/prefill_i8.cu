@@ -11,9 +11,11 @@
 // 16-row x 8-token fragment: one m16n8k32 per Q8_0 block, one m16n8k16 per Q6_K sub-block
 // (whose integer scale is applied in int32, the fp32 scale once per superblock).
 //
-// Work item = (expert tile of <= 64 routed (token, slot) pairs, 128 weight rows); one
-// persistent CTA per SM takes items from a counter the index kernel zeroed.  8 warps, each
-// a 32-row x 32-token tile (2 x 4 fragments).  Per K step of 256:
+// Work item = (expert tile of <= TN routed (token, slot) pairs, 128 weight rows); one
+// persistent CTA per SM takes items from a counter the index kernel zeroed.  TN = 64 (32 or
+// more pairs per expert): 8 warps, each a 32-row x 32-token tile (2 x 4 fragments);
+// TN = 8 (8 to 31 pairs per expert, e.g. the output head at 8 tokens): 8 warps of 16 rows
+// x 8 tokens, so few tokens do not pay for 64-token MMAs.  Per K step of 256:
 //   * cp.async (16 B per thread, double-buffered) brings the 128 weight rows' raw block
 //     bytes of the step (Q8_0: 8 blocks of 34 B = 272 B; Q6_K: one 210-byte superblock,
 //     widened to 16-byte boundaries) and the tile's 64 activation rows (codes + scales) to
@@ -40,7 +42,8 @@ namespace qwb {
 namespace {
 
 constexpr int kI8TM = 128;      // weight rows per item
-constexpr int kI8TN = 64;       // token pairs per item (index tile size)
+constexpr int kI8TNBig = 64;    // token pairs per item (index tile size), many tokens per expert
+constexpr int kI8TNSmall = 8;   // ... 8 to 31 tokens per expert
 constexpr int kI8KS = 256;      // K per step
 constexpr int kI8Row = 272;     // padded code row stride in shared memory (256 + 16)
 constexpr int kI8Threads = 256;
@@ -57,29 +60,40 @@ struct I8Geo {
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23, bit pattern 0x4B400000
 constexpr int kMagicBits = 0x4B400000;
 
-// Pipeline slots of K step ks: copies land in raw / off [ks & 1] and aq / da [ks % 3]; the
-// repack writes wq / dw / dwp / dap / sc [ks & 1].  In the iteration of step ks the MMAs
-// read step ks while the repack writes step ks + 1 and the copies of step ks + 2 land.
-template <int TYPE>
+// Copy pipeline depth D: K steps whose copies are in flight.  A 64-token step's MMAs take
+// about one memory latency, so one step ahead (D = 2) hides it; an 8-token step computes
+// little and keeps more steps in flight (3 for Q8_0, 4 for Q6_K: what 227 KB allows).
+template <int TYPE, int TN>
+struct I8Depth {
+    static constexpr int D = TN == kI8TNBig ? 2 : (TYPE == QWB_TYPE_Q8_0 ? 3 : 4);
+};
+
+// Pipeline slots of K step ks: copies land in raw / off [ks % D] and aq / da [ks % (D + 1)];
+// the repack writes wq / dw / dwp / dap / sc [ks & 1].  In the iteration of step ks the MMAs
+// read step ks while the repack writes step ks + 1 and the copies of step ks + D land.
+template <int TYPE, int TN>
 struct I8Smem {
-    uint8_t raw[2][kI8TM][I8Geo<TYPE>::raw];  // raw weight bytes (cp.async)
+    static constexpr int D = I8Depth<TYPE, TN>::D;
+    uint8_t raw[D][kI8TM][I8Geo<TYPE>::raw];  // raw weight bytes (cp.async)
     uint8_t wq[2][kI8TM][kI8Row];             // repacked int8 codes
-    uint8_t aq[3][kI8TN][kI8Row];             // activation codes (cp.async from the planes)
+    uint8_t aq[D + 1][TN][kI8Row];            // activation codes (cp.async from the planes)
     float dw[2][kI8TM][I8Geo<TYPE>::ndw];     // Q6_K: weight scale of the step
     // Q8_0: weight scales of block j for the rows one lane reads, (g, g+8, g+16, g+24) of its
     // warp's 32 rows; and activation scales of token pair k (tokens 2k, 2k+1) of block j as
     // {d(2k), d(2k+1), -kMagic d(2k), -kMagic d(2k+1)} (stride 33 pairs: no bank conflicts)
     float dwp[2][I8Geo<TYPE>::nj][4][8][4];
-    float dap[2][I8Geo<TYPE>::nj][I8Geo<TYPE>::q6 ? 1 : kI8TN / 2 + 1][4];
+    float dap[2][I8Geo<TYPE>::nj][I8Geo<TYPE>::q6 ? 1 : TN / 2 + 1][4];
     int sc[2][I8Geo<TYPE>::q6 ? kI8TM : 1][16];  // Q6_K sub-block scales of the step
-    float da[3][kI8TN][I8Geo<TYPE>::nda];        // activation scales (cp.async)
-    int off[2][kI8TM];                           // Q6_K: offset of the superblock in its raw row
-    long long tok_o[kI8TN];                   // output byte offset of each pair
-    int tok_ar[kI8TN];                        // activation plane row of each pair
+    float da[D + 1][TN][I8Geo<TYPE>::nda];       // activation scales (cp.async)
+    int off[D][kI8TM];                           // Q6_K: offset of the superblock in its raw row
+    long long tok_o[TN];                      // output byte offset of each pair
+    int tok_ar[TN];                           // activation plane row of each pair
     int item;
 };
 
-static_assert(sizeof(I8Smem<QWB_TYPE_Q8_0>) <= 232448 && sizeof(I8Smem<QWB_TYPE_Q6_K>) <= 232448,
+static_assert(sizeof(I8Smem<QWB_TYPE_Q8_0, kI8TNBig>) <= 232448 && sizeof(I8Smem<QWB_TYPE_Q6_K, kI8TNBig>) <= 232448 &&
+                  sizeof(I8Smem<QWB_TYPE_Q8_0, kI8TNSmall>) <= 232448 &&
+                  sizeof(I8Smem<QWB_TYPE_Q6_K, kI8TNSmall>) <= 232448,
               "one CTA per SM: at most 227 KB of shared memory");
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
@@ -88,13 +102,20 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src, bool vali
                  : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+// wait until at most N of this thread's most recent copy groups are still pending
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t &r0, uint32_t &r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
 
 // one 32-element block (m16n8k32) of A = {a0..a3} and B = {b0, b1}, added to `bias`
@@ -114,12 +135,13 @@ __device__ __forceinline__ void mma_k16(int *c, uint32_t a0, uint32_t a1, uint32
 }
 
 // Issue the copies of K step `ks` of the current item into its slots.
-template <int TYPE>
-__device__ __forceinline__ void i8_issue(const I8PrefillArgs &a, I8Smem<TYPE> &S, int ks, const uint8_t *wbase,
+template <int TYPE, int TN>
+__device__ __forceinline__ void i8_issue(const I8PrefillArgs &a, I8Smem<TYPE, TN> &S, int ks, const uint8_t *wbase,
                                          int nrows, int ntok) {
     using G = I8Geo<TYPE>;
+    constexpr int D = I8Depth<TYPE, TN>::D;
     const int tid = threadIdx.x;
-    const int buf = ks & 1, b3 = ks % 3;
+    const int buf = ks % D, b3 = ks % (D + 1);
     constexpr int pieces = G::raw / 16;
     for (int i = tid; i < kI8TM * pieces; i += kI8Threads) {
         const int r = i / pieces, c = i - r * pieces;
@@ -140,7 +162,7 @@ __device__ __forceinline__ void i8_issue(const I8PrefillArgs &a, I8Smem<TYPE> &S
         }
     }
     constexpr int dpieces = G::nda / 4;
-    for (int i = tid; i < kI8TN * (16 + dpieces); i += kI8Threads) {
+    for (int i = tid; i < TN * (16 + dpieces); i += kI8Threads) {
         const int k = i / (16 + dpieces), c = i - k * (16 + dpieces);
         const bool ok = k < ntok;
         const int64_t ar = ok ? S.tok_ar[k] : 0;
@@ -157,12 +179,13 @@ __device__ __forceinline__ void i8_issue(const I8PrefillArgs &a, I8Smem<TYPE> &S
 }
 
 // Repack row r's raw bytes of step ks (two threads per row) into int8 codes + scales.
-template <int TYPE>
-__device__ __forceinline__ void i8_repack(I8Smem<TYPE> &S, int ks, int tid) {
+template <int TYPE, int TN>
+__device__ __forceinline__ void i8_repack(I8Smem<TYPE, TN> &S, int ks, int tid) {
+    constexpr int D = I8Depth<TYPE, TN>::D;
     const int r = tid >> 1, half = tid & 1;
-    const int buf = ks & 1, b3 = ks % 3;
+    const int buf = ks & 1, rb = ks % D, b3 = ks % (D + 1);  // repacked / raw / activation slots
     if constexpr (TYPE == QWB_TYPE_Q8_0) {
-        const uint8_t *src = S.raw[buf][r] + 136 * half;  // 4 blocks of 34 B
+        const uint8_t *src = S.raw[rb][r] + 136 * half;  // 4 blocks of 34 B
         uint8_t *dst = S.wq[buf][r] + 128 * half;
         // row r = 32 wm + 16 mi + 8 h + g is slot 2 mi + h of lane group g in warp row wm
         const int wm = r >> 5, g = r & 7, slot = ((r >> 3) & 3);
@@ -177,7 +200,7 @@ __device__ __forceinline__ void i8_repack(I8Smem<TYPE> &S, int ks, int tid) {
             d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
         // activation scales of token pair k, block j (8 threads per pair)
-        {
+        if (tid < 4 * TN) {
             const int k = tid >> 3, j = tid & 7;
             const float d0 = S.da[b3][2 * k][j], d1 = S.da[b3][2 * k + 1][j];
             *(float4 *) &S.dap[buf][j][k][0] = make_float4(d0, d1, -kMagic * d0, -kMagic * d1);
@@ -185,7 +208,7 @@ __device__ __forceinline__ void i8_repack(I8Smem<TYPE> &S, int ks, int tid) {
     } else {
         // Q6_K superblock: ql[128] qh[64] sc[16] d; element 128*hf + 32*i + l has ql nibble
         // (ql[64hf + 32(i&1) + l], high when i >= 2) and qh bits 2i..2i+1 of qh[32hf + l]
-        const uint8_t *sb = S.raw[buf][r] + S.off[buf][r];  // 2-byte aligned
+        const uint8_t *sb = S.raw[rb][r] + S.off[rb][r];  // 2-byte aligned
         const int hf = half;
         uint32_t qa[8], qb[8], qh[8];
         lds_words8_a2(sb + 64 * hf, qa);
@@ -212,13 +235,20 @@ __device__ __forceinline__ void i8_repack(I8Smem<TYPE> &S, int ks, int tid) {
     }
 }
 
-template <int TYPE>
+// Warp tiling of the 128-row x TN-token item: TN = 64, 4 x 2 warps of 32 rows x 32 tokens
+// (MI = 2 row fragments x NI = 4 token fragments); TN = 8, 8 warps of 16 rows x 8 tokens
+// (MI = NI = 1, B fragments from a 2-matrix ldmatrix).
+template <int TYPE, int TN>
 __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArgs a) {
     using G = I8Geo<TYPE>;
+    constexpr int D = I8Depth<TYPE, TN>::D;
+    constexpr bool big = TN == kI8TNBig;
+    constexpr int MI = big ? 2 : 1, NI = big ? 4 : 1;
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    I8Smem<TYPE> &S = *(I8Smem<TYPE> *) smem_raw;
+    I8Smem<TYPE, TN> &S = *(I8Smem<TYPE, TN> *) smem_raw;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int wm = warp & 3, wn = warp >> 2;  // warp tile: rows 32*wm.., tokens 32*wn..
+    const int row0 = big ? 32 * (warp & 3) : 16 * warp;  // the warp's first row
+    const int tok0 = big ? 32 * (warp >> 2) : 0;          // and first token
     const int n_rb = (int) ceil_div(a.M, kI8TM);
     const int64_t n_items = (int64_t) (*a.n_tiles) * n_rb;
     const int nks = (int) (a.K / kI8KS);
@@ -232,7 +262,7 @@ __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArg
         const int ntok = t.z;
         const int64_t e = (t.x >= 0 && t.x < a.n_as) ? t.x : -1;
         __syncthreads();  // the previous item's buffers are no longer read
-        if (tid < kI8TN) {
+        if (tid < TN) {
             if (tid < ntok) {
                 const int p = a.pairs[t.y + tid];
                 const int tt = p / a.n_used, j = p - tt * a.n_used;
@@ -259,68 +289,77 @@ __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArg
         }
         const uint8_t *wbase = a.W + (size_t) e * a.nb2 + (size_t) r0 * a.nb1;
 
-        float acc[2][4][4];
+        float acc[MI][NI][4];
 #pragma unroll
-        for (int mi = 0; mi < 2; ++mi)
+        for (int mi = 0; mi < MI; ++mi)
 #pragma unroll
-            for (int ni = 0; ni < 4; ++ni)
+            for (int ni = 0; ni < NI; ++ni)
 #pragma unroll
                 for (int v = 0; v < 4; ++v) acc[mi][ni][v] = 0.f;
 
-        // prologue: steps 0 and 1 in flight, step 0 repacked
-        i8_issue<TYPE>(a, S, 0, wbase, nrows, ntok);
-        if (nks > 1) {
-            i8_issue<TYPE>(a, S, 1, wbase, nrows, ntok);
-            cp_async_wait1();
-        } else {
-            cp_async_wait0();
+        // prologue: steps 0 .. D-1 in flight (one copy group per step, empty past the last
+        // step, so group g is always step g), step 0 repacked
+#pragma unroll
+        for (int st = 0; st < D; ++st) {
+            if (st < nks) i8_issue<TYPE, TN>(a, S, st, wbase, nrows, ntok);
+            else cp_async_commit();
         }
-        __syncthreads();  // step 0 has landed for every thread
-        i8_repack<TYPE>(S, 0, tid);
+        cp_async_wait<D - 1>();  // step 0
+        __syncthreads();         // step 0 has landed for every thread
+        i8_repack<TYPE, TN>(S, 0, tid);
         for (int ks = 0; ks < nks; ++ks) {
-            const int buf = ks & 1, b3 = ks % 3;
-            if (ks + 1 < nks) cp_async_wait0();  // this thread's copies of step ks + 1
+            const int buf = ks & 1, b3 = ks % (D + 1);
+            cp_async_wait<D - 2>();  // this thread's copies of step ks + 1
             // One barrier per step: step ks + 1 has landed, step ks is repacked, and the
             // MMAs of step ks - 1 are done, so its slots may be refilled / rewritten.
             __syncthreads();
-            if (ks + 2 < nks) i8_issue<TYPE>(a, S, ks + 2, wbase, nrows, ntok);
-            if (ks + 1 < nks) i8_repack<TYPE>(S, ks + 1, tid);
+            if (ks + D < nks) i8_issue<TYPE, TN>(a, S, ks + D, wbase, nrows, ntok);
+            else cp_async_commit();
+            if (ks + 1 < nks) i8_repack<TYPE, TN>(S, ks + 1, tid);
             const uint32_t wq_base = smem_u32(&S.wq[buf][0][0]), aq_base = smem_u32(&S.aq[b3][0][0]);
-            int isum[2][4][4];  // Q6_K: integer sum of the superblock (sub-block scales applied)
+            int isum[MI][NI][4];  // Q6_K: integer sum of the superblock (sub-block scales applied)
 #pragma unroll
-            for (int mi = 0; mi < 2; ++mi)
+            for (int mi = 0; mi < MI; ++mi)
 #pragma unroll
-                for (int ni = 0; ni < 4; ++ni)
+                for (int ni = 0; ni < NI; ++ni)
 #pragma unroll
                     for (int v = 0; v < 4; ++v) isum[mi][ni][v] = 0;
 #pragma unroll 2
             for (int j = 0; j < 8; ++j) {  // 32 elements per j
-                uint32_t af[2][4];
+                uint32_t af[MI][4];
 #pragma unroll
-                for (int mi = 0; mi < 2; ++mi) {
-                    const int row = 32 * wm + 16 * mi + (lane & 7) + ((lane >> 3) & 1) * 8;
+                for (int mi = 0; mi < MI; ++mi) {
+                    const int row = row0 + 16 * mi + (lane & 7) + ((lane >> 3) & 1) * 8;
                     const int col = 32 * j + (lane >> 4) * 16;
                     ldsm_x4(wq_base + row * kI8Row + col, af[mi][0], af[mi][1], af[mi][2], af[mi][3]);
                 }
-                uint32_t bf[4][2];
+                uint32_t bf[NI][2];
+                if constexpr (big) {
 #pragma unroll
-                for (int np = 0; np < 2; ++np) {
-                    const int tok = 32 * wn + 16 * np + (lane & 7) + 8 * (lane >> 4);
-                    const int col = 32 * j + 16 * ((lane >> 3) & 1);
-                    ldsm_x4(aq_base + tok * kI8Row + col, bf[2 * np][0], bf[2 * np][1], bf[2 * np + 1][0],
-                            bf[2 * np + 1][1]);
+                    for (int np = 0; np < 2; ++np) {
+                        const int tok = tok0 + 16 * np + (lane & 7) + 8 * (lane >> 4);
+                        const int col = 32 * j + 16 * ((lane >> 3) & 1);
+                        ldsm_x4(aq_base + tok * kI8Row + col, bf[2 * np][0], bf[2 * np][1], bf[2 * np + 1][0],
+                                bf[2 * np + 1][1]);
+                    }
+                } else {  // lanes 0-15 address tokens 0-7, k 0-15 / 16-31 (lanes 16-31 repeat them)
+                    const int tok = lane & 7, col = 32 * j + 16 * ((lane >> 3) & 1);
+                    ldsm_x2(aq_base + tok * kI8Row + col, bf[0][0], bf[0][1]);
                 }
                 if constexpr (TYPE == QWB_TYPE_Q8_0) {
                     // {row g, g+8} of mi 0, then of mi 1; per ni {d(tok), d(tok+1), -M d(tok), -M d(tok+1)}
-                    const float4 dw4 = *(const float4 *) &S.dwp[buf][j][wm][lane >> 2][0];
-                    float4 da4[4];
+                    const float4 dw4 = *(const float4 *) &S.dwp[buf][j][row0 >> 5][lane >> 2][0];
+                    float4 da4[NI];
 #pragma unroll
-                    for (int ni = 0; ni < 4; ++ni) da4[ni] = *(const float4 *) &S.dap[buf][j][16 * wn + 4 * ni + (lane & 3)][0];
+                    for (int ni = 0; ni < NI; ++ni)
+                        da4[ni] = *(const float4 *) &S.dap[buf][j][tok0 / 2 + 4 * ni + (lane & 3)][0];
 #pragma unroll
-                    for (int mi = 0; mi < 2; ++mi) {
-                        const float w0 = mi ? dw4.z : dw4.x, w1 = mi ? dw4.w : dw4.y;
+                    for (int mi = 0; mi < MI; ++mi) {
+                        // rows row0 + 16 mi + {g, g + 8}: 16-row half ((row0 >> 4) & 1) + mi of the 32-row group
+                        const bool hi = (((row0 >> 4) & 1) + mi) != 0;
+                        const float w0 = hi ? dw4.z : dw4.x, w1 = hi ? dw4.w : dw4.y;
 #pragma unroll
-                        for (int ni = 0; ni < 4; ++ni) {
+                        for (int ni = 0; ni < NI; ++ni) {
                             int c[4];
                             mma_k32(c, af[mi], bf[ni][0], bf[ni][1], kMagicBits);
                             // c0: (row g, tok 2q), c1: (g, 2q+1), c2: (g+8, 2q), c3: (g+8, 2q+1)
@@ -333,19 +372,19 @@ __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArg
                     }
                 } else {
                     // sub-blocks 2j (A regs 0,1 / B reg 0) and 2j+1 (A regs 2,3 / B reg 1)
-                    int scr[2][2][2];  // [mi][row g / g+8][sub-block]
+                    int scr[MI][2][2];  // [mi][row g / g+8][sub-block]
 #pragma unroll
-                    for (int mi = 0; mi < 2; ++mi) {
-                        const int row = 32 * wm + 16 * mi + (lane >> 2);
+                    for (int mi = 0; mi < MI; ++mi) {
+                        const int row = row0 + 16 * mi + (lane >> 2);
                         scr[mi][0][0] = S.sc[buf][row][2 * j];
                         scr[mi][0][1] = S.sc[buf][row][2 * j + 1];
                         scr[mi][1][0] = S.sc[buf][row + 8][2 * j];
                         scr[mi][1][1] = S.sc[buf][row + 8][2 * j + 1];
                     }
 #pragma unroll
-                    for (int mi = 0; mi < 2; ++mi) {
+                    for (int mi = 0; mi < MI; ++mi) {
 #pragma unroll
-                        for (int ni = 0; ni < 4; ++ni) {
+                        for (int ni = 0; ni < NI; ++ni) {
 #pragma unroll
                             for (int sb = 0; sb < 2; ++sb) {
                                 int c[4];
@@ -362,12 +401,12 @@ __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArg
             if constexpr (TYPE == QWB_TYPE_Q6_K) {
                 // one fp32 scale per superblock: (d_w * d_a) * isum
 #pragma unroll
-                for (int mi = 0; mi < 2; ++mi) {
-                    const int row = 32 * wm + 16 * mi + (lane >> 2);
+                for (int mi = 0; mi < MI; ++mi) {
+                    const int row = row0 + 16 * mi + (lane >> 2);
                     const float dw0 = S.dw[buf][row][0], dw1 = S.dw[buf][row + 8][0];
 #pragma unroll
-                    for (int ni = 0; ni < 4; ++ni) {
-                        const int tok = 32 * wn + 8 * ni + 2 * (lane & 3);
+                    for (int ni = 0; ni < NI; ++ni) {
+                        const int tok = tok0 + 8 * ni + 2 * (lane & 3);
                         const float da0 = S.da[b3][tok][ks & 3], da1 = S.da[b3][tok + 1][ks & 3];
                         acc[mi][ni][0] += __fmul_rn(dw0, da0) * (float) isum[mi][ni][0];
                         acc[mi][ni][1] += __fmul_rn(dw0, da1) * (float) isum[mi][ni][1];
@@ -379,13 +418,13 @@ __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArg
         }
         // outputs: dst[row] of each (token, slot) pair
 #pragma unroll
-        for (int mi = 0; mi < 2; ++mi) {
+        for (int mi = 0; mi < MI; ++mi) {
 #pragma unroll
-            for (int ni = 0; ni < 4; ++ni) {
+            for (int ni = 0; ni < NI; ++ni) {
 #pragma unroll
                 for (int v = 0; v < 4; ++v) {
-                    const int row = 32 * wm + 16 * mi + (lane >> 2) + 8 * (v >> 1);
-                    const int tok = 32 * wn + 8 * ni + 2 * (lane & 3) + (v & 1);
+                    const int row = row0 + 16 * mi + (lane >> 2) + 8 * (v >> 1);
+                    const int tok = tok0 + 8 * ni + 2 * (lane & 3) + (v & 1);
                     if (row < nrows && tok < ntok)
                         ((float *) ((char *) a.dst + S.tok_o[tok]))[r0 + row] = acc[mi][ni][v];
                 }
@@ -395,16 +434,17 @@ __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArg
     }
 }
 
-template <int TYPE>
+template <int TYPE, int TN>
 cudaError_t launch_i8_t(const I8PrefillArgs &a, cudaStream_t s) {
-    const size_t smem = sizeof(I8Smem<TYPE>);
+    const size_t smem = sizeof(I8Smem<TYPE, TN>);
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(pf_i8_kernel<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        cudaError_t e =
+            cudaFuncSetAttribute(pf_i8_kernel<TYPE, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    pf_i8_kernel<TYPE><<<num_sms(), kI8Threads, smem, s>>>(a);
+    pf_i8_kernel<TYPE, TN><<<num_sms(), kI8Threads, smem, s>>>(a);
     return cudaGetLastError();
 }
 
@@ -416,13 +456,23 @@ bool pf_i8_eligible(int type, int64_t K, int64_t M, int64_t P, int64_t n_as, con
     // each superblock to 16-byte boundaries inside the 16-byte aligned tensor
     if (type == QWB_TYPE_Q8_0 ? ((uintptr_t) W | nb1 | nb2) % 16 : (uintptr_t) W % 16) return false;
     const int64_t used = std::min<int64_t>(P, n_as);
-    return used > 0 && P >= 32 * used;
+    return used > 0 && P >= kI8TNSmall * used;
 }
 
-int pf_i8_tile_tokens() { return kI8TN; }
+// routed pairs per used expert on average: >= 32, 64-token tiles; 8 to 31, 8-token tiles
+int pf_i8_tile_tokens(int64_t P, int64_t n_as) {
+    const int64_t used = std::max<int64_t>(1, std::min<int64_t>(P, n_as));
+    return P >= 32 * used ? kI8TNBig : kI8TNSmall;
+}
 
-cudaError_t launch_pf_i8(int type, const I8PrefillArgs &a, cudaStream_t s) {
-    return type == QWB_TYPE_Q6_K ? launch_i8_t<QWB_TYPE_Q6_K>(a, s) : launch_i8_t<QWB_TYPE_Q8_0>(a, s);
+cudaError_t launch_pf_i8(int type, int tile_tokens, const I8PrefillArgs &a, cudaStream_t s) {
+    if (tile_tokens == kI8TNBig)
+        return type == QWB_TYPE_Q6_K ? launch_i8_t<QWB_TYPE_Q6_K, kI8TNBig>(a, s)
+                                     : launch_i8_t<QWB_TYPE_Q8_0, kI8TNBig>(a, s);
+    if (tile_tokens == kI8TNSmall)
+        return type == QWB_TYPE_Q6_K ? launch_i8_t<QWB_TYPE_Q6_K, kI8TNSmall>(a, s)
+                                     : launch_i8_t<QWB_TYPE_Q8_0, kI8TNSmall>(a, s);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace qwb

@@ -37,7 +37,9 @@ def _want(t, w, K, M, b):
     (O.Q4_K, 2048, 768, 5),
     (O.Q4_K, 1024, 256, 64),    # many tokens: tensor-core grouped GEMM
     (O.Q6_K, 2048, 4096, 1),    # output-head rows (Q6_K), decode
-    (O.Q6_K, 768, 2048, 12),    # > 8 tokens: several token passes per stage
+    (O.Q6_K, 768, 2048, 12),    # 8-31 tokens: int8 tensor cores, 8-token tiles
+    (O.Q6_K, 2048, 4096, 8),    # output-head rows at 8 tokens
+    (O.Q8_0, 1024, 300, 20),
     (O.Q8_0, 2048, 200, 3),
     (O.Q8_0, 512, 96, 40),
 ])

@@ -87,6 +87,48 @@ def test_pool_write_round_trip():
     assert L.lib().qwb_pool_write_slabs(C.byref(d), slab - 1, _copies([(base, 4)]), 1, _stream()) == 3
 
 
+def test_pool_write_copy_engine_fallback():
+    # sources the gather kernel cannot read (pageable host memory) or not 16-byte aligned
+    # go through one copy per slab; slots named twice still end with the later source
+    slab, n_slots = 65552, 5  # 64 KB + 16: the last chunk is partial
+    pool = torch.zeros(slab * n_slots, dtype=torch.uint8, device="cuda")
+    d = _pool_desc(pool, slab, n_slots)
+    pageable = [D.slab_bytes(slab, 40 + i) for i in range(3)]
+    entries = [(pageable[0].ctypes.data, 3), (pageable[1].ctypes.data, 0), (pageable[2].ctypes.data, 3)]
+    assert L.lib().qwb_pool_write_slabs(C.byref(d), slab, _copies(entries), 3, _stream()) == 0
+    # page-locked but misaligned by one byte
+    raw = _pinned(np.concatenate([np.zeros(1, np.uint8), D.slab_bytes(slab, 50), D.slab_bytes(slab, 51)]))
+    mis = [(raw.data_ptr() + 1, 1), (raw.data_ptr() + 1 + slab, 4)]
+    assert L.lib().qwb_pool_write_slabs(C.byref(d), slab, _copies(mis), 2, _stream()) == 0
+    got = pool.view(n_slots, slab).cpu().numpy()
+    assert np.array_equal(got[3], pageable[2]) and np.array_equal(got[0], pageable[1])
+    assert np.array_equal(got[1], D.slab_bytes(slab, 50)) and np.array_equal(got[4], D.slab_bytes(slab, 51))
+    assert not got[2].any()
+
+
+def test_pool_write_gather_partial_chunks_and_duplicates():
+    # the gather kernel: slab sizes that end inside a 64 KB chunk and inside a 4-load
+    # group, many slots (more than one launch's table of 128), duplicates keep the last
+    slab, n_slots = 16 * 1000 + 16, 300
+    pool = torch.zeros(slab * n_slots, dtype=torch.uint8, device="cuda")
+    d = _pool_desc(pool, slab, n_slots)
+    src = torch.from_numpy(np.concatenate([D.slab_bytes(slab, 200 + i) for i in range(260)])).cuda()
+    rng = np.random.default_rng(3)
+    slots = rng.choice(n_slots, 250, replace=False).tolist() + [7, 7, 11]
+    srcs = list(range(250)) + [250, 251, 252]
+    slots[5] = 11  # slot 11 named earlier too: the last entry (source 252) wins
+    entries = [(src.data_ptr() + i * slab, sl) for i, sl in zip(srcs, slots)]
+    assert L.lib().qwb_pool_write_slabs(C.byref(d), slab, _copies(entries), len(entries), _stream()) == 0
+    got = pool.view(n_slots, slab).cpu().numpy()
+    final = {}
+    for i, sl in zip(srcs, slots):
+        final[sl] = i
+    for sl, i in final.items():
+        assert np.array_equal(got[sl], D.slab_bytes(slab, 200 + i)), (sl, i)
+    untouched = [sl for sl in range(n_slots) if sl not in final]
+    assert not got[untouched].any()
+
+
 def _golden():
     with open(G) as f:
         return json.load(f)["cases"]

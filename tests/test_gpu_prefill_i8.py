@@ -70,6 +70,11 @@ CASES = [
     (O.Q6_K, 768, 2048, 8, 128, 4, 4),      # config-2 down shape
     (O.Q6_K, 1024, 300, 8, 256, 4, 1),
     (O.Q6_K, 2048, 128, 8, 64, 8, 8),
+    # 8 to 31 pairs per used expert: 8-token tiles (16-row warps, one 8-token MMA column)
+    (O.Q8_0, 1024, 300, 16, 40, 4, 1),      # 10 per expert, partial tiles and row blocks
+    (O.Q8_0, 4096, 128, 8, 12, 8, 8),       # 12 per expert, one activation row per pair
+    (O.Q6_K, 768, 2048, 16, 64, 4, 4),      # 16 per expert, config-2 down shape
+    (O.Q6_K, 2048, 300, 8, 16, 4, 1),       # exactly 8 per expert
 ]
 
 
@@ -107,9 +112,9 @@ def test_zipf_routing_against_reference_build(qwb, t):
     assert e <= TOL, (e, O.max_abs_rel(got, want))
 
 
-@pytest.mark.parametrize("t", [O.Q8_0, O.Q6_K])
-def test_matches_streaming_path(qwb, t):
-    K, M, n_as, T, n_used = 1024, 384, 8, 160, 8
+@pytest.mark.parametrize("t,T", [(O.Q8_0, 160), (O.Q6_K, 160), (O.Q8_0, 12), (O.Q6_K, 12)])
+def test_matches_streaming_path(qwb, t, T):
+    K, M, n_as, n_used = 1024, 384, 8, 8
     w = D.weights(t, n_as, M, K, seed=51)
     b = cu(D.acts((T, 1, K), seed=52))
     ids = cu(np.stack([D.rng(53 + i).permutation(n_as)[:n_used] for i in range(T)]).astype(np.int32))
