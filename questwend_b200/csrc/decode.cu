@@ -701,10 +701,37 @@ bool gateup_decode_supported(int type, int64_t K, size_t row_bytes, size_t nb1, 
     return (size_t) per_cta * 2 * row_bytes + 128 <= 200 * 1024;
 }
 
+// Shared memory per SM and reserved per CTA (228 KB and 1 KB on B200).
+static void sm_smem(size_t &per_sm, size_t &reserved) {
+    static int sm = 0, rsv = -1;
+    if (!sm) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+        cudaDeviceGetAttribute(&rsv, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+        if (sm <= 0) sm = 233472;
+        if (rsv < 0) rsv = 1024;
+    }
+    per_sm = (size_t) sm;
+    reserved = (size_t) rsv;
+}
+
 cudaError_t launch_gateup_decode(const GateUpDecodeArgs &a, cudaStream_t s) {
     const int G = num_sms();
     const int64_t per_cta = ceil_div((int64_t) a.n_used * a.F, G);
-    const size_t smem = 128 + (size_t) per_cta * 2 * a.row_bytes;
+    size_t smem = 128 + (size_t) per_cta * 2 * a.row_bytes;
+    // One gate/up CTA per SM.  At ~95 KB two of them fit one SM, and under programmatic
+    // launch (the router still holds 16 SMs when this grid starts) the block scheduler
+    // placed two on some SMs while others had none: those SMs streamed twice the bytes and
+    // set the layer's time.  Asking for just over half of an SM's shared memory keeps one
+    // per SM, while the down kernel launched after it still fits beside it (its weight
+    // copies overlap this kernel).  Measured on config 2 (48 layers, one B200, A/B on the
+    // same box): 975 -> 1103 tok/s.
+    size_t per_sm = 0, reserved = 0;
+    sm_smem(per_sm, reserved);
+    const size_t one_per_sm = per_sm / 2 - reserved + 256;
+    if (smem < one_per_sm && a.partner_smem && one_per_sm + a.partner_smem + 2 * reserved <= per_sm)
+        smem = one_per_sm;
     if (a.K == 2048) {
         cudaError_t e = set_smem(gateup_decode_kernel<8>, smem);
         if (e != cudaSuccess) return e;
@@ -719,6 +746,10 @@ static size_t down_decode_smem(int64_t H, int n_used, int nsb, size_t rb) {
     const int64_t n = ceil_div(H, num_sms());
     return 256 + (size_t) (kDecodeThreads / 32) * nsb * 320 + align_up((size_t) n_used * n * 4, 128) +
            (size_t) n_used * down_span_stride((int) n, rb);
+}
+
+size_t down_decode_smem_bytes(int64_t H, int n_used, size_t row_bytes) {
+    return down_decode_smem(H, n_used, 3, row_bytes);
 }
 
 bool down_decode_supported(int type, int64_t F, int64_t H, size_t row_bytes, size_t nb1, int n_used) {

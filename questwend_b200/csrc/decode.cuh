@@ -39,6 +39,7 @@ struct GateUpDecodeArgs {
     Q8Planes xq;
     float *act;             // [n_used][F]
     qwb_status_block *st;
+    size_t partner_smem;    // dynamic shared memory of the down kernel launched after it (0: unknown)
 };
 
 struct DownDecodeArgs {
@@ -59,5 +60,6 @@ bool gateup_decode_supported(int type, int64_t K, size_t row_bytes, size_t nb1, 
 cudaError_t launch_gateup_decode(const GateUpDecodeArgs &a, cudaStream_t s);
 bool down_decode_supported(int type, int64_t F, int64_t H, size_t row_bytes, size_t nb1, int n_used);
 cudaError_t launch_down_decode(int type, const DownDecodeArgs &a, cudaStream_t s);
+size_t down_decode_smem_bytes(int64_t H, int n_used, size_t row_bytes);
 
 }  // namespace qwb

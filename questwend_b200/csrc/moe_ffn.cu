@@ -299,6 +299,7 @@ extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, s
         g.g_nb2 = d->gate.nb[2]; g.u_nb2 = d->up.nb[2]; g.row_bytes = row_bytes(d->gate.type, H);
         g.F = F; g.K = H; g.n_slots_g = d->gate.ne[2]; g.n_slots_u = d->up.ne[2];
         g.n_used = (int) K; g.slots = slots; g.xq = xq; g.act = act; g.st = st;
+        g.partner_smem = down_decode_smem_bytes(H, (int) K, row_bytes(d->down.type, F));
         e = launch_gateup_decode(g, s);
         if (e != cudaSuccess) return QWB_ERR_CUDA;
         profile_mark(s, QWB_KERNEL_GATE_UP);
