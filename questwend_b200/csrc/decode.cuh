@@ -5,7 +5,9 @@
 
 namespace qwb {
 
-constexpr int kDecodeChunks = 4;    // weight copies per CTA are split into this many mbarrier chunks
+constexpr int kDecodeChunks = 1;    // mbarrier chunks of a gate/up CTA's weight copies: one (two bulk copies,
+                                    // gate and up spans) beat 2-3 (-4 %) and 4 (-9 %) and 8 (-19 %) on config 2:
+                                    // each bulk copy costs a fixed issue time, compute overlap gains less
 constexpr int kDecodeThreads = 256;  // gate/up and down CTAs: 8 warps, so both fit one SM together
 
 constexpr int kMaxRouteE = 512;     // experts the decode routing handles
