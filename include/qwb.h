@@ -289,8 +289,9 @@ QWB_API qwb_status qwb_moe_ep_experts(const qwb_moe_ep_experts_desc *desc, void 
  * memory) and 16-byte aligned, one kernel launch gathers the whole group, reading the
  * sources directly; otherwise one cudaMemcpyAsync per slab (pageable sources are staged
  * by the driver), the odd slots on a second stream of the library's, forked from
- * `stream` and joined back into it with events.  Either way, work queued on `stream`
- * after the call sees every slab.
+ * `stream` and joined back into it with events.  A source inside the pool itself (a slot
+ * copied to another slot) makes every copy run in array order on `stream`.  Either way,
+ * work queued on `stream` after the call sees every slab.
  * Arguments are checked before the first copy is issued: src_slab_bytes must equal
  * pool->nb[2] (QWB_ERR_SHAPE), every slot must lie in [0, pool->ne[2])
  * (QWB_ERR_INVALID_ARG), so an error writes nothing. */

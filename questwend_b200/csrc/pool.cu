@@ -226,7 +226,15 @@ extern "C" QWB_API qwb_status qwb_pool_write_slabs(const qwb_tensor *pool, size_
     char *base = (char *) pool->data;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= qwb::kMaxDevices) return QWB_ERR_CUDA;
-    {
+    // A source inside the pool (a slot copied to another slot) may be overwritten by an
+    // earlier entry: then every copy runs in array order on the caller's stream.
+    const uintptr_t lo = (uintptr_t) base, hi = lo + (uintptr_t) pool->ne[2] * nb2;
+    bool in_order = false;
+    for (int i = 0; i < n && !in_order; ++i) {
+        const uintptr_t a0 = (uintptr_t) copies[i].src;
+        in_order = a0 < hi && a0 + nb2 > lo;
+    }
+    if (!in_order) {
         // gather kernel: every source device-readable and 16-byte aligned, the slots too
         std::vector<const void *> view(n, nullptr);
         bool gather = nb2 % 16 == 0 && (uintptr_t) base % 16 == 0 && qwb::device_view(base, dev) == base;
@@ -265,7 +273,7 @@ extern "C" QWB_API qwb_status qwb_pool_write_slabs(const qwb_tensor *pool, size_
     std::lock_guard<std::mutex> lk(qwb::g_side_mu);
     qwb::SideStream &ss = qwb::g_side[dev];
     bool ok;
-    if (n == 1 || !qwb::side_ready(ss)) {
+    if (n == 1 || in_order || !qwb::side_ready(ss)) {
         ok = true;
         for (int i = 0; i < n && ok; ++i) ok = issue(i, s);
     } else {

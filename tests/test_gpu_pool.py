@@ -106,6 +106,23 @@ def test_pool_write_copy_engine_fallback():
     assert not got[2].any()
 
 
+def test_pool_write_slot_to_slot_in_array_order():
+    # sources inside the pool: copies run in array order, so slot 2 receives slot 0's bytes
+    # from before entry 1 overwrote slot 0
+    slab, n_slots = 4096, 4
+    init = np.concatenate([D.slab_bytes(slab, 60 + i) for i in range(n_slots)])
+    pool = torch.from_numpy(init).cuda()
+    d = _pool_desc(pool, slab, n_slots)
+    new0 = torch.from_numpy(D.slab_bytes(slab, 70)).cuda()
+    entries = [(pool.data_ptr(), 2), (new0.data_ptr(), 0), (pool.data_ptr() + 3 * slab, 1)]
+    assert L.lib().qwb_pool_write_slabs(C.byref(d), slab, _copies(entries), 3, _stream()) == 0
+    got = pool.view(n_slots, slab).cpu().numpy()
+    assert np.array_equal(got[2], D.slab_bytes(slab, 60))
+    assert np.array_equal(got[0], D.slab_bytes(slab, 70))
+    assert np.array_equal(got[1], D.slab_bytes(slab, 63))
+    assert np.array_equal(got[3], D.slab_bytes(slab, 63))
+
+
 def test_pool_write_gather_partial_chunks_and_duplicates():
     # the gather kernel: slab sizes that end inside a 64 KB chunk and inside a 4-load
     # group, many slots (more than one launch's table of 128), duplicates keep the last
