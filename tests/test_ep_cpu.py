@@ -1,8 +1,8 @@
-"""Expert parallelism: partition and exchange logic on CPU ranks (gloo, world size 2).
+"""Expert parallelism: partition and exchange logic on CPU ranks (gloo, world sizes 2 and 4).
 
-questwend_b200.expert_parallel.moe_layer runs unchanged on two CPU processes with a test
+questwend_b200.expert_parallel.moe_layer runs unchanged on 2 or 4 CPU processes with a test
 backend whose compute steps are the CPU oracle (rms_norm, router top-k, mul_mat_id on the
-rank's expert range, swiglu, masked weighted sum).  The outputs of the two ranks must
+rank's expert range, swiglu, masked weighted sum).  The outputs of the ranks must
 equal a one-rank run of the same backend over all tokens and all experts up to f32
 summation order (1e-6 normalized RMS), and that one-rank run must match the oracle's own
 build_moe layer (1e-4).  No GPU is involved."""
@@ -51,9 +51,9 @@ class OracleBackend:
         return torch.from_numpy(out)
 
 
-def _inputs():
+def _inputs(world):
     r = D.rng(11)
-    x = r.standard_normal((2 * T_RANK, H), dtype=np.float32)
+    x = r.standard_normal((world * T_RANK, H), dtype=np.float32)
     router_w = (r.standard_normal((E, H), dtype=np.float32) * 0.02).astype(np.float32)
     norm_w = (1.0 + 0.1 * r.standard_normal(H)).astype(np.float32)
     gate = D.weights(O.Q4_K, E, F, H, seed=12)
@@ -73,7 +73,7 @@ def _rank_main(rank, world, port, q):
 
     from questwend_b200.expert_parallel import moe_layer, shard_range
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
-    x, router_w, norm_w, gate, up, down = _inputs()
+    x, router_w, norm_w, gate, up, down = _inputs(world)
     lo, n = shard_range(E, world, rank)
     xs = torch.from_numpy(x[rank * T_RANK:(rank + 1) * T_RANK].copy())
     out, sel, w = moe_layer(xs, torch.from_numpy(router_w), _shard(gate, up, down, lo, n), K_USED, E,
@@ -89,27 +89,28 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_two_cpu_ranks_match_one_rank_and_oracle():
+@pytest.mark.parametrize("world", [2, 4])
+def test_cpu_ranks_match_one_rank_and_oracle(world):
     here = os.path.dirname(os.path.abspath(__file__))
     os.environ["PYTHONPATH"] = os.pathsep.join([os.path.dirname(here), here, os.environ.get("PYTHONPATH", "")])
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
-    for _ in range(2):
-        rank, out, sel = q.get(timeout=120)
+    for _ in range(world):
+        rank, out, sel = q.get(timeout=180)
         res[rank] = (out, sel)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    ep_out = np.concatenate([res[0][0], res[1][0]])
-    ep_sel = np.concatenate([res[0][1], res[1][1]])
+    ep_out = np.concatenate([res[r][0] for r in range(world)])
+    ep_sel = np.concatenate([res[r][1] for r in range(world)])
 
     # one rank, all experts: same backend, no exchange
-    x, router_w, norm_w, gate, up, down = _inputs()
+    x, router_w, norm_w, gate, up, down = _inputs(world)
     bk = OracleBackend()
     xn, sel, w = bk.prepare(torch.from_numpy(x), torch.from_numpy(router_w), K_USED, torch.from_numpy(norm_w), 1e-6, 0)
     single = bk.experts(xn, sel, w, _shard(gate, up, down, 0, E), E).numpy() + x
