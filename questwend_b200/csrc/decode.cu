@@ -669,11 +669,13 @@ size_t router_decode_smem(const RouterDecodeArgs &r) {
 
 cudaError_t launch_router_decode(const RouterDecodeArgs &r, cudaStream_t s) {
     const size_t smem = router_decode_smem(r);
-    static bool configured = false;
-    if (!configured) {
+    static bool configured[kAttrDevices] = {};  // per device: attributes hold for one device
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kAttrDevices) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
         cudaError_t e = cudaFuncSetAttribute(router_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
-        configured = true;
+        configured[dev] = true;
     }
     cudaError_t e = set_smem(router_decode_kernel, smem);
     if (e != cudaSuccess) return e;

@@ -41,6 +41,25 @@ cudaError_t launch_quantize_rows(int kind, const float *x, int64_t x_stride, int
 
 int num_sms();
 
+// cudaFuncSetAttribute changes a kernel's attribute on the current device only, so a
+// process that drives several GPUs must set it on each.  A launcher keeps one of these
+// per kernel: the largest dynamic shared-memory limit it has set, per device.
+constexpr int kAttrDevices = 64;
+struct DeviceSmemLimit {
+    size_t bytes[kAttrDevices] = {};
+};
+template <class Kernel>
+inline cudaError_t ensure_dyn_smem(Kernel kern, size_t smem, DeviceSmemLimit &limit) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kAttrDevices) return cudaErrorInvalidDevice;
+    if (smem <= limit.bytes[dev]) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    if (e == cudaSuccess) limit.bytes[dev] = smem;
+    return e;
+}
+
 // records a profiling mark when qwb_profile_enable is active (api.cu)
 void profile_mark(cudaStream_t s, int tag);
 

@@ -277,14 +277,11 @@ template <int TYPE, int NT, bool GLU>
 static cudaError_t launch_gemv_t(const GemvArgs &a, int max_items, cudaStream_t s) {
     auto kern = mmid_gemv_kernel<TYPE, NT, GLU>;
     const size_t smem = 128 + 2 * a.stage_bytes;
-    static size_t configured = 0;
-    if (smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-        if (e != cudaSuccess) return e;
-        configured = smem;
-    }
+    static DeviceSmemLimit limit;
+    cudaError_t e = ensure_dyn_smem(kern, smem, limit);
+    if (e != cudaSuccess) return e;
     int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     const int grid = std::max(1, std::min(max_items, per_sm * num_sms()));
@@ -372,11 +369,10 @@ cudaError_t launch_index(const int32_t *ids, int64_t s0, int64_t s1, int n_used,
                          MmidIndex ix, float *dst, size_t dnb1, size_t dnb2, int64_t M, qwb_status_block *st,
                          cudaStream_t s, int skip_neg) {
     const size_t smem = (size_t) 3 * n_as * 4;
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(mmid_index_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    static DeviceSmemLimit limit;
+    if (smem > 48 * 1024) {
+        cudaError_t e = ensure_dyn_smem(mmid_index_kernel, smem, limit);
         if (e != cudaSuccess) return e;
-        configured = smem;
     }
     mmid_index_kernel<<<1, 1024, smem, s>>>(ids, s0, s1, n_used, T, n_as, NT, ix, dst, dnb1, dnb2, M, st, skip_neg);
     return cudaGetLastError();

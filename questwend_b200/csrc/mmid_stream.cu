@@ -374,11 +374,10 @@ template <int TYPE, bool GLU>
 cudaError_t launch_stream_t(const GemvArgs &a, cudaStream_t s) {
     auto kern = mmid_stream_kernel<TYPE, GLU>;
     const size_t smem = (size_t) a.ring_off + (size_t) a.nslot * a.slot;
-    static size_t configured = 0;
-    if (smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    static DeviceSmemLimit limit;
+    {
+        cudaError_t e = ensure_dyn_smem(kern, smem, limit);
         if (e != cudaSuccess) return e;
-        configured = smem;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms());

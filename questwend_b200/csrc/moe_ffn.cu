@@ -148,14 +148,11 @@ template <int TYPE>
 static cudaError_t launch_down_t(DownArgs d, cudaStream_t s) {
     auto kern = moe_down_decode_kernel<TYPE>;
     const size_t smem = 128 + (size_t) d.smem_act + (size_t) d.n_used * d.wspan;
-    static size_t configured = 0;
-    if (smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-        if (e != cudaSuccess) return e;
-        configured = smem;
-    }
+    static DeviceSmemLimit limit;
+    cudaError_t e = ensure_dyn_smem(kern, smem, limit);
+    if (e != cudaSuccess) return e;
     int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     const int grid = std::max(1, std::min(d.n_rb, per_sm * num_sms()));

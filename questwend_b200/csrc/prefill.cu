@@ -654,12 +654,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_q4k_kernel(const Prefil
 }
 
 cudaError_t launch_pf_gemm_q4k(const PrefillArgs &a, cudaStream_t s) {
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(pf_gemm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    static DeviceSmemLimit limit;
+    cudaError_t e = ensure_dyn_smem(pf_gemm_q4k_kernel, (size_t) kPfSmem, limit);
+    if (e != cudaSuccess) return e;
     pf_gemm_q4k_kernel<<<num_sms(), kPfThreads, kPfSmem, s>>>(a);
     return cudaGetLastError();
 }

@@ -437,13 +437,9 @@ __global__ void __launch_bounds__(kI8Threads, 1) pf_i8_kernel(const I8PrefillArg
 template <int TYPE, int TN>
 cudaError_t launch_i8_t(const I8PrefillArgs &a, cudaStream_t s) {
     const size_t smem = sizeof(I8Smem<TYPE, TN>);
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e =
-            cudaFuncSetAttribute(pf_i8_kernel<TYPE, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    static DeviceSmemLimit limit;
+    cudaError_t e = ensure_dyn_smem(pf_i8_kernel<TYPE, TN>, smem, limit);
+    if (e != cudaSuccess) return e;
     pf_i8_kernel<TYPE, TN><<<num_sms(), kI8Threads, smem, s>>>(a);
     return cudaGetLastError();
 }
