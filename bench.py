@@ -1,7 +1,7 @@
 """Benchmark of the quantized-MoE expert hot path on B200 (and the reference CPU arm).
 
 Workload (one "step"): batch-1 decode of one token through the 48 MoE FFN layers of a
-Qwen3-30B-A3B-shaped decoder (BASELINE config 2): hidden 2048, 128 experts, top-8
+Qwen3-30B-A3B-shaped decoder: hidden 2048, 128 experts, top-8
 softmax routing with renormalisation, expert intermediate 768, Q4_K gate/up, Q6_K down,
 f32 router; each layer is QuestWend's ffn_norm + build_moe graph (rms_norm * ffn_norm
 weight -> router mul_mat -> route -> 3x mul_mat_id -> swiglu -> weighted sum) plus the
@@ -24,7 +24,7 @@ every step.  `roofline` is the gate/up GEMV kernel (the largest weight stream pe
 `cpu_baseline` times the reference's own ggml CPU backend (oracle/_ref, built from the
 reference sources) on one layer of the same shapes, scaled to 48 layers.
 
-`prefill` (rank 0): BASELINE config 3, the prefill grouped-GEMM sweep of MUL_MAT_ID on
+`prefill` (rank 0): the prefill grouped-GEMM sweep of MUL_MAT_ID on
 Q4_K experts (hidden 4096, 128 experts, top-8, expert intermediate 1536; gate/up shape
 [4096 -> 1536] with one activation row per token and down shape [1536 -> 4096] with one
 per (token, slot)), n_tokens in {512, 2048, 8192}, routing from Gumbel-perturbed
@@ -34,16 +34,16 @@ for the tensor-core kernel alone (event marks around it).  The weights of all 12
 (453 MB per matrix) exceed L2.  Its `roofline` compares the GEMM kernel with the measured
 dense bf16 peak; its `cpu_baseline` times the reference CPU backend on T = 512, gate shape.
 
-`decode_mmid` (rank 0): BASELINE config 4's expert shape (hidden 4096 -> expert FFN 1536,
+`decode_mmid` (rank 0): the large-model expert shape (hidden 4096 -> expert FFN 1536,
 128 Q4_K experts, top-8) as a decode-batch MUL_MAT_ID at T = 1, 8, 64 tokens, the path a
 ggml backend takes for a decode graph's MUL_MAT_ID nodes (weight streaming: each selected
 expert row read once for all its tokens).  GB/s counts the distinct expert weights per
 call; `frac` is against the measured HBM copy bandwidth, for the whole call (`us`) and for
 the streaming kernel alone (`kernel_us`).
 
-`gathers` (rank 0): BASELINE config 5 part 1 - GET_ROWS on a 151936 x 4096 table stored as
+`gathers` (rank 0): GET_ROWS on a 151936 x 4096 embedding table stored as
 Q4_K / Q6_K / Q8_0 with index streams of n = 1, 512, 8192 (uniform, 50 % repeats; bytes =
-n x (row + 16 KB f32 written + index)) - and config 2's Q6_K output head [2048 -> 151936]
+n x (row + 16 KB f32 written + index)) - and the decoder's Q6_K output head [2048 -> 151936]
 (255 MB) as quantized MUL_MAT at T = 1 and 8 tokens.
 """
 from __future__ import annotations
@@ -246,11 +246,11 @@ def prefill_experts(seed=7):
     return out
 
 
-MMID_TOKENS = (1, 8, 64)  # BASELINE config 4 decode batches
+MMID_TOKENS = (1, 8, 64)  # decode batches of the large-model expert shape
 
 
 def decode_mmid_sweep(q, lib, dev, tokens=MMID_TOKENS, n_pools=8):
-    """Decode-batch MUL_MAT_ID (BASELINE config 4 shape: hidden 4096 -> expert FFN 1536,
+    """Decode-batch MUL_MAT_ID (large-model expert shape: hidden 4096 -> expert FFN 1536,
     128 Q4_K experts, top-8 of uniform random routing) at T = 1, 8, 64 tokens: the
     weight-streaming path qwb_mul_mat_id takes for few tokens per expert.  Timed from CUDA
     graph replays of 8 calls; call i reads pool i of 8 identical expert pools, so the
@@ -333,7 +333,7 @@ def decode_mmid_sweep(q, lib, dev, tokens=MMID_TOKENS, n_pools=8):
             "peak": hbm, "peak_kind": kind, "points": points}
 
 
-VOCAB, EMB = 151936, 4096  # BASELINE config 5 embedding table; config 2 output head is VOCAB x H
+VOCAB, EMB = 151936, 4096  # embedding table rows x width; the decoder's output head is VOCAB x H
 GATHER_N = (1, 512, 8192)
 
 
@@ -364,7 +364,7 @@ def _graph_time(fn, n_call=8, reps=10):
 
 
 def gathers_sweep(q, dev):
-    """BASELINE config 5 part 1 and config 2's output head.
+    """GET_ROWS on the embedding table and the decoder's output head.
     GET_ROWS on a 151936 x 4096 table stored as Q4_K / Q6_K / Q8_0 (350 / 510 / 661 MB)
     with index streams of n = 1, 512, 8192 rows, uniform random with 50 % repeats; 8 index
     sets rotate between calls so the rows read are not L2 hits.  Bytes = n x (row bytes +
@@ -394,7 +394,7 @@ def gathers_sweep(q, dev):
             out["get_rows"].append({"type": {12: "Q4_K", 14: "Q6_K", 8: "Q8_0"}[t], "n": n, "us": 1e3 * ms,
                                     "gbs": nbytes / (ms * 1e-3) / 1e9, "frac": nbytes / (ms * 1e-3) / 1e9 / hbm})
         del tab, T
-    # output head (config 2): Q6_K [H = 2048 -> VOCAB]
+    # the decoder's output head: Q6_K [H = 2048 -> VOCAB]
     rows = synth_blocks(Q6_K, 512, H, rng)
     rb = rows.size // 512
     heads = []
@@ -550,7 +550,7 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu):
             points.append({"tokens": T, "shape": name, "ms": t_ms, "tflops": fl / (t_ms * 1e-3) / 1e12,
                            "gemm_ms": g_ms, "gemm_tflops": fl / (g_ms * 1e-3) / 1e12 if g_ms > 0 else None})
     L.check("qwb_profile_enable", lib.qwb_profile_enable(0))
-    # Q8_0 experts (config 3's second weight type), gate/up shape, and Q6_K experts, down
+    # Q8_0 experts (the sweep's second weight type), gate/up shape, and Q6_K experts, down
     # shape: the integer tensor-core kernel
     q8_points = []
     rng = np.random.default_rng(17)
@@ -760,13 +760,13 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="MoE layers per step (default 48; fewer only for profiling captures)")
-    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (config 3) sweep")
-    ap.add_argument("--no-mmid", action="store_true", help="skip the decode-batch MUL_MAT_ID (config 4) sweep")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill sweep")
+    ap.add_argument("--no-mmid", action="store_true", help="skip the decode-batch MUL_MAT_ID sweep")
     ap.add_argument("--no-gathers", action="store_true",
-                    help="skip the GET_ROWS (config 5) and output-head (config 2) measurements")
+                    help="skip the GET_ROWS and output-head measurements")
     ap.add_argument("--no-slabs", action="store_true", help="skip the expert pool write (slab upload) measurement")
     ap.add_argument("--only-prefill", action="store_true",
-                    help="run only the prefill (config 3) sweep, without its CPU baseline (profiling runs)")
+                    help="run only the prefill sweep, without its CPU baseline (profiling runs)")
     ap.add_argument("--only-mmid", action="store_true",
                     help="run only the decode-batch MUL_MAT_ID sweep and print its JSON (profiling runs)")
     ap.add_argument("--mmid-tokens", default=",".join(str(t) for t in MMID_TOKENS),

@@ -2,7 +2,7 @@
 // programmatic dependent launch (PDL).
 //
 // Reference: the same build_moe subgraph as moe_ffn.cu (core/runtime.cpp:2743-2816, ffn_norm
-// :2979), at the decode shape QuestWend runs per token (SURVEY config 1/2).  Decode is
+// :2979), at the batch-1 decode shape QuestWend runs per token.  Decode is
 // HBM-bound: per layer 8 experts x (gate + up + down) are streamed once.  Layout of the work:
 //
 //   router_decode   CTA = 2 router rows.  Before waiting on the previous kernel it
@@ -727,8 +727,8 @@ cudaError_t launch_gateup_decode(const GateUpDecodeArgs &a, cudaStream_t s) {
     // placed two on some SMs while others had none: those SMs streamed twice the bytes and
     // set the layer's time.  Asking for just over half of an SM's shared memory keeps one
     // per SM, while the down kernel launched after it still fits beside it (its weight
-    // copies overlap this kernel).  Measured on config 2 (48 layers, one B200, A/B on the
-    // same box): 975 -> 1103 tok/s.
+    // copies overlap this kernel).  Measured on the 30B-A3B decode stack (48 layers, one
+    // B200, A/B on the same box): 975 -> 1103 tok/s.
     size_t per_sm = 0, reserved = 0;
     sm_smem(per_sm, reserved);
     const size_t one_per_sm = per_sm / 2 - reserved + 256;

@@ -5,9 +5,10 @@
 
 namespace qwb {
 
-constexpr int kDecodeChunks = 1;    // mbarrier chunks of a gate/up CTA's weight copies: one (two bulk copies,
-                                    // gate and up spans) beat 2-3 (-4 %) and 4 (-9 %) and 8 (-19 %) on config 2:
-                                    // each bulk copy costs a fixed issue time, compute overlap gains less
+// mbarrier chunks of a gate/up CTA's weight copies.  One (two bulk copies: the gate and up
+// spans) beat 2-3 chunks (-4 %), 4 (-9 %) and 8 (-19 %) on the 30B-A3B decode stack: each
+// bulk copy costs a fixed issue time, and starting the dots on a first chunk gains less.
+constexpr int kDecodeChunks = 1;
 constexpr int kDecodeThreads = 256;  // gate/up and down CTAs: 8 warps, so both fit one SM together
 
 constexpr int kMaxRouteE = 512;     // experts the decode routing handles
