@@ -63,8 +63,8 @@ sys.path.insert(0, ROOT)
 import numpy as np  # noqa: E402
 
 H, F, E, K_USED, LAYERS = 2048, 768, 128, 8, 48
-# dram__bytes_read.sum + dram__bytes_write.sum of one gate/up decode launch, from the ncu
-# capture summarised in profiles/decode_moe_layer_v2_ncu.md (same kernel, same shapes)
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate/up decode launch, from an ncu
+# capture of this kernel at these shapes (48-layer stack, one token)
 GATEUP_TRAFFIC_BYTES = 14_179_840
 Q4_K, Q6_K = 12, 14
 ROW_GU = H // 256 * 144        # bytes per gate/up row
@@ -122,7 +122,7 @@ def quantized_experts(seed=0):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms while running."""
 
     def __init__(self, index):
         self.index, self.proc, self.lines = index, None, []
@@ -133,7 +133,7 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -174,51 +174,140 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_reference_layer_ms(threads, iters, layers_experts):
-    """ms per MoE layer of the reference ggml CPU backend (oracle/_ref), config-1 shapes."""
+def cpu_info():
+    """Host CPU model, logical CPU count and the ISA extensions the reference build uses."""
+    model, isa = None, []
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if model is None and ln.startswith("model name"):
+                    model = ln.split(":", 1)[1].strip()
+                if ln.startswith("flags"):
+                    fl = set(ln.split(":", 1)[1].split())
+                    isa = [x for x in ("avx2", "fma", "f16c", "avx512f", "avx512bw", "avx512_vnni",
+                                       "avx512_bf16", "amx_tile", "amx_int8") if x in fl]
+                    break
+    except OSError:
+        pass
+    return {"model": model, "logical_cpus": os.cpu_count(), "isa": isa}
+
+
+def host_threads():
+    """Threads the host can run at once for this process: the CPUs in its affinity mask,
+    capped by a cgroup CPU quota when one is set (spinning ggml worker threads beyond
+    what the quota allows slow the CPU backend down instead of speeding it up)."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    try:
+        with open("/sys/fs/cgroup/cpu.max") as f:
+            quota, period = f.read().split()[:2]
+        if quota != "max":
+            n = min(n, max(1, int(int(quota) // int(period))))
+    except (OSError, ValueError):
+        pass
+    return max(1, n)
+
+
+def stats(ms):
+    a = np.asarray(ms, dtype=np.float64)
+    return {"median": float(np.median(a)), "p10": float(np.percentile(a, 10)),
+            "p90": float(np.percentile(a, 90)), "n": int(a.size)}
+
+
+@functools.lru_cache(maxsize=1)
+def _cpu_decode_inputs():
+    g, u, d = quantized_experts()
+    reps = E // UNIQUE
+    gate, up, down = (np.tile(a, reps) for a in (g, u, d))
+    rng = np.random.default_rng(1)
+    rw = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((1, H)).astype(np.float32)
+    nw = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    return gate, up, down, rw, x, nw
+
+
+def cpu_decode_layer_times(threads, samples, warm=3):
+    """ms of each of `samples` evaluations of one MoE layer (config-1 shapes: ffn_norm,
+    router, top-8, Q4_K gate/up, Q6_K down, weighted sum) on the reference's ggml CPU
+    backend (oracle/_ref) with `threads` threads, after `warm` untimed evaluations."""
     import oracle as O
     if not O.ref_available():
         return None
     O.set_ref_threads(threads)
-    g, u, d = layers_experts
-    rng = np.random.default_rng(1)
-    rw = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
-    x = rng.standard_normal((1, H)).astype(np.float32)
-    reps = E // UNIQUE
-    nw = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
-    gate, up, down = (np.tile(a, reps) for a in (g, u, d))
-    r = O.moe_layer(x, rw, Q4_K, gate, up, Q6_K, down, F, E, K_USED, impl="ref", iters=iters,
-                    norm_w=nw, norm_eps=1e-6)
-    return r["ms"]
+    gate, up, down, rw, x, nw = _cpu_decode_inputs()
+    O.moe_layer(x, rw, Q4_K, gate, up, Q6_K, down, F, E, K_USED, impl="ref", iters=warm + samples,
+                norm_w=nw, norm_eps=1e-6)
+    return O.ref_last_times()[warm:]
+
+
+def cpu_prefill_times(threads, samples, warm=1):
+    """ms of each of `samples` reference CPU MUL_MAT_ID calls at T = 512, gate/up shape of
+    the prefill sweep (Q4_K, hidden 4096 -> 1536, 128 experts, top-8, Zipf routing)."""
+    import oracle as O
+    if not O.ref_available():
+        return None
+    O.set_ref_threads(threads)
+    T = PF_TOKENS[0]
+    ids = zipf_ids(T, E, K_USED, seed=T)
+    x = np.random.default_rng(3).standard_normal((T, 1, PF_H)).astype(np.float32)
+    w = np.tile(prefill_experts()[0], E // PF_UNIQUE)
+    O.mul_mat_id(Q4_K, w, PF_H, PF_F, E, x, ids, impl="ref", iters=warm + samples)
+    return O.ref_last_times()[warm:]
+
+
+def run_cpu_leg(args):
+    """--cpu-leg: the reference CPU timings for the GPU arm's cpu_baseline, in a process of
+    its own (no CUDA context, no torch threads): decode layer and prefill call, with all
+    host threads and with one."""
+    nproc = host_threads()
+    out = {"cpu": cpu_info()}
+    for name, threads, n in (("decode", nproc, 300), ("decode_1t", 1, 60)):
+        t = cpu_decode_layer_times(threads, n)
+        out[name] = None if t is None else dict(stats(t), threads=threads)
+    if not args.no_prefill:
+        for name, threads, n in (("prefill", nproc, 8), ("prefill_1t", 1, 2)):
+            t = cpu_prefill_times(threads, n)
+            out[name] = None if t is None else dict(stats(t), threads=threads)
+    print(json.dumps(out))
+
+
+def cpu_leg_subprocess(no_prefill):
+    """Runs --cpu-leg in a fresh interpreter and returns its JSON (None on failure)."""
+    cmd = [sys.executable, os.path.abspath(__file__), "--cpu-leg"] + (["--no-prefill"] if no_prefill else [])
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+        return json.loads(r.stdout.strip().splitlines()[-1])
+    except Exception as ex:  # the baseline is reported, never required
+        print(f"cpu leg failed: {ex}", file=sys.stderr)
+        return None
 
 
 def run_reference(args):
-    """--impl reference: the reference's own CPU path, all host threads, same workload."""
+    """--impl reference: the reference's own CPU path, all host threads, same workload.
+    A step = 5 evaluations of one MoE layer (config-1 shapes) scaled by the 48 layers."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     import oracle as O
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     if not O.ref_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (needs the reference sources)"}))
         return
-    experts = quantized_experts()
-    cpu_reference_layer_ms(threads, 2, experts)  # warm-up
-    per_step = []
+    cpu_decode_layer_times(threads, 5)  # first-touch of the 340 MB expert tables, thread pool start
     for _ in range(args.warmup):
-        cpu_reference_layer_ms(threads, 1, experts)
-    for _ in range(args.steps):
-        per_step.append(cpu_reference_layer_ms(threads, 5, experts) * LAYERS)
+        cpu_decode_layer_times(threads, 5, warm=1)
+    per_step = [float(np.mean(cpu_decode_layer_times(threads, 5, warm=1))) * LAYERS for _ in range(args.steps)]
     ms = float(np.mean(per_step))
     tok_s = 1000.0 / ms
-    sample = f"one MoE layer (config-1 shapes, Q4_K gate/up, Q6_K down) x 5 evaluations per step, scaled x{LAYERS} layers"
+    sample = (f"one MoE layer (config-1 shapes, Q4_K gate/up, Q6_K down) x 5 evaluations per step, "
+              f"scaled x{LAYERS} layers")
     print(json.dumps({
         "impl": "reference", "metric": "decode_tokens_per_s", "value": tok_s, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "step_ms": stats(per_step),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4_K/q6_K x q8_K -> f32",
         "data": "synthetic", "config": workload_config(args.gpus),
         "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "reference",
-                         "sample": sample},
+                         "sample": sample, "cpu": cpu_info()},
         "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
 
@@ -503,7 +592,8 @@ def slab_sweep(q, dev, iters=20):
             "audit_compare_ms": audit_ms[0], "audit_checksums_ms": audit_ms[1], "audit_equal": True}
 
 
-def prefill_sweep(q, lib, dev, warmup, iters, cpu):
+def prefill_sweep(q, lib, dev, warmup, iters, cpu=None):
+    """cpu: the --cpu-leg JSON (reference CPU timings), or None."""
     import ctypes as C
 
     import torch
@@ -616,21 +706,21 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu):
            "roofline": {"bound": "tensor", "kernel": f"grouped GEMM, gate/up shape, T={PF_TOKENS[-1]}",
                         "achieved": top["gemm_tflops"], "peak": peak, "peak_kind": pkind, "unit": "TFLOP/s",
                         "frac": top["gemm_tflops"] / peak if top["gemm_tflops"] else None, "traffic": None}}
-    if cpu:
-        import oracle as O
-        if O.ref_available():
-            threads = os.cpu_count() or 1
-            O.set_ref_threads(threads)
-            T = PF_TOKENS[0]
-            ids = zipf_ids(T, E, K_USED, seed=T)
-            x = np.random.default_rng(3).standard_normal((T, 1, PF_H)).astype(np.float32)
-            w = np.tile(experts[0], reps)
-            O.mul_mat_id(Q4_K, w, PF_H, PF_F, E, x, ids, impl="ref", iters=1)
-            _, ms = O.mul_mat_id(Q4_K, w, PF_H, PF_F, E, x, ids, impl="ref", iters=3)
-            fl = 2.0 * T * K_USED * PF_H * PF_F
-            res["cpu_baseline"] = {"value": fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "cores": threads,
-                                   "kind": "reference",
-                                   "sample": f"reference ggml CPU mul_mat_id, T={T}, gate shape, 3 calls ({ms:.1f} ms each)"}
+    gate_pts = [p for p in points if p["shape"] == "gate_up"]
+    res.update({"metric": "prefill_tflops", "value": top["tflops"], "unit": "TFLOP/s",
+                "value_what": f"whole qwb_mul_mat_id call, Q4_K gate/up shape, T={PF_TOKENS[-1]}",
+                "gemm_tflops": top["gemm_tflops"],
+                "by_tokens": {str(p["tokens"]): p["tflops"] for p in gate_pts}})
+    if cpu and cpu.get("prefill"):
+        c, T = cpu["prefill"], PF_TOKENS[0]
+        fl = 2.0 * T * K_USED * PF_H * PF_F
+        res["cpu_baseline"] = {"value": fl / (c["median"] * 1e-3) / 1e12, "unit": "TFLOP/s", "cores": c["threads"],
+                               "kind": "reference", "cpu": cpu.get("cpu"),
+                               "sample": f"reference ggml CPU mul_mat_id, T={T}, gate shape, median of {c['n']} calls "
+                                         f"({c['median']:.1f} ms)"}
+        if cpu.get("prefill_1t"):
+            c1 = cpu["prefill_1t"]
+            res["cpu_baseline"]["value_1_thread"] = fl / (c1["median"] * 1e-3) / 1e12
     return res
 
 
@@ -773,9 +863,19 @@ def main():
                     help="comma-separated token counts of the decode-batch MUL_MAT_ID sweep")
     ap.add_argument("--mmid-pools", type=int, default=8,
                     help="expert pools (453 MB each) the sweep rotates through between calls")
+    ap.add_argument("--cpu-leg", action="store_true",
+                    help="internal: print the reference CPU timings used by cpu_baseline and exit")
     args = ap.parse_args()
+    if args.cpu_leg:
+        return run_cpu_leg(args)
     if args.impl == "reference":
         return run_reference(args)
+    world0 = int(os.environ.get("WORLD_SIZE", "1"))
+    # the reference CPU timings first, in a process of their own, before this one touches
+    # the GPU (they are a reported baseline; the GPU timings below do not overlap them)
+    cpu_leg = None
+    if world0 == 1 and not args.no_cpu and not (args.only_mmid or args.only_prefill):
+        cpu_leg = cpu_leg_subprocess(args.no_prefill)
 
     import torch
     import torch.distributed as dist
@@ -797,7 +897,7 @@ def main():
         print(json.dumps({"decode_mmid": decode_mmid_sweep(q, lib, torch.device("cuda", local), mmid_tokens, args.mmid_pools)}))
         return
     if args.only_prefill:
-        print(json.dumps({"prefill": prefill_sweep(q, lib, torch.device("cuda", local), args.warmup, 10, cpu=False)}))
+        print(json.dumps({"prefill": prefill_sweep(q, lib, torch.device("cuda", local), args.warmup, 10)}))
         return
 
     # ---------------------------------------------------------------- weights
@@ -841,6 +941,8 @@ def main():
             if rc:
                 raise L.QwbError("qwb_moe_ffn", rc)
 
+    # clocks and throttle reasons sampled from the eager warm-up to the end of the e2e loop
+    clk = ClockSampler(local).__enter__()
     # eager warm-up, layer by layer with checks (also configures kernel attributes
     # outside capture)
     s_main = torch.cuda.current_stream()
@@ -880,15 +982,16 @@ def main():
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        torch.cuda.synchronize()
-        t0.record()
-        for _ in range(args.steps):
-            graph.replay()
-        t1.record()
-        torch.cuda.synchronize()
-    ms_step = t0.elapsed_time(t1) / args.steps
+    # an event after every replay: the step total and each step's time (median, p10, p90)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    torch.cuda.synchronize()
+    evs[0].record()
+    for i in range(args.steps):
+        graph.replay()
+        evs[i + 1].record()
+    torch.cuda.synchronize()
+    ms_step = evs[0].elapsed_time(evs[-1]) / args.steps
+    step_ms = stats([evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)])
     # per-kernel durations: replays of the profiled graph right after the timed region
     per_kernel = {}
     ms = (C.c_float * (n_rec - 1))()
@@ -914,6 +1017,7 @@ def main():
     e1.record()
     torch.cuda.synchronize()
     ms_e2e = e0.elapsed_time(e1) / args.steps
+    clk.__exit__(None, None, None)
 
     times = torch.tensor([ms_step, ms_e2e], device=dev)
     if world > 1:
@@ -938,12 +1042,13 @@ def main():
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "q4_K/q6_K x q8_K -> f32", "data": "synthetic (seeded quantized blocks: random codes, scales sized like quantized N(0,0.02))",
         "config": workload_config(world, n_layers),
+        "step_ms": step_ms,
         "decode_hbm_gbs": step_bytes / (ms_step * 1e-3) / 1e9,
         "decode_hbm_frac": step_bytes / (ms_step * 1e-3) / 1e9 / hbm,
         "roofline": {"bound": "hbm", "kernel": "moe gate/up GEMV (GLU) per layer", "achieved": achieved,
                      "peak": hbm, "peak_kind": kind, "unit": "GB/s",
                      "frac": achieved / hbm if achieved else None, "traffic": GATEUP_TRAFFIC_BYTES,
-                     "traffic_source": "ncu capture, profiles/decode_moe_layer_v2_ncu.md",
+                     "traffic_source": "ncu capture of this kernel (dram bytes read + written per launch)",
                      "algorithmic_bytes": gu_bytes},
         "kernels_us": {"router": 1e3 * float(np.mean(per_kernel.get(1, [0]))), "gate_up": 1e3 * (gu_ms or 0),
                        "down": 1e3 * (dn_ms or 0)},
@@ -954,16 +1059,21 @@ def main():
         "device_errors": flags,
         "clocks": clk.summary(),
     }
-    if rank == 0 and world == 1 and not args.no_cpu:
-        threads = os.cpu_count() or 1
-        lm = cpu_reference_layer_ms(threads, 20, (g, u, d))
-        if lm is not None:
-            result["cpu_baseline"] = {"value": 1000.0 / (lm * n_layers), "unit": "tokens/s", "cores": threads,
-                                      "kind": "reference",
-                                      "sample": f"one MoE layer x 20 evaluations ({lm:.3f} ms each), scaled x{n_layers}"}
+    if cpu_leg and cpu_leg.get("decode"):
+        c = cpu_leg["decode"]
+        result["cpu_baseline"] = {
+            "value": 1000.0 / (c["median"] * n_layers), "unit": "tokens/s", "cores": c["threads"],
+            "kind": "reference", "cpu": cpu_leg.get("cpu"),
+            "sample": f"one MoE layer on the reference ggml CPU backend, median of {c['n']} evaluations "
+                      f"after 3 untimed ({c['median']:.3f} ms; p10 {c['p10']:.3f}, p90 {c['p90']:.3f}), "
+                      f"scaled x{n_layers} layers"}
+        if cpu_leg.get("decode_1t"):
+            c1 = cpu_leg["decode_1t"]
+            result["cpu_baseline"]["value_1_thread"] = 1000.0 / (c1["median"] * n_layers)
+            result["cpu_baseline"]["layer_ms_1_thread"] = c1["median"]
     del graph, pgraph
     if rank == 0 and not args.no_prefill:
-        result["prefill"] = prefill_sweep(q, lib, dev, args.warmup, 10, cpu=(world == 1 and not args.no_cpu))
+        result["prefill"] = prefill_sweep(q, lib, dev, args.warmup, 10, cpu=cpu_leg)
     if rank == 0 and not args.no_mmid:
         result["decode_mmid"] = decode_mmid_sweep(q, lib, dev, mmid_tokens, args.mmid_pools)
     if rank == 0 and not args.no_gathers:

@@ -140,16 +140,22 @@ QWB_API qwb_status qwb_mul_mat_id(const qwb_tensor *as, const qwb_tensor *b, con
  * ggml backend inside graph_compute, code running under another framework's CUDA graph
  * capture (where cudaMalloc is not allowed), or a host whose device memory is all
  * committed to its expert-slot pool.  This entry point has no counterpart in the
- * reference; it computes exactly what qwb_mul_mat_id computes, using a fixed scratch
- * array of QWB_NOALLOC_SCRATCH_BYTES that the library's device image carries (the CUDA
- * driver reserves it on every GPU that loads the library, until the process exits).
- *   - Problems needing more than QWB_NOALLOC_SCRATCH_BYTES of workspace
- *     (qwb_mul_mat_id_workspace_size) return QWB_ERR_LIMIT.
+ * reference.  It always runs the GEMV / weight-streaming kernels (never the tensor-core
+ * GEMMs that qwb_mul_mat_id picks for many tokens per expert), so its results match
+ * qwb_mul_mat_id's to within fp32 summation order; its scratch is a fixed array of
+ * QWB_NOALLOC_SCRATCH_BYTES that the library's device image carries (the CUDA driver
+ * reserves it on every GPU that loads the library, until the process exits).
+ *   - The limit applies to the workspace of that GEMV plan.  qwb_mul_mat_id_workspace_size
+ *     returns the larger of that plan and the tensor-core one, so a problem it sizes at or
+ *     below QWB_NOALLOC_SCRATCH_BYTES is always accepted; a larger one may still be.
+ *     Problems beyond the limit return QWB_ERR_LIMIT before any work is queued.
  *   - All calls on a device share the array, which keeps the last call's contents (every
  *     byte a call reads it has written first); calls that overlap on the GPU race on it,
  *     so the caller must order them (one stream, or events).
  *   - The first call on each device resolves the array's address with that device
- *     current; make it before any stream capture.
+ *     current and keeps it for the life of the process; make it before any stream
+ *     capture, and do not use this entry point across a cudaDeviceReset of that device
+ *     (the array may be reloaded at another address).
  * No cudaMalloc, cudaFree or other allocating call is made. */
 #define QWB_NOALLOC_SCRATCH_BYTES (8u << 20) /* 8 MiB per device */
 QWB_API qwb_status qwb_mul_mat_id_noalloc(const qwb_tensor *as, const qwb_tensor *b,

@@ -116,6 +116,8 @@ def ref():
         vp, i64, i32, f32, f64 = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_double
         cp, ip = C.c_char_p, C.POINTER(C.c_int)
         lib.qref_set_threads.argtypes = [i32]
+        lib.qref_last_times.restype = i32
+        lib.qref_last_times.argtypes = [vp, i32]
         lib.qref_quantize.restype = C.c_size_t
         lib.qref_quantize.argtypes = [i32, vp, vp, i64, i64]
         lib.qref_from_float.argtypes = [i32, vp, vp, i64, i64]
@@ -335,6 +337,14 @@ def moe_layer(x, router_w, type_gu, gate, up, type_d, down, F, n_mat, n_used,
 
 def set_ref_threads(n: int):
     ref().qref_set_threads(n)
+
+
+def ref_last_times() -> np.ndarray:
+    """ms of each timed evaluation of the last reference call that was given iters > 0."""
+    n = ref().qref_last_times(None, 0)
+    out = np.zeros(max(n, 1), dtype=np.float64)
+    ref().qref_last_times(_p(out), n)
+    return out[:n]
 
 
 def nrmse(got: np.ndarray, want: np.ndarray) -> float:

@@ -75,19 +75,38 @@ struct Graph {
         buf = ggml_backend_alloc_ctx_tensors(ctx, cpu());
         for (auto & c : copies) ggml_backend_tensor_set(c.first, c.second, 0, ggml_nbytes(c.first));
     }
-    double compute(int iters) {
-        ggml_backend_graph_compute(cpu(), gf);  // warm-up (also the result for iters==0)
-        if (iters <= 0) return 0.0;
-        auto t0 = std::chrono::steady_clock::now();
-        for (int i = 0; i < iters; ++i) ggml_backend_graph_compute(cpu(), gf);
-        auto t1 = std::chrono::steady_clock::now();
-        return std::chrono::duration<double, std::milli>(t1 - t0).count() / iters;
-    }
+    // one untimed evaluation (also the result for iters == 0), then `iters` timed ones;
+    // returns the mean ms and keeps each evaluation's ms for qref_last_times
+    double compute(int iters);
 };
+
+std::vector<double> g_last_times;
+
+double Graph::compute(int iters) {
+    ggml_backend_graph_compute(cpu(), gf);
+    g_last_times.clear();
+    if (iters <= 0) return 0.0;
+    double total = 0.0;
+    for (int i = 0; i < iters; ++i) {
+        auto t0 = std::chrono::steady_clock::now();
+        ggml_backend_graph_compute(cpu(), gf);
+        auto t1 = std::chrono::steady_clock::now();
+        g_last_times.push_back(std::chrono::duration<double, std::milli>(t1 - t0).count());
+        total += g_last_times.back();
+    }
+    return total / iters;
+}
 
 }  // namespace
 
 extern "C" {
+
+// per-evaluation ms of the last timed call (at most n copied); returns how many it holds
+int qref_last_times(double * out, int n) {
+    const int have = (int) g_last_times.size();
+    for (int i = 0; i < have && i < n; ++i) out[i] = g_last_times[i];
+    return have;
+}
 
 void qref_set_threads(int n) {
     g_threads = n > 0 ? n : 1;

@@ -52,8 +52,16 @@ def build(force: bool = False, verbose: bool = False) -> str:
     nvcc = _nvcc()
     os.makedirs(OUT, exist_ok=True)
 
+    # a translation unit is recompiled when it, or any header, is newer than its object
+    headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
+    headers.append(os.path.join(HERE, "..", "include", "qwb.h"))
+    hdr_mtime = max(os.path.getmtime(f) for f in headers if os.path.exists(f))
+
     def compile_one(src):
         obj = os.path.join(OUT, os.path.basename(src) + ".o")
+        if (not force and os.path.exists(obj)
+                and os.path.getmtime(obj) >= max(os.path.getmtime(src), hdr_mtime)):
+            return obj
         cmd = [nvcc] + NVFLAGS + ["-c", src, "-o", obj]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:

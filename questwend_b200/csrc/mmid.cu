@@ -448,7 +448,9 @@ size_t qwb::mul_mat_id_workspace(const qwb_tensor *as, const qwb_tensor *b, cons
 
 extern "C" QWB_API size_t qwb_mul_mat_id_workspace_size(const qwb_tensor *as, const qwb_tensor *b,
                                                         const qwb_tensor *ids) {
-    return qwb::mul_mat_id_workspace(as, b, ids, true);
+    // the larger of the two plans (tensor-core kernels allowed, GEMV kernels only): the
+    // GEMV plan's expert index can be the larger one for rows too long to stream
+    return std::max(qwb::mul_mat_id_workspace(as, b, ids, true), qwb::mul_mat_id_workspace(as, b, ids, false));
 }
 
 qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor *ids,
