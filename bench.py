@@ -834,6 +834,72 @@ def run_ep(args, world, rank, local):
     dist.destroy_process_group()
 
 
+def run_ggml_leg(args):
+    """--ggml-leg: the decode stack and a prefill stack through ggml itself, the way
+    QuestWend runs them (ggml_backend_graph_compute on the whole graph), on two backends of
+    the same B200: the stock ggml-cuda backend (the reference's own GPU path: MMVQ / MMQ
+    kernels, Q8_1 activations), and libggml-qwb.so installed as the "cuda" backend beside
+    it (build_moe subgraphs fused into qwb_moe_ffn, everything else handed to ggml-cuda).
+    The host is the reference's own ggml library (compiled from its sources); weights are
+    the bench's seeded synthetic blocks (UNIQUE images per role, expert e of layer l =
+    image (e + l) mod UNIQUE).  Runs in a process of its own (it loads ggml's CUDA
+    backends next to nothing else)."""
+    import shutil
+    import tempfile
+
+    import oracle as O
+    if not O.ref_available():
+        print(json.dumps({"unavailable": "reference ggml (oracle/_ref) not built"}))
+        return
+    cuda_lib = os.path.join(ROOT, "oracle", "_ref", "cuda", "libggml-cuda.so")
+    qwb_lib = os.path.join(ROOT, "questwend_b200", "libggml-qwb.so")
+    if not (os.path.exists(cuda_lib) and os.path.exists(qwb_lib)):
+        print(json.dumps({"unavailable": "reference ggml-cuda build or libggml-qwb.so missing"}))
+        return
+    inst = tempfile.mkdtemp()
+    shutil.copy(qwb_lib, os.path.join(inst, "libggml-cuda-qwb.so"))
+    os.symlink(cuda_lib, os.path.join(inst, "libggml-cuda.so"))
+    os.symlink(os.path.join(ROOT, "questwend_b200", "libqwb.so"), os.path.join(inst, "libqwb.so"))
+    g, u, d = quantized_experts(seed=0)
+    rng = np.random.default_rng(2)
+    L = args.layers
+    rw = (rng.standard_normal((L, E, H)) * 0.02).astype(np.float32)
+    nw = (1.0 + 0.1 * rng.standard_normal((L, H))).astype(np.float32)
+    out = {"host": "reference ggml (ggml_backend_graph_compute on the whole stack graph)",
+           "config": {"layers": L, "hidden": H, "experts": E, "top_k": K_USED, "expert_ffn": F,
+                      "gate_up": "Q4_K", "down": "Q6_K"}, "points": []}
+    for T, iters in ((1, max(args.steps, 5)), (PF_GGML_T, 3)):
+        x = rng.standard_normal((T, H)).astype(np.float32)
+        res = {}
+        for name, path in (("stock_ggml_cuda", cuda_lib), ("qwb", os.path.join(inst, "libggml-cuda-qwb.so"))):
+            r = O.backend_moe_stack(path, L, H, F, E, K_USED, T, Q4_K, g, u, Q6_K, d, UNIQUE, rw, nw, x,
+                                    iters=iters)
+            res[name] = r
+            pt = {"backend": name, "tokens": T, "rc": r["rc"], "ms_per_pass": r["ms"],
+                  "tokens_per_s": T * 1000.0 / r["ms"] if r["ms"] > 0 else None, "passes": iters}
+            if name == "qwb":
+                pt["stats_per_pass"] = dict(zip(("fused_layers", "own_nodes", "delegated_nodes", "delegated_runs"),
+                                                [v / (iters + 1) for v in r["stats"][:4]]))
+            out["points"].append(pt)
+        if res["qwb"]["rc"] == 0 and res["stock_ggml_cuda"]["rc"] == 0:
+            out["points"][-1]["nrmse_vs_stock"] = O.nrmse(res["qwb"]["out"], res["stock_ggml_cuda"]["out"])
+    print(json.dumps(out))
+
+
+def ggml_leg_subprocess(args):
+    cmd = [sys.executable, os.path.abspath(__file__), "--ggml-leg", "--layers", str(args.layers),
+           "--steps", str(min(args.steps, 50))]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
+        return json.loads(r.stdout.strip().splitlines()[-1])
+    except Exception as ex:  # reported, never required
+        print(f"ggml leg failed: {ex}", file=sys.stderr)
+        return None
+
+
+PF_GGML_T = 2048  # the prefill batch of the decoder workload
+
+
 def workload_config(n, n_layers=LAYERS):
     return {"workload": "qwen3-30b-a3b MoE FFN stack, batch-1 decode", "layers": n_layers, "hidden": H,
             "experts": E, "top_k": K_USED, "expert_ffn": F, "gate_up": "Q4_K", "down": "Q6_K",
@@ -865,9 +931,15 @@ def main():
                     help="expert pools (453 MB each) the sweep rotates through between calls")
     ap.add_argument("--cpu-leg", action="store_true",
                     help="internal: print the reference CPU timings used by cpu_baseline and exit")
+    ap.add_argument("--ggml-leg", action="store_true",
+                    help="internal: time the stack through ggml on the stock ggml-cuda backend and on "
+                         "libggml-qwb.so, print the JSON and exit")
+    ap.add_argument("--no-ggml", action="store_true", help="skip the ggml drop-in comparison")
     args = ap.parse_args()
     if args.cpu_leg:
         return run_cpu_leg(args)
+    if args.ggml_leg:
+        return run_ggml_leg(args)
     if args.impl == "reference":
         return run_reference(args)
     world0 = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1080,6 +1152,11 @@ def main():
         result["gathers"] = gathers_sweep(q, dev)
     if rank == 0 and not args.no_slabs:
         result["slab_upload"] = slab_sweep(q, dev)
+    if rank == 0 and not args.no_ggml:
+        # the GPU memory this process holds is released first: the leg loads 2 x 16 GB stacks
+        del layers, descs, ws, base
+        torch.cuda.empty_cache()
+        result["ggml_dropin"] = ggml_leg_subprocess(args)
     if rank == 0:
         print(json.dumps(result))
     if world > 1:

@@ -18,7 +18,9 @@
  *     default stream), performs no host synchronisation, no device allocation and no
  *     host read-back of device data, so it can be captured in a CUDA graph.
  *   - Scratch memory is caller-owned ("workspace"); sizes come from the *_workspace_size
- *     queries.  Workspaces must be 256-byte aligned.
+ *     queries.  Workspaces must be 256-byte aligned, and their first 256 bytes (a control
+ *     block of the fused MoE layer's kernels, which leave it zeroed) must be zero before
+ *     the first call that uses them: clear a new workspace once.
  *   - Host-detectable errors (bad type, shape, stride, alignment, workspace) return a
  *     qwb_status and launch nothing.  Data-dependent errors found on the device (an
  *     expert / row id out of range) never fault: the kernel skips the access, writes

@@ -137,6 +137,10 @@ def ref():
         lib.qref_mul_mat.argtypes = [i32, vp, i64, i64, vp, i64, vp, i32]
         lib.qref_backend_mul_mat.argtypes = [cp, i32, vp, i64, i64, vp, i64, vp]
         lib.qref_backend_sched_mul_mat_id.argtypes = [cp, i32, vp, i64, i64, i64, vp, i64, vp, i64, f32, vp, ip, ip]
+        lib.qref_backend_moe_stack.argtypes = [cp, cp, i32, i64, i64, i64, i64, i64, i32, vp, vp, i32, vp, i64,
+                                               vp, vp, vp, vp, i64, vp, vp, i32, C.POINTER(C.c_double),
+                                               C.POINTER(C.c_uint64)]
+        lib.qref_dropin_first_gpu.argtypes = [cp, C.c_char_p, i32]
         _ref = lib
     return _ref
 
@@ -280,6 +284,37 @@ def backend_sched_mul_mat_id(path: str, t: int, w: np.ndarray, K: int, M: int, n
     rc = ref().qref_backend_sched_mul_mat_id(path.encode(), t, _p(w), K, M, n_as, _p(b), T, _p(ids), n_used,
                                              scale, _p(dst), C.byref(n_splits), C.byref(on_backend))
     return dst, rc, n_splits.value, bool(on_backend.value)
+
+
+def backend_moe_stack(path, L, H, F, E, n_used, T, type_gu, gate_u, up_u, type_d, down_u, n_unique,
+                      router_w, norm_w, x, g2s=None, n_slots=0, iters=0, params=None):
+    """A stack of L QuestWend MoE FFN blocks (ffn_norm, build_moe, residual) computed by
+    the ggml backend library at `path` (None: the reference's CPU backend).  Expert e of
+    layer l is image (e + l) % n_unique of gate_u / up_u / down_u.  g2s [L][3][E] selects
+    the expert-cache branch (slot pools of n_slots, T = 1).  Returns dict(rc, out [T, H],
+    selected [L, n_used] (cache branch), ms per run, stats: fused layers, nodes run one at
+    a time on libqwb.so, nodes delegated, delegated runs, delegating mode)."""
+    out = np.zeros((T, H), dtype=np.float32)
+    sel = np.zeros((L, n_used), dtype=np.int32)
+    ms = C.c_double(0.0)
+    st = (C.c_uint64 * 5)()
+    g = None if g2s is None else np.ascontiguousarray(g2s, dtype=np.int32)
+    rw = np.ascontiguousarray(router_w, dtype=np.float32)
+    nw = np.ascontiguousarray(norm_w, dtype=np.float32)
+    xx = np.ascontiguousarray(x, dtype=np.float32)
+    rc = ref().qref_backend_moe_stack(None if path is None else path.encode(),
+                                      None if params is None else params.encode(), L, H, F, E, n_used, T,
+                                      type_gu, _p(gate_u), _p(up_u), type_d, _p(down_u), n_unique, _p(rw), _p(nw),
+                                      _p(xx), _p(g), n_slots, _p(out), _p(sel), iters, C.byref(ms), st)
+    return dict(rc=rc, out=out, selected=sel, ms=ms.value, stats=list(st))
+
+
+def dropin_first_gpu(directory: str) -> str:
+    """ggml_backend_load_all_from_path(directory), then the name of the first GPU device
+    that initialises: the device QuestWend's runtime takes (core/runtime.cpp:996-1010)."""
+    buf = C.create_string_buffer(256)
+    rc = ref().qref_dropin_first_gpu(directory.encode(), buf, 256)
+    return buf.value.decode() if rc == 0 else f"<error {rc}>"
 
 
 def route(logits: np.ndarray, n_used: int, norm: bool = True, scale: float = 0.0,

@@ -24,6 +24,8 @@
 #include "ggml-backend.h"
 #include "ggml-cpu.h"
 
+#include <algorithm>
+
 #include <chrono>
 #include <cmath>
 #include <cstdint>
@@ -336,11 +338,11 @@ static ggml_backend_reg_t load_backend_once(const char * path) {
     return reg;
 }
 
-static ggml_backend_t backend_open(const char * path, int * rc) {
+static ggml_backend_t backend_open(const char * path, int * rc, const char * params = "workspace_mb=512") {
     ggml_backend_reg_t reg = load_backend_once(path);
     if (!reg) { *rc = -1; return nullptr; }
     if (ggml_backend_reg_dev_count(reg) == 0) { *rc = -2; return nullptr; }
-    ggml_backend_t be = ggml_backend_dev_init(ggml_backend_reg_dev_get(reg, 0), "workspace_mb=64");
+    ggml_backend_t be = ggml_backend_dev_init(ggml_backend_reg_dev_get(reg, 0), params);
     *rc = be ? 0 : -3;
     return be;
 }
@@ -507,6 +509,212 @@ int qref_backend_sched_mul_mat_id(const char * path, int type, const void * as, 
     ggml_backend_free(cb);
     ggml_backend_free(be);
     return rc;
+}
+
+
+// ------------------------------------------------------------------------------------
+// A stack of L decoder MoE FFN blocks as QuestWend builds them (core/runtime.cpp:
+// 2972-2993 around build_moe :2743-2816):
+//     cur = scale(cur, 1) (a stand-in for the attention block: an op outside the MoE path)
+//     ffn_in = rms_norm(cur) * ffn_norm;  cur = build_moe(ffn_in) + cur
+// computed by the backend library at `path` (ggml_backend_load), or by the CPU backend
+// when path is NULL.  Graph tensors are placed by ggml's graph allocator (gallocr, with
+// memory reuse, as QuestWend's runtime does); weights sit in a buffer marked as weights.
+//   expert matrices: n_unique distinct byte images per role; expert e of layer l is image
+//     (e + l) % n_unique (gate/up [H, F] type_gu, down [F, H] type_d)
+//   g2s == NULL: the resident branch, T tokens, expert tensors [.., .., E]
+//   g2s != NULL: the expert-cache branch (T = 1): slot pools [.., .., n_slots], one I32
+//     table per (layer, role) in g2s_all [1, E, 3L] (g2s: [L][3][E]), and every layer's
+//     selection copied into sel_all [n_used, L] (read back into `selected`)
+// router_w [L][E][H], norm_w [L][H], x [T][H] -> out [T][H].  Runs the graph once, then
+// `iters` timed times (synchronised each time, the input set before each, outside the
+// timing): *ms = mean ms per run.  stats (5 values,
+// may be NULL): the QWB backend's counters (fused layers, own nodes, delegated nodes,
+// delegated runs) and whether it delegates, all zero for other backends.
+int qref_backend_moe_stack(const char * path, const char * params, int L, int64_t H, int64_t F, int64_t E,
+                           int64_t n_used, int64_t T, int type_gu, const void * gate_u, const void * up_u,
+                           int type_d, const void * down_u, int64_t n_unique, const float * router_w,
+                           const float * norm_w, const float * x, const int32_t * g2s, int64_t n_slots,
+                           float * out, int32_t * selected, int iters, double * ms, uint64_t * stats) {
+    int rc = 0;
+    ggml_backend_t be = nullptr;
+    ggml_backend_reg_t reg = nullptr;
+    if (path) {
+        be = backend_open(path, &rc, params ? params : "workspace_mb=512");
+        if (!be) return rc;
+        reg = load_backend_once(path);
+    } else {
+        be = ggml_backend_cpu_init();
+        ggml_backend_cpu_set_n_threads(be, g_threads);
+    }
+    const bool cache = g2s != nullptr;
+    if (cache && T != 1) { ggml_backend_free(be); return -6; }
+    const int64_t NE = cache ? n_slots : E;
+    const size_t rb_gu = ggml_row_size((ggml_type) type_gu, H), rb_d = ggml_row_size((ggml_type) type_d, F);
+    const size_t ex_gu = rb_gu * F, ex_d = rb_d * H;
+
+    ggml_init_params wp = {ggml_tensor_overhead() * (6 * (size_t) L + 4), nullptr, true};
+    ggml_context * wctx = ggml_init(wp);
+    std::vector<ggml_tensor *> tg(L), tu(L), td(L), trw(L), tnw(L);
+    for (int l = 0; l < L; ++l) {
+        tg[l] = ggml_new_tensor_3d(wctx, (ggml_type) type_gu, H, F, NE);
+        tu[l] = ggml_new_tensor_3d(wctx, (ggml_type) type_gu, H, F, NE);
+        td[l] = ggml_new_tensor_3d(wctx, (ggml_type) type_d, F, H, NE);
+        trw[l] = ggml_new_tensor_2d(wctx, GGML_TYPE_F32, H, E);
+        tnw[l] = ggml_new_tensor_1d(wctx, GGML_TYPE_F32, H);
+    }
+    ggml_tensor * g2s_all = cache ? ggml_new_tensor_3d(wctx, GGML_TYPE_I32, 1, E, 3 * L) : nullptr;
+    ggml_tensor * sel_all = cache ? ggml_new_tensor_2d(wctx, GGML_TYPE_I32, n_used, L) : nullptr;
+    ggml_backend_buffer_type_t bt = ggml_backend_get_default_buffer_type(be);
+    ggml_backend_buffer_t wbuf = ggml_backend_alloc_ctx_tensors_from_buft(wctx, bt);
+    ggml_context * ctx = nullptr;
+    ggml_gallocr_t galloc = nullptr;
+    if (!wbuf) {
+        rc = -4;
+    } else {
+        ggml_backend_buffer_set_usage(wbuf, GGML_BACKEND_BUFFER_USAGE_WEIGHTS);
+        const uint8_t * img[3] = {(const uint8_t *) gate_u, (const uint8_t *) up_u, (const uint8_t *) down_u};
+        for (int l = 0; l < L; ++l) {
+            for (int64_t s = 0; s < NE; ++s) {
+                // slot s holds expert e: the identity, or the expert the layer's table sends to s
+                int64_t e = s;
+                if (cache)
+                    for (int64_t k = 0; k < E; ++k)
+                        if (g2s[((size_t) l * 3 + 0) * E + k] == s) e = k;
+                const int64_t u = (e + l) % n_unique;
+                ggml_backend_tensor_set(tg[l], img[0] + u * ex_gu, s * ex_gu, ex_gu);
+                ggml_backend_tensor_set(tu[l], img[1] + u * ex_gu, s * ex_gu, ex_gu);
+                ggml_backend_tensor_set(td[l], img[2] + u * ex_d, s * ex_d, ex_d);
+            }
+            ggml_backend_tensor_set(trw[l], router_w + (size_t) l * E * H, 0, ggml_nbytes(trw[l]));
+            ggml_backend_tensor_set(tnw[l], norm_w + (size_t) l * H, 0, ggml_nbytes(tnw[l]));
+        }
+        if (cache) ggml_backend_tensor_set(g2s_all, g2s, 0, ggml_nbytes(g2s_all));
+
+        ggml_init_params ip = {ggml_tensor_overhead() * (64 * (size_t) L + 64) + ggml_graph_overhead_custom(8192, false),
+                               nullptr, true};
+        ctx = ggml_init(ip);
+        ggml_cgraph * gf = ggml_new_graph_custom(ctx, 8192, false);
+        ggml_tensor * inp = ggml_new_tensor_2d(ctx, GGML_TYPE_F32, H, T);
+        ggml_set_input(inp);
+        ggml_tensor * cur = inp;
+        for (int l = 0; l < L; ++l) {
+            // stand-in for the attention block between MoE blocks (nodes a MoE backend hands
+            // on): an identity scale
+            cur = ggml_scale(ctx, cur, 1.0f);
+            ggml_tensor * ffn_in = ggml_mul(ctx, ggml_rms_norm(ctx, cur, 1e-6f), tnw[l]);
+            // route_experts (runtime.cpp:2693-2734): softmax gating, expert_weights_norm
+            ggml_tensor * logits = ggml_mul_mat(ctx, trw[l], ffn_in);
+            ggml_tensor * probs = ggml_soft_max(ctx, logits);
+            ggml_tensor * sel = ggml_argsort_top_k(ctx, probs, n_used);
+            ggml_tensor * w = ggml_get_rows(ctx, ggml_reshape_3d(ctx, probs, 1, E, T), sel);
+            w = ggml_reshape_2d(ctx, w, n_used, T);
+            ggml_tensor * ws = ggml_clamp(ctx, ggml_sum_rows(ctx, w), 6.103515625e-5f, INFINITY);
+            w = ggml_reshape_3d(ctx, ggml_div(ctx, w, ws), 1, n_used, T);
+            ggml_build_forward_expand(gf, w);
+            ggml_tensor * moe;
+            if (cache) {
+                ggml_tensor * sel_col = ggml_view_2d(ctx, sel_all, n_used, 1, sel_all->nb[1], (size_t) l * sel_all->nb[1]);
+                ggml_build_forward_expand(gf, ggml_cpy(ctx, sel, sel_col));
+                auto remap = [&](int role) {
+                    const int idx = l * 3 + role;
+                    ggml_tensor * tab = ggml_view_2d(ctx, g2s_all, 1, E, g2s_all->nb[1], (size_t) idx * g2s_all->nb[2]);
+                    return ggml_reshape_2d(ctx, ggml_get_rows(ctx, tab, sel), n_used, 1);
+                };
+                ggml_tensor * sg = remap(0), * su = remap(1), * sd = remap(2);
+                ggml_tensor * x3 = ggml_reshape_3d(ctx, ffn_in, H, 1, 1);
+                ggml_tensor * up = ggml_mul_mat_id(ctx, tu[l], x3, su);
+                ggml_tensor * gate = ggml_mul_mat_id(ctx, tg[l], x3, sg);
+                ggml_tensor * act = ggml_swiglu_split(ctx, gate, up);
+                ggml_tensor * experts = ggml_mul_mat_id(ctx, td[l], act, sd);
+                ggml_tensor * et = ggml_cont(ctx, ggml_transpose(ctx, ggml_reshape_2d(ctx, experts, H, n_used)));
+                moe = ggml_mul_mat(ctx, et, ggml_reshape_2d(ctx, w, n_used, 1));
+            } else {
+                ggml_tensor * x3 = ggml_reshape_3d(ctx, ffn_in, H, 1, T);
+                ggml_tensor * up = ggml_mul_mat_id(ctx, tu[l], x3, sel);
+                ggml_tensor * gate = ggml_mul_mat_id(ctx, tg[l], x3, sel);
+                ggml_tensor * act = ggml_swiglu_split(ctx, gate, up);
+                ggml_tensor * experts = ggml_mul_mat_id(ctx, td[l], act, sel);
+                if (T == 1) {
+                    ggml_tensor * et = ggml_cont(ctx, ggml_transpose(ctx, ggml_reshape_2d(ctx, experts, H, n_used)));
+                    moe = ggml_mul_mat(ctx, et, ggml_reshape_2d(ctx, w, n_used, 1));
+                } else {
+                    experts = ggml_mul(ctx, experts, w);
+                    ggml_build_forward_expand(gf, experts);
+                    std::vector<ggml_tensor *> v(n_used);
+                    for (int64_t i = 0; i < n_used; ++i) {
+                        v[i] = ggml_view_2d(ctx, experts, H, T, experts->nb[2], (size_t) i * experts->nb[1]);
+                        ggml_build_forward_expand(gf, v[i]);
+                    }
+                    moe = v[0];
+                    for (int64_t i = 1; i < n_used; ++i) {
+                        moe = ggml_add(ctx, moe, v[i]);
+                        ggml_build_forward_expand(gf, moe);
+                    }
+                    if (n_used == 1) moe = ggml_cont(ctx, moe);
+                }
+            }
+            cur = ggml_add(ctx, moe, cur);
+        }
+        ggml_set_output(cur);
+        ggml_build_forward_expand(gf, cur);
+        galloc = ggml_gallocr_new(bt);
+        if (!ggml_gallocr_alloc_graph(galloc, gf)) {
+            rc = -4;
+        } else {
+            ggml_backend_tensor_set(inp, x, 0, ggml_nbytes(inp));
+            if (ggml_backend_graph_compute(be, gf) != GGML_STATUS_SUCCESS) rc = -5;
+            ggml_backend_synchronize(be);
+            double total = 0.0;
+            for (int i = 0; i < iters && rc == 0; ++i) {
+                // inputs are set before every compute: the graph allocator may reuse an
+                // input's memory once its last reader has run
+                ggml_backend_tensor_set(inp, x, 0, ggml_nbytes(inp));
+                auto t0 = std::chrono::steady_clock::now();
+                if (ggml_backend_graph_compute(be, gf) != GGML_STATUS_SUCCESS) rc = -5;
+                ggml_backend_synchronize(be);
+                total += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+            }
+            if (ms) *ms = iters > 0 ? total / iters : 0.0;
+            if (rc == 0) {
+                ggml_backend_tensor_get(cur, out, 0, ggml_nbytes(cur));
+                if (cache && selected) ggml_backend_tensor_get(sel_all, selected, 0, ggml_nbytes(sel_all));
+            }
+        }
+    }
+    if (stats) {
+        for (int k = 0; k < 5; ++k) stats[k] = 0;
+        if (reg) {
+            typedef int (*stats_fn)(ggml_backend_t, uint64_t *, int);
+            typedef int (*deleg_fn)();
+            if (auto f = (stats_fn) ggml_backend_reg_get_proc_address(reg, "ggml_backend_qwb_get_stats")) f(be, stats, 4);
+            if (auto f = (deleg_fn) ggml_backend_reg_get_proc_address(reg, "ggml_backend_qwb_is_delegating")) stats[4] = f();
+        }
+    }
+    if (galloc) ggml_gallocr_free(galloc);
+    if (ctx) ggml_free(ctx);
+    if (wbuf) ggml_backend_buffer_free(wbuf);
+    ggml_free(wctx);
+    ggml_backend_free(be);
+    return rc;
+}
+
+
+// QuestWend's device choice (core/runtime.cpp:944-957, 996-1010) after loading every
+// backend library in `dir` the way ggml_backend_load_all() does: the first GPU device
+// that initialises.  Writes its name; returns 0, or -1 when no GPU device initialised.
+int qref_dropin_first_gpu(const char * dir, char * name, int cap) {
+    ggml_backend_load_all_from_path(dir);
+    for (size_t i = 0; i < ggml_backend_dev_count(); ++i) {
+        ggml_backend_dev_t dev = ggml_backend_dev_get(i);
+        if (ggml_backend_dev_type(dev) != GGML_BACKEND_DEVICE_TYPE_GPU) continue;
+        ggml_backend_t be = ggml_backend_dev_init(dev, nullptr);
+        if (!be) continue;
+        snprintf(name, (size_t) cap, "%s", ggml_backend_dev_name(dev));
+        ggml_backend_free(be);
+        return 0;
+    }
+    return -1;
 }
 
 }  // extern "C"

@@ -146,6 +146,9 @@ struct Scratch {
         ws = nullptr;
         ws_bytes = 0;
         if (!cuda_ok(cudaMalloc(&ws, need), "cudaMalloc(workspace)")) return false;
+        // the fused layer keeps a control block at the start of its workspace, zero
+        // between calls (its kernels leave it zeroed)
+        if (!cuda_ok(cudaMemset(ws, 0, need), "cudaMemset(workspace)")) return false;
         ws_bytes = need;
         return true;
     }
@@ -252,13 +255,17 @@ struct Uses {
 
 struct MoeRegion {
     ggml_tensor *x = nullptr, *router_w = nullptr, *wg = nullptr, *wu = nullptr, *wd = nullptr;
-    ggml_tensor *out = nullptr;      // the weighted sum (moe_out)
-    ggml_tensor *sel = nullptr;      // [n_used, T] i32 view of the argsort
-    ggml_tensor *weights = nullptr;  // [1, n_used, T] normalised routing weights
-    const int32_t *g2s = nullptr;    // gate, up, down tables, consecutive (slot-remap branch)
+    ggml_tensor *out = nullptr;       // moe_out, or the residual add when that is absorbed
+    ggml_tensor *sel = nullptr;       // [n_used, T] i32 view of the argsort
+    ggml_tensor *weights = nullptr;   // [1, n_used, T] normalised routing weights
+    ggml_tensor *norm_w = nullptr;    // ffn_norm weight when rms_norm * ffn_norm is absorbed (x: its input)
+    ggml_tensor *residual = nullptr;  // the residual add's other operand when the add is absorbed
+    float norm_eps = 0.f;
+    const int32_t *g2s = nullptr;     // gate, up, down tables, consecutive (slot-remap branch)
     int64_t H = 0, F = 0, E = 0, n_used = 0, T = 0;
     std::vector<ggml_tensor *> nodes;
-    int first = 0;  // node index where the fused call runs (the router mul_mat)
+    int first = 0;        // node index where the fused call runs (the layer's first node)
+    bool direct = false;  // the layer's nodes are consecutive: results written in place
     bool sel_out = false, weights_out = false;  // read after the layer: materialise
 };
 
@@ -427,6 +434,39 @@ bool match_moe(const Uses &u, ggml_tensor *D, MoeRegion &r) {
     }
     if (!f32_contig(r.out) || r.out->ne[0] != r.H || r.out->ne[1] != r.T) return false;
 
+    ggml_tensor *head = logits;  // the layer's first node: it reads only inputs from outside
+    // ffn_in = rms_norm(cur) * ffn_norm (runtime.cpp:2979) when nothing else reads it (a
+    // shared expert does), and l_out = moe_out + cur (:2993): one qwb_moe_ffn call then
+    // covers the whole block, its router normalising on the fly
+    {
+        ggml_tensor *xm = r.x, *rn = xm->src[0], *nw = xm->src[1];
+        bool only_region = is_op(xm, GGML_OP_MUL) && is_op(rn, GGML_OP_RMS_NORM) && u.only(rn) == xm &&
+                           !(xm->flags & GGML_TENSOR_FLAG_OUTPUT) && !(rn->flags & GGML_TENSOR_FLAG_OUTPUT) &&
+                           f32_contig(nw) && nw->ne[0] == r.H && ggml_nelements(nw) == r.H &&
+                           f32_contig(rn->src[0]) && ggml_are_same_shape(rn->src[0], xm);
+        if (only_region) {
+            std::unordered_set<const ggml_tensor *> in0(N.begin(), N.end());
+            for (ggml_tensor *c : u.of(xm)) only_region &= in0.count(c) != 0;
+        }
+        if (only_region) {
+            memcpy(&r.norm_eps, rn->op_params, sizeof(float));
+            r.norm_w = nw;
+            r.x = rn->src[0];
+            head = rn;
+            N.insert(N.end(), {rn, xm});
+        }
+    }
+    if (ggml_tensor *add = u.only(r.out)) {
+        ggml_tensor *other = add->src[0] == r.out ? add->src[1] : add->src[0];
+        if (is_op(add, GGML_OP_ADD) && (add->src[0] == r.out || add->src[1] == r.out) && other != r.out &&
+            f32_contig(other) && ggml_are_same_shape(other, r.out) && f32_contig(add) &&
+            !(r.out->flags & GGML_TENSOR_FLAG_OUTPUT) && (!r.norm_w || other == r.x)) {
+            N.push_back(add);
+            r.residual = other;
+            r.out = add;
+        }
+    }
+
     // every intermediate is read only inside the layer; the selection and the weights may
     // also be read after it (the expert cache records the selection)
     std::unordered_set<const ggml_tensor *> in(N.begin(), N.end());
@@ -446,7 +486,12 @@ bool match_moe(const Uses &u, ggml_tensor *D, MoeRegion &r) {
         if (it == u.index.end()) return false;
         r.first = std::min(r.first, it->second);
     }
-    if (u.index.at(logits) != r.first) return false;
+    if (u.index.at(head) != r.first) return false;
+    // consecutive nodes: nothing runs between the fused call and the nodes that would have
+    // produced its results, so it writes them in place (see d_compute)
+    int last = 0;
+    for (ggml_tensor *n : N) last = std::max(last, u.index.at(n));
+    r.direct = last - r.first + 1 == (int) N.size();
     qwb_moe_ffn_desc d{};
     d.gate = view_of(r.wg);
     d.up = view_of(r.wu);
@@ -745,6 +790,7 @@ struct DBackend {
     cudaEvent_t ev_to_ours = nullptr, ev_to_inner = nullptr;
     Scratch sc;
     bool fuse = true, own_mul_mat = false;
+    int64_t fuse_max_tokens = 64;  // larger batches: per-node MUL_MAT_ID (tensor-core GEMMs)
     bool ours_active = false;  // this library's stream holds work the inner stream has not joined
     std::vector<ggml_tensor *> run;
     uint64_t stats[kStatN] = {};
@@ -752,6 +798,8 @@ struct DBackend {
     Uses uses;
     std::vector<MoeRegion> regions;
     std::unordered_map<const ggml_tensor *, int> region_of;
+    bool analysed = false;
+    uint64_t fingerprint = 0;
 };
 
 ggml_guid *dbackend_guid() {
@@ -763,12 +811,22 @@ ggml_guid *dbackend_guid() {
 bool is_dbackend(ggml_backend_t b) { return b && ggml_guid_matches(b->guid, dbackend_guid()); }
 ggml_backend_t inner_of(ggml_backend_t b) { return is_dbackend(b) ? ((DBackend *) b->context)->inner : b; }
 
+#ifdef QWB_HANDOFF_FENCE
+__global__ void handoff_fence_kernel() {}
+#endif
+
 // inner stream -> this library's stream
 void to_ours(DBackend *c) {
     if (c->ours_active) return;
     ggml_backend_event e{c->dev->inner, (void *) c->ev_to_ours};
     c->inner->iface.event_record(c->inner, &e);
     cuda_ok(cudaStreamWaitEvent(c->stream, c->ev_to_ours, 0), "cudaStreamWaitEvent");
+#ifdef QWB_HANDOFF_FENCE
+    handoff_fence_kernel<<<1, 1, 0, c->stream>>>();
+#endif
+#ifdef QWB_DEBUG_SYNC
+    cudaDeviceSynchronize();
+#endif
     c->ours_active = true;
 }
 // this library's stream -> inner stream
@@ -777,11 +835,19 @@ void to_inner(DBackend *c) {
     cuda_ok(cudaEventRecord(c->ev_to_inner, c->stream), "cudaEventRecord");
     ggml_backend_event e{c->dev->inner, (void *) c->ev_to_inner};
     c->inner->iface.event_wait(c->inner, &e);
+#ifdef QWB_DEBUG_SYNC
+    cudaDeviceSynchronize();
+#endif
     c->ours_active = false;
 }
 
 ggml_status flush_run(DBackend *c, ggml_cgraph *g) {
-    if (c->run.empty()) return GGML_STATUS_SUCCESS;
+    bool work = false;
+    for (const ggml_tensor *t : c->run) work |= !view_op(t->op);
+    if (!work) {  // views only: nothing for ggml-cuda to do, no hand-over needed
+        c->run.clear();
+        return GGML_STATUS_SUCCESS;
+    }
     to_inner(c);
     ggml_cgraph sub = ggml_graph_view(g, 0, 0);
     sub.nodes = c->run.data();
@@ -811,6 +877,9 @@ FusedLayout fused_layout(const MoeRegion &r, const qwb_moe_ffn_desc &d) {
 qwb_moe_ffn_desc fused_desc(const MoeRegion &r) {
     qwb_moe_ffn_desc d{};
     d.x = (const float *) r.x->data;
+    d.norm_w = r.norm_w ? (const float *) r.norm_w->data : nullptr;
+    d.norm_eps = r.norm_eps;
+    d.residual = r.residual ? (const float *) r.residual->data : nullptr;
     d.router_w = (const float *) r.router_w->data;
     d.g2s = r.g2s;
     d.gate = view_of(r.wg);
@@ -820,7 +889,25 @@ qwb_moe_ffn_desc fused_desc(const MoeRegion &r) {
     return d;
 }
 
+// Structure of a graph: nodes, ops and operands (a graph computed again, QuestWend's
+// reused decode graph, keeps its analysis).
+uint64_t graph_fingerprint(const ggml_cgraph *g) {
+    uint64_t h = 1469598103934665603ull ^ (uint64_t) g->n_nodes;
+    auto mix = [&h](uint64_t v) { h = (h ^ v) * 1099511628211ull; };
+    for (int i = 0; i < g->n_nodes; ++i) {
+        const ggml_tensor *n = g->nodes[i];
+        mix((uint64_t) (uintptr_t) n);
+        mix((uint64_t) n->op | ((uint64_t) n->flags << 32));
+        for (int s = 0; s < 3; ++s) mix((uint64_t) (uintptr_t) n->src[s]);
+    }
+    return h;
+}
+
 void find_regions(DBackend *c, ggml_cgraph *g) {
+    const uint64_t fp = graph_fingerprint(g);
+    if (c->analysed && fp == c->fingerprint) return;
+    c->analysed = true;
+    c->fingerprint = fp;
     c->regions.clear();
     c->region_of.clear();
     if (!c->fuse) return;
@@ -829,7 +916,7 @@ void find_regions(DBackend *c, ggml_cgraph *g) {
         ggml_tensor *n = g->nodes[i];
         if (n->op != GGML_OP_MUL_MAT_ID || c->region_of.count(n)) continue;
         MoeRegion r;
-        if (!match_moe(c->uses, n, r)) continue;
+        if (!match_moe(c->uses, n, r) || r.T > c->fuse_max_tokens) continue;
         bool overlap = false;
         for (ggml_tensor *m : r.nodes) overlap |= c->region_of.count(m) != 0;
         if (overlap) continue;
@@ -914,6 +1001,13 @@ ggml_status d_compute(ggml_backend_t be, ggml_cgraph *g) {
                 d.out = (float *) (ws + l.out);
                 d.selected = (int32_t *) (ws + l.sel);
                 d.weights = (float *) (ws + l.w);
+                if (r.direct) {
+                    // nothing else runs until the layer's last node: its result tensors hold
+                    // no live data now (ggml-alloc gave them memory free from the layer's
+                    // first node on, or the residual operand itself, read before written)
+                    d.out = (float *) r.out->data;
+                    d.weights = r.weights_out ? (float *) r.weights->data : d.weights;
+                }
                 const qwb_status rc = qwb_moe_ffn(&d, ws, l.ffn, c->sc.status, (qwb_stream_t) c->stream);
                 if (rc != QWB_OK) {
                     std::fprintf(stderr, "ggml-qwb: fused MoE layer (%s): %s\n", r.out->name, qwb_status_string(rc));
@@ -925,7 +1019,9 @@ ggml_status d_compute(ggml_backend_t be, ggml_cgraph *g) {
             // the layer's results land in the graph's tensors where ggml would produce them
             // (so ggml-alloc's reuse of their memory before that point stays valid)
             cudaError_t e = cudaSuccess;
-            if (t == r.out) {
+            if (r.direct && t != r.sel) {
+                // written in place by the fused call
+            } else if (t == r.out) {
                 to_ours(c);
                 e = cudaMemcpyAsync(r.out->data, ws + l.out, (size_t) (r.H * r.T) * 4, cudaMemcpyDeviceToDevice,
                                     c->stream);
@@ -944,7 +1040,7 @@ ggml_status d_compute(ggml_backend_t be, ggml_cgraph *g) {
             }
             continue;
         }
-        if (ggml_is_empty(t) || view_op(t->op)) continue;
+        if (ggml_is_empty(t)) continue;
         if (own_node(c, t)) {
             if ((st = flush_run(c, g)) != GGML_STATUS_SUCCESS) break;
             to_ours(c);
@@ -1064,8 +1160,11 @@ void dd_props(ggml_backend_dev_t d, ggml_backend_dev_props *p) {
     p->type = GGML_BACKEND_DEVICE_TYPE_GPU;
 }
 
-// params: "workspace_mb=N" (default 256), "fuse=0" (no build_moe fusion), "mul_mat=1"
-// (quantized MUL_MAT on libqwb.so too); the rest is passed to ggml-cuda.
+// params: "workspace_mb=N" (default 256), "fuse=0" (no build_moe fusion),
+// "fuse_max_tokens=N" (fuse layers of at most N tokens, default 64: the fused layer runs
+// its expert GEMVs on the weight-streaming kernel, while per-node MUL_MAT_ID takes the
+// tensor-core GEMMs for many tokens per expert), "mul_mat=1" (quantized MUL_MAT on
+// libqwb.so too); the rest is passed to ggml-cuda.
 ggml_backend_t dd_init(ggml_backend_dev_t d, const char *params) {
     auto *dd = (DDev *) d->context;
     ggml_backend_t inner = ggml_backend_dev_init(dd->inner, params);
@@ -1079,6 +1178,7 @@ ggml_backend_t dd_init(ggml_backend_dev_t d, const char *params) {
     c->inner = inner;
     c->fuse = param_size(params, "fuse=", 1) != 0;
     c->own_mul_mat = param_size(params, "mul_mat=", 0) != 0;
+    c->fuse_max_tokens = (int64_t) param_size(params, "fuse_max_tokens=", 64);
     bool ok = cuda_ok(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "cudaStreamCreate") &&
               cuda_ok(cudaEventCreateWithFlags(&c->ev_to_ours, cudaEventDisableTiming), "cudaEventCreate") &&
               cuda_ok(cudaEventCreateWithFlags(&c->ev_to_inner, cudaEventDisableTiming), "cudaEventCreate") &&
