@@ -690,8 +690,11 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu=None):
         assert torch.isfinite(out).all()
         fl = 2.0 * T * K_USED * PF_H * PF_F
         t_ms = float(np.median(tot))
+        # the library's rule: 128-token tcgen05 tiles at >= 96 routed pairs per expert
+        path = ("tcgen05 kind::i8 grouped GEMM" if T * K_USED >= 96 * min(T * K_USED, E)
+                else "int8 tensor cores (mma.sync)")
         q8_points.append({"tokens": T, "shape": "down", "type": "Q6_K", "ms": t_ms,
-                          "tflops": fl / (t_ms * 1e-3) / 1e12, "path": "int8 tensor cores (mma.sync)"})
+                          "tflops": fl / (t_ms * 1e-3) / 1e12, "path": path})
     del W6, q6buf, q6base
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:

@@ -421,7 +421,7 @@ qwb_status plan_mmid(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor
     p.pf8 = allow_prefill && pf_i8_eligible(p.type, p.K, p.M, p.P, p.n_as, as->data, as->nb[1], as->nb[2]);
     p.stream = !p.pf && !p.pf8 && stream_fits(p.type, p.K, as->nb[1], as->nb[1], false);
     p.NT = p.pf    ? kPfTileN
-           : p.pf8 ? pf_i8_tile_tokens(p.P, p.n_as)
+           : p.pf8 ? pf_i8_tile_tokens(p.type, p.P, p.n_as)
            : p.stream ? (int) std::max<int64_t>(1, p.P)
                       : pick_nt(p.P, p.n_as);
     p.planes = planes_bytes(p.n_b * p.T, p.K, p.vdt == QWB_TYPE_Q8_K);
@@ -431,6 +431,10 @@ qwb_status plan_mmid(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor
         const int64_t max_tiles = mmid_max_tiles(p.P, p.n_as, p.NT);
         p.btiles = align_up((size_t) max_tiles * pf_btile_stride(p.K), 256);
         p.da = align_up((size_t) max_tiles * pf_da_stride(p.K), 256);
+    } else if (p.pf8 && p.NT == kTc8TileTokens) {
+        const int64_t max_tiles = mmid_max_tiles(p.P, p.n_as, p.NT);
+        p.btiles = align_up((size_t) max_tiles * tc8_btile_stride(p.K), 256);
+        p.da = align_up((size_t) max_tiles * tc8_da_stride(p.K), 256);
     }
     // [0, 256) is the control block of the fused kernels
     p.total = kCtrlBytes + p.planes + p.index + p.btiles + p.da;
@@ -540,6 +544,16 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
         q.dnb2 = dst->nb[2];
         q.work = ix.work + 2;
         q.st = st;
+        if (p.NT == kTc8TileTokens) {
+            uint8_t *bt = (uint8_t *) ws + kCtrlBytes + p.planes + p.index;
+            float *bda = (float *) (bt + p.btiles);
+            e = launch_tc8_gather(pl, q.act_dstride, p.K, ix.tiles, ix.n_tiles, ix.max_tiles, ix.pairs,
+                                  (int) p.n_used, (int) p.n_b, bt, bda, s);
+            if (e != cudaSuccess) return QWB_ERR_CUDA;
+            profile_mark(s, QWB_KERNEL_OTHER);
+            q.btiles = bt;
+            q.bda = bda;
+        }
         e = launch_pf_i8(p.type, p.NT, q, s);
         profile_mark(s, QWB_KERNEL_GROUPED_GEMM);
         return e == cudaSuccess ? QWB_OK : QWB_ERR_CUDA;

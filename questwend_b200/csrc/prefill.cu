@@ -188,36 +188,6 @@ struct PfBars {
 };
 static_assert(sizeof(PfBars) <= 512, "barrier block");
 
-// Bounded wait.  The thread is suspended between polls until the phase completes.
-__device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
-                                        qwb_status_block *st) {
-    if (mbar_try_wait(bar, parity, 200000u)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (true) {
-        if (mbar_try_wait(bar, parity, 200000u)) return true;
-        if (*abort) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            *abort = 1;
-            report(st, QWB_DEVERR_TIMEOUT, 0);
-            return false;
-        }
-    }
-}
-// warp-uniform wait: lane 0 polls, the result is broadcast
-__device__ __forceinline__ bool pf_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort,
-                                             qwb_status_block *st) {
-    int ok = 1;
-    if ((threadIdx.x & 31) == 0) ok = pf_wait(bar, parity, abort, st);
-    return __shfl_sync(0xffffffffu, ok, 0) != 0;
-}
-// One arrival of count 32 on behalf of the whole warp, after every lane's own memory and
-// tcgen05 operations are ordered by the caller's fences.
-__device__ __forceinline__ void warp_arrive(uint64_t *bar) {
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0)
-        asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0], 32;" ::"r"(smem_u32(bar)) : "memory");
-}
-
 struct PfItem {
     int tile, mt, p0, cnt, Nt, rows;
     int64_t slot;  // -1: invalid expert id / slot

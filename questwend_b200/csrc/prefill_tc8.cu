@@ -1,0 +1,459 @@
+// prefill_tc8.cu - MUL_MAT_ID on Q6_K experts with many tokens per expert as a grouped
+// GEMM on the 5th-generation tensor cores (tcgen05.mma kind::i8: s8 x s8 -> s32
+// accumulators in tensor memory).
+//
+// Reference arithmetic (ggml_compute_forward_mul_mat_id, ggml-cpu/ggml-cpu.c:1554-1736;
+// Q6_K x Q8_K, ggml-cpu/quants.c:851-915): for every superblock of 256,
+//     sumf += (d_w * d_a) * (float) sum_s sc_s * isum_s   over its 16 sub-blocks of 16,
+//     isum_s = sum (q6 - 32) * q_a, sc_s the sub-block's int8 scale.
+// The integer superblock sum is kept exact: the sub-block scale is folded into the
+// weights, v = sc * (q - 32) in [-4064, 4096], written as two int8 planes
+// v = 64 * a1 + a0 (a0 in [-32, 31], a1 in [-63, 64]); two MMAs per K=32 (planes a1 and
+// a0, same activations) accumulate sum a1 * q_a and sum a0 * q_a over the superblock, and
+// 64 * acc1 + acc0 is the reference's integer superblock sum (|.| < 2^31).  The epilogue
+// adds (d_w * d_a) * (float) sum, once per 256 K.
+//
+// Q8_0 does not use this kernel: its rank-1 block scale d_w * d_a changes every 32 K, so a
+// tensor-memory accumulator would need an epilogue pass per 32 K (read, scale, add,
+// restart); the register accumulators of the mma.sync kernel (prefill_i8.cu) do that
+// cheaper.
+//
+// Work item = (token tile of <= 128 (token, slot) pairs of one expert, 128 weight rows);
+// one persistent CTA per SM takes items blockIdx.x, + gridDim.x, ...  Warp roles:
+//   warps 0-3   producers, one thread per weight row: 16-byte cp.async of the raw
+//               superblocks (widened to 16-byte boundaries) and one bulk copy per step of
+//               the tile's activation codes and scales, gathered beforehand into the B
+//               operand's core-matrix layout (tc8_gather_kernel: the bulk copies keep far
+//               more bytes in flight per SM than 16-byte copies of scattered rows); then
+//               the repack of the codes into the A operand's two planes and the step's
+//               scales; one mbarrier arrival per step
+//   warp 4      TMEM allocation and the MMA-issuing thread
+//   warps 5-12  epilogue: two warpgroups (token columns 0-63 / 64-127), one weight row
+//               per thread, the item's sums in registers
+// Pipeline step = 128 K elements (half a superblock); A/B operand stages are
+// triple-buffered, the two superblock accumulators (a1 and a0 planes, 256 columns each)
+// double-buffered in the 512 tensor-memory columns.  Every wait is bounded; a timeout sets
+// QWB_DEVERR_TIMEOUT and all roles drain and exit.
+#include <algorithm>
+
+#include "common.cuh"
+#include "dot.cuh"
+#include "kernels.cuh"
+#include "mmid.cuh"
+#include "umma.cuh"
+
+namespace qwb {
+
+namespace {
+
+constexpr int kT8M = 128;        // weight rows per item
+constexpr int kT8N = 128;        // token pairs per item (index tile)
+constexpr int kT8Step = 128;     // K per pipeline step
+constexpr int kT8Stages = 3;     // A/B operand stages
+constexpr int kT8EpStages = 4;   // scale slots (one per step)
+constexpr int kT8Threads = 13 * 32;
+constexpr int kT8WarpMma = 4;
+constexpr int kT8WarpEpi = 5;    // 5..12
+constexpr int kT8A = 2 * kT8M * kT8Step;  // 32768: A stage bytes (planes a1 | a0)
+constexpr int kT8B = kT8N * kT8Step;      // 16384: B stage bytes
+constexpr int kT8RawRow = 240;            // raw bytes per row per superblock (widened)
+constexpr uint32_t kT8Lbo = 128 * 16;     // leading byte offset of a 128-row operand slab
+constexpr uint32_t kT8TmemCols = 512;
+constexpr uint32_t kT8DaBytes = 4 * kT8N;  // activation scales per step of a tile
+
+// scales of one superblock: d of weight row m and d_a of token n
+struct T8Ep {
+    float dw[kT8M];
+    float da[kT8N];
+};
+
+struct T8Smem {
+    uint8_t a[kT8Stages][kT8A];
+    uint8_t b[kT8Stages][kT8B];
+    uint8_t raw[2][kT8M * kT8RawRow];
+    T8Ep ep[kT8EpStages];
+    float dstage[kT8Stages][kT8N];  // activation scales of the step (bulk copy)
+    int raw_off[2][kT8M];           // offset of the superblock inside its widened row bytes
+    uint64_t full[kT8Stages], empty[kT8Stages], bfull[kT8Stages];
+    uint64_t acc_full[2], acc_empty[2];
+    uint64_t ep_full[kT8EpStages], ep_empty[kT8EpStages];
+    uint64_t drain;
+    uint32_t tmem;
+    int abort;
+};
+static_assert(sizeof(T8Smem) <= 232448, "one CTA per SM: at most 227 KB of shared memory");
+
+struct T8Item {
+    int tile, mt, p0, cnt, Nt, rows;
+    int64_t slot;  // -1: invalid expert id
+};
+__device__ __forceinline__ T8Item t8_item(const I8PrefillArgs &a, int m_tiles, int it) {
+    T8Item x;
+    x.tile = it / m_tiles;
+    x.mt = it - x.tile * m_tiles;
+    const int4 t = a.tiles[x.tile];
+    x.p0 = t.y;
+    x.cnt = t.z;
+    x.Nt = (t.z + 15) & ~15;
+    x.rows = (int) min((int64_t) kT8M, a.M - (int64_t) x.mt * kT8M);
+    x.slot = (t.x >= 0 && t.x < a.n_as) ? (int64_t) t.x : -1;
+    return x;
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// barrier among the 128 producer threads only
+__device__ __forceinline__ void producers_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// byte offset of operand element (row r, k) in a 128-row stage (k < 128)
+__device__ __forceinline__ uint32_t t8_off(int r, int k) {
+    return (uint32_t) (k >> 4) * kT8Lbo + (uint32_t) (r >> 3) * 128u + (uint32_t) (r & 7) * 16u + (uint32_t) (k & 15);
+}
+
+// 4 codes q (0..63, one per byte of w) of sub-block scale sc -> int8 planes a1, a0 with
+// sc * (q - 32) = 64 * a1 + a0.  Two 16-bit lanes per 32-bit word: with sc' = sc + 128 in
+// [0, 255], z = q * sc' - 128 q + (4128 - 32 sc) = sc (q - 32) + 4128 lies in [64, 8224]
+// and no lane borrows from or carries into its neighbour; then a0 + 32 = z & 63 and
+// a1 + 64 = z >> 6.
+__device__ __forceinline__ void q6_planes(uint32_t w, int sc, uint32_t &a1, uint32_t &a0) {
+    const uint32_t scp = (uint32_t) (sc + 128);
+    const uint32_t bias = (uint32_t) (4096 - 32 * sc + 32) * 0x10001u;
+    const uint32_t x01 = __byte_perm(w, 0, 0x4140), x23 = __byte_perm(w, 0, 0x4342);
+    const uint32_t z01 = x01 * scp + bias - (x01 << 7), z23 = x23 * scp + bias - (x23 << 7);
+    const uint32_t lo01 = z01 & 0x003F003Fu, lo23 = z23 & 0x003F003Fu;
+    const uint32_t hi01 = (z01 >> 6) & 0x03FF03FFu, hi23 = (z23 >> 6) & 0x03FF03FFu;
+    a0 = __vsub4(__byte_perm(lo01, lo23, 0x6420), 0x20202020u);
+    a1 = __vsub4(__byte_perm(hi01, hi23, 0x6420), 0x40404040u);
+}
+
+// Gathered activations: per tile and 128-K step, the B operand stage exactly as the MMA
+// reads it (token n's codes k at t8_off(n, k)) and the superblock's activation scales.
+// Grid (max_tiles, steps); tiles past the index's count exit.
+__global__ void __launch_bounds__(256) tc8_gather_kernel(Q8Planes act, int act_dstride, int64_t K,
+                                                         const int4 *__restrict__ tiles, const int *__restrict__ n_tiles,
+                                                         const int *__restrict__ pairs, int n_used, int n_b,
+                                                         uint8_t *__restrict__ btiles, float *__restrict__ bda) {
+    const int tile = blockIdx.x, s = blockIdx.y, nsteps = (int) gridDim.y;
+    if (tile >= *n_tiles) return;
+    const int4 t = tiles[tile];
+    __shared__ int64_t arow[kT8N];
+    for (int n = threadIdx.x; n < kT8N; n += blockDim.x) {
+        int64_t r = -1;
+        if (n < t.z) {
+            const int p = pairs[t.y + n];
+            const int tt = p / n_used, j = p - tt * n_used;
+            r = (int64_t) tt * n_b + j % n_b;
+        }
+        arow[n] = r;
+    }
+    __syncthreads();
+    uint8_t *dst = btiles + ((size_t) tile * nsteps + s) * kT8B;
+    // chunk c: token n = c % 128, 16-byte column kc = c / 128 (consecutive threads write
+    // consecutive 16-byte pieces of one core-matrix column)
+    for (int c = threadIdx.x; c < kT8N * 8; c += blockDim.x) {
+        const int n = c & (kT8N - 1), kc = c >> 7;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (arow[n] >= 0) v = *(const uint4 *) (act.qs + arow[n] * K + (int64_t) s * kT8Step + 16 * kc);
+        *(uint4 *) (dst + t8_off(n, 16 * kc)) = v;
+    }
+    float *da = bda + ((size_t) tile * nsteps + s) * (kT8DaBytes / 4);
+    for (int n = threadIdx.x; n < kT8N; n += blockDim.x)
+        da[n] = arow[n] >= 0 ? act.d[arow[n] * act_dstride + (s >> 1)] : 0.f;
+}
+
+__global__ void __launch_bounds__(kT8Threads, 1) pf_tc8_kernel(const I8PrefillArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    T8Smem &S = *(T8Smem *) smem_raw;
+    volatile int *abort = &S.abort;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int m_tiles = (int) ceil_div(a.M, kT8M);
+    const int total = *a.n_tiles * m_tiles;
+    if ((int) blockIdx.x >= total) return;
+    const int nsteps = (int) (a.K / kT8Step);
+    const int n_items = (total - (int) blockIdx.x + (int) gridDim.x - 1) / (int) gridDim.x;
+    const int gsteps = n_items * nsteps;  // this CTA's steps over all its items
+
+    if (tid == 0) {
+        for (int i = 0; i < kT8Stages; ++i) {
+            mbar_init(&S.full[i], 128);
+            mbar_init(&S.empty[i], 1);
+            mbar_init(&S.bfull[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&S.acc_full[i], 1);
+            mbar_init(&S.acc_empty[i], 256);
+        }
+        for (int i = 0; i < kT8EpStages; ++i) {
+            mbar_init(&S.ep_full[i], 128);
+            mbar_init(&S.ep_empty[i], 256);
+        }
+        mbar_init(&S.drain, 1);
+        S.abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == kT8WarpMma) {
+        umma::tmem_alloc(&S.tmem, kT8TmemCols);
+        umma::tmem_relinquish();
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tbase = S.tmem;
+
+    if (warp < kT8WarpMma) {
+        // ------------------------------------------------------------ producers
+        const int r = tid;  // weight row / token row of this thread
+        // item state cached per item index (k = CTA-local item)
+        int c_item = -1, c_tile = 0;
+        int n_issued = 0, n_seen = 0;  // steps whose bulk copies were issued / waited for
+        const uint8_t *wrow = nullptr;  // this thread's weight row, null when out of range
+        auto item_state = [&](int k) {
+            if (k == c_item) return;
+            c_item = k;
+            const T8Item x = t8_item(a, m_tiles, (int) blockIdx.x + k * (int) gridDim.x);
+            wrow = (x.slot >= 0 && r < x.rows)
+                       ? a.W + (size_t) x.slot * a.nb2 + ((size_t) x.mt * kT8M + r) * a.nb1
+                       : nullptr;
+            c_tile = x.tile;
+        };
+        // copies of global step g: the B codes of the step and their scales and, on even
+        // steps, the raw bytes of the superblock it starts; one cp.async group per step
+        auto issue = [&](int g) {
+            if (g < gsteps) {
+                const int k = g / nsteps, s = g - k * nsteps, st = g % kT8Stages;
+                item_state(k);
+                if (g >= kT8Stages) {
+                    // the stage's previous MMAs are done (the MMA thread commits it)
+                    if (!pf_wait_warp(&S.empty[st], ((g / kT8Stages) & 1) ^ 1, abort, a.st)) {
+                        cp_async_commit();
+                        return false;
+                    }
+                }
+                // B and its scales: the tile's gathered stage, two bulk copies on bfull[st]
+                if (r == 0) {
+                    const size_t ts = (size_t) c_tile * nsteps + s;
+                    mbar_arrive_expect_tx(&S.bfull[st], (uint32_t) kT8B + kT8DaBytes);
+                    bulk_g2s(S.b[st], a.btiles + ts * kT8B, (uint32_t) kT8B, &S.bfull[st]);
+                    bulk_g2s(S.dstage[st], a.bda + ts * (kT8DaBytes / 4), kT8DaBytes, &S.bfull[st]);
+                }
+                n_issued = g + 1;
+                if ((s & 1) == 0) {
+                    // the 210-byte superblock widened to 16-byte boundaries (<= 15 pieces)
+                    const int u = s >> 1, rs = (g >> 1) & 1;
+                    const uintptr_t s0 = (uintptr_t) (wrow ? wrow : a.W) + (uintptr_t) u * Q6K_BYTES;
+                    const uintptr_t a0 = s0 & ~(uintptr_t) 15;
+                    S.raw_off[rs][r] = (int) (s0 - a0);
+                    for (int c = 0; c < 15; ++c) {
+                        const bool in = wrow && (a0 + 16 * c < s0 + Q6K_BYTES);
+                        cp_async16(&S.raw[rs][r * kT8RawRow + 16 * c], (const void *) (in ? a0 + 16 * c : a0), in);
+                    }
+                }
+            }
+            cp_async_commit();
+            return true;
+        };
+        bool ok = issue(0);
+        ok = ok && issue(1);
+        // Every producer thread runs all gsteps iterations (the named barriers need all
+        // 128 of them); after a timeout anywhere the iterations do no work.
+        for (int g = 0; g < gsteps; ++g) {
+            producers_sync();  // step g - 1 repacked by every producer: its raw unit may be refilled
+            if (ok && !*abort) ok = issue(g + 2);
+            cp_async_wait<2>();  // this thread's copies of step g
+            producers_sync();    // everyone's
+            if (!ok || *abort) {
+                ok = false;
+                continue;
+            }
+            const int k = g / nsteps, s = g - k * nsteps, st = g % kT8Stages, rs = (g >> 1) & 1;
+            item_state(k);
+            // scale slot of this step
+            const int es = g % kT8EpStages;
+            if (!(ok = pf_wait_warp(&S.ep_empty[es], ((g / kT8EpStages) & 1) ^ 1, abort, a.st))) continue;
+            if (!(ok = pf_wait_warp(&S.bfull[st], (g / kT8Stages) & 1, abort, a.st))) continue;  // the step's scales
+            n_seen = g + 1;
+            auto &ep = S.ep[es];
+            uint8_t *A = S.a[st];
+            // half h = s & 1 of the superblock: elements 128 h + 32 i + l of sub-lanes
+            // i = 0..3 (ql at 64 h + 32 (i & 1), high nibbles when i >= 2; qh bits 2i, 2i+1)
+            const uint8_t *sb = S.raw[rs] + r * kT8RawRow + S.raw_off[rs][r];
+            const int h = s & 1;
+            uint32_t qh[8];
+            lds_words8_a2(sb + 128 + 32 * h, qh);
+#pragma unroll 1
+            for (int i = 0; i < 4; ++i) {
+                uint32_t qa[8];
+                lds_words8_a2(sb + 64 * h + 32 * (i & 1), qa);
+                const int8_t *scp = (const int8_t *) (sb + 192) + 8 * h + 2 * i;
+                const int sc0 = scp[0], sc1 = scp[1];  // sub-blocks of l = 0..15 and 16..31
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    const uint32_t nib = i < 2 ? (qa[m] & 0x0f0f0f0fu) : ((qa[m] >> 4) & 0x0f0f0f0fu);
+                    const uint32_t q = nib | (((qh[m] >> (2 * i)) & 0x03030303u) << 4);
+                    uint32_t p1, p0;
+                    q6_planes(q, m < 4 ? sc0 : sc1, p1, p0);
+                    // elements l = 4m .. 4m + 3 of sub-lane i: k = 32 i + 4 m within the half
+                    const int kk = 32 * i + 4 * m;
+                    *(uint32_t *) (A + t8_off(r, kk)) = p1;
+                    *(uint32_t *) (A + kT8M * kT8Step + t8_off(r, kk)) = p0;
+                }
+            }
+            if (h == 1) {  // the superblock's scales, once both halves are in
+                ep.dw[r] = h2f(*(const uint16_t *) (sb + 208));
+                ep.da[r] = S.dstage[st][r];
+            }
+            fence_proxy_async_smem();  // the operands are read by the tensor cores
+            // one arrival per thread on both: operands and scales of step g are in place
+            asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&S.full[st])) : "memory");
+            asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&S.ep_full[es])) : "memory");
+        }
+        cp_async_wait<0>();  // no copy stays in flight past the kernel
+        if (r == 0) {
+            // bulk copies issued for steps this loop did not consume (only after an abort)
+            for (int g = n_seen; g < n_issued; ++g) mbar_wait(&S.bfull[g % kT8Stages], (g / kT8Stages) & 1);
+        }
+    } else if (warp == kT8WarpMma) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            uint32_t acc_i = 0;
+            bool ok = true;
+            for (int g = 0; g < gsteps && ok; ++g) {
+                const int k = g / nsteps, s = g - k * nsteps, st = g % kT8Stages;
+                const T8Item x = t8_item(a, m_tiles, (int) blockIdx.x + k * (int) gridDim.x);
+                const uint32_t idesc = umma::idesc_i8(kT8M, x.Nt);
+                if (!(ok = pf_wait(&S.full[st], (g / kT8Stages) & 1, abort, a.st))) break;
+                if (!(ok = pf_wait(&S.bfull[st], (g / kT8Stages) & 1, abort, a.st))) break;
+                umma::fence_after_sync();
+                const uint32_t a_s = smem_u32(S.a[st]), b_s = smem_u32(S.b[st]);
+                const int h = s & 1, rg = (int) (acc_i & 1);
+                if (h == 0) {
+                    if (!(ok = pf_wait(&S.acc_empty[rg], ((acc_i >> 1) & 1) ^ 1, abort, a.st))) break;
+                    umma::fence_after_sync();
+                }
+                const uint32_t d1 = tbase + (uint32_t) rg * 256, d0 = d1 + 128;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const uint64_t bd = umma::sdesc(b_s + 2 * b * kT8Lbo, kT8Lbo, 128);
+                    const uint32_t acc = (h | b) != 0;
+                    umma::mma_i8_ss(d1, umma::sdesc(a_s + 2 * b * kT8Lbo, kT8Lbo, 128), bd, idesc, acc);
+                    umma::mma_i8_ss(d0, umma::sdesc(a_s + kT8M * kT8Step + 2 * b * kT8Lbo, kT8Lbo, 128), bd, idesc,
+                                    acc);
+                }
+                umma::commit(&S.empty[st]);
+                if (h == 1) {
+                    umma::commit(&S.acc_full[rg]);
+                    ++acc_i;
+                }
+            }
+            // every MMA issued by this thread has completed before TMEM is released
+            umma::commit(&S.drain);
+            mbar_wait(&S.drain, 0);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int qd = warp & 3, g = (warp - kT8WarpEpi) >> 2, m = qd * 32 + lane;
+        const uint32_t lane_base = (uint32_t) (qd * 32) << 16;
+        uint32_t acc_i = 0;
+        bool ok = true;
+        int gstep = 0;
+        for (int k = 0; k < n_items && ok; ++k) {
+            const T8Item x = t8_item(a, m_tiles, (int) blockIdx.x + k * (int) gridDim.x);
+            // output offsets (floats) of token columns 64 g + lane and 64 g + 32 + lane
+            uint32_t off[2] = {0, 0};
+#pragma unroll
+            for (int uu = 0; uu < 2; ++uu) {
+                const int n = 64 * g + 32 * uu + lane;
+                if (n < x.cnt) {
+                    const int p = __ldg(a.pairs + x.p0 + n);
+                    const int t = p / a.n_used, j = p - t * a.n_used;
+                    off[uu] = (uint32_t) (((size_t) j * a.dnb1 + (size_t) t * a.dnb2) >> 2);
+                }
+            }
+            const int nch = max(0, min(2, (x.Nt - 64 * g + 31) / 32));  // 32-column chunks with tokens
+            float out[64];
+#pragma unroll
+            for (int i = 0; i < 64; ++i) out[i] = 0.f;
+            for (int s = 0; s < nsteps && ok; ++s, ++gstep) {
+                const int es = gstep % kT8EpStages;
+                if (!(ok = pf_wait_warp(&S.ep_full[es], (gstep / kT8EpStages) & 1, abort, a.st))) break;
+                const auto &ep = S.ep[es];
+                if (s & 1) {
+                    const int rg = (int) (acc_i & 1);
+                    if (!(ok = pf_wait_warp(&S.acc_full[rg], (acc_i >> 1) & 1, abort, a.st))) break;
+                    umma::fence_after_sync();
+                    const float dw = ep.dw[m];
+                    const uint32_t d1 = tbase + lane_base + (uint32_t) rg * 256 + 64 * g;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        if (16 * c < 32 * nch) {  // warp-uniform: 16-column pieces with tokens
+                            uint32_t v1[16], v0[16];
+                            umma::ld16(d1 + 16 * c, v1);
+                            umma::ld16(d1 + 128 + 16 * c, v0);
+                            umma::wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const int col = 64 * g + 16 * c + i;
+                                const int isum = 64 * (int) v1[i] + (int) v0[i];
+                                out[16 * c + i] = __fmaf_rn(__fmul_rn(dw, ep.da[col]), (float) isum, out[16 * c + i]);
+                            }
+                        }
+                    }
+                    umma::fence_before_sync();
+                    warp_arrive(&S.acc_empty[rg]);
+                    ++acc_i;
+                }
+                warp_arrive(&S.ep_empty[es]);
+            }
+            if (!ok) break;
+            // rows of an invalid expert id come out as zeros (their weights were zero-filled)
+            const int64_t row = (int64_t) x.mt * kT8M + m;
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+                const uint32_t o = __shfl_sync(0xffffffffu, off[i >> 5], i & 31);
+                if (m < x.rows && 64 * g + i < x.cnt) a.dst[(size_t) o + row] = out[i];
+            }
+            if (x.slot < 0 && x.mt == 0 && m == 0 && g == 0) report(a.st, QWB_DEVERR_ID_RANGE, a.tiles[x.tile].x);
+        }
+    }
+
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == kT8WarpMma) {
+        umma::fence_after_sync();
+        umma::tmem_dealloc(tbase, kT8TmemCols);
+    }
+}
+
+}  // namespace
+
+size_t tc8_btile_stride(int64_t K) { return (size_t) (K / kT8Step) * kT8B; }
+size_t tc8_da_stride(int64_t K) { return (size_t) (K / kT8Step) * kT8DaBytes; }
+
+cudaError_t launch_tc8_gather(Q8Planes act, int act_dstride, int64_t K, const int4 *tiles, const int *n_tiles,
+                              int max_tiles, const int *pairs, int n_used, int n_b, uint8_t *btiles, float *bda,
+                              cudaStream_t s) {
+    if (max_tiles <= 0) return cudaSuccess;
+    dim3 grid((unsigned) max_tiles, (unsigned) (K / kT8Step));
+    tc8_gather_kernel<<<grid, 256, 0, s>>>(act, act_dstride, K, tiles, n_tiles, pairs, n_used, n_b, btiles, bda);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pf_tc8(const I8PrefillArgs &a, cudaStream_t s) {
+    const size_t smem = sizeof(T8Smem);
+    static DeviceSmemLimit limit;
+    cudaError_t e = ensure_dyn_smem(pf_tc8_kernel, smem, limit);
+    if (e != cudaSuccess) return e;
+    pf_tc8_kernel<<<num_sms(), kT8Threads, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace qwb

@@ -1,7 +1,8 @@
 // umma.cuh - 5th-generation tensor core (tcgen05) building blocks for sm_100a.
 //
 // Thin inline-PTX wrappers: tensor-memory (TMEM) allocation, the kind::f16 MMA with the A
-// operand in TMEM or shared memory and B in shared memory, commit to an mbarrier,
+// operand in TMEM or shared memory and B in shared memory, the kind::i8 MMA (both operands
+// in shared memory), commit to an mbarrier,
 // 32x32b TMEM loads/stores and the tcgen05 ordering fences.  Descriptor encodings follow
 // the PTX ISA's "matrix descriptor" and "instruction descriptor" tables for tcgen05.mma.
 //
@@ -143,5 +144,58 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// kind::i8 instruction descriptor: A, B signed 8-bit, D signed 32-bit, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+    return (2u << 4)                         // D format: s32
+           | (1u << 7) | (1u << 10)          // A, B format: signed 8-bit
+           | (0u << 15) | (0u << 16)         // A, B K-major
+           | ((uint32_t) (N >> 3) << 17)     // N / 8
+           | ((uint32_t) (M >> 4) << 24);    // M / 16
+}
+// D[tmem] (+)= A[smem] * B[smem]^T, s8 x s8 -> s32, K = 32 (issued by one thread).
+// Shared-memory layout of 8-bit operands (K-major, no swizzle): core matrices of 8 rows x
+// 16 bytes; element (r, k) of an R-row slab at (k / 16) * (R * 16) + (r / 8) * 128 +
+// (r % 8) * 16 + (k % 16): leading byte offset R * 16, stride byte offset 128.
+__device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 }  // namespace umma
+
+// Bounded wait.  The thread is suspended between polls until the phase completes.
+__device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                        qwb_status_block *st) {
+    if (mbar_try_wait(bar, parity, 200000u)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity, 200000u)) return true;
+        if (*abort) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            *abort = 1;
+            report(st, QWB_DEVERR_TIMEOUT, 0);
+            return false;
+        }
+    }
+}
+// warp-uniform wait: lane 0 polls, the result is broadcast
+__device__ __forceinline__ bool pf_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                             qwb_status_block *st) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = pf_wait(bar, parity, abort, st);
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+// One arrival of count 32 on behalf of the whole warp, after every lane's own memory and
+// tcgen05 operations are ordered by the caller's fences.
+__device__ __forceinline__ void warp_arrive(uint64_t *bar) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0)
+        asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0], 32;" ::"r"(smem_u32(bar)) : "memory");
+}
+
 }  // namespace qwb

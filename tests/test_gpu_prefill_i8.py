@@ -1,10 +1,15 @@
 """GPU parity: MUL_MAT_ID on Q8_0 and Q6_K experts with many tokens per expert, the
-integer tensor-core kernel (mma.sync s8 x s8 -> s32: one m16n8k32 per Q8_0 block with fp32
-block scaling in block order; one m16n8k16 per Q6_K sub-block with its int8 scale in
-int32 and fp32 scaling per superblock), against the oracle's dots (activations quantized
-as the CPU backend does: Q8_0 CPU variant / Q8_K), against the reference's own ggml CPU
-backend under skewed routing, and against the weight-streaming path on the same inputs.
-Bar: nRMS <= 1e-4 (max abs-rel error in the message)."""
+integer tensor-core kernels:
+  * mma.sync s8 x s8 -> s32 (prefill_i8.cu): one m16n8k32 per Q8_0 block with fp32 block
+    scaling in block order; one m16n8k16 per Q6_K sub-block with its int8 scale in int32
+    and fp32 scaling per superblock (Q8_0 at every size, Q6_K below 96 pairs per expert);
+  * tcgen05.mma kind::i8 (prefill_tc8.cu, Q6_K at >= 96 pairs per expert): the sub-block
+    scales folded into two int8 weight planes, s32 accumulators in tensor memory, fp32
+    scaling per superblock;
+against the oracle's dots (activations quantized as the CPU backend does: Q8_0 CPU
+variant / Q8_K), against the reference's own ggml CPU backend under skewed routing, and
+against the weight-streaming path on the same inputs.  Bar: nRMS <= 1e-4 (max abs-rel
+error in the message)."""
 import ctypes as C
 
 import numpy as np
@@ -70,6 +75,10 @@ CASES = [
     (O.Q6_K, 768, 2048, 8, 128, 4, 4),      # config-2 down shape
     (O.Q6_K, 1024, 300, 8, 256, 4, 1),
     (O.Q6_K, 2048, 128, 8, 64, 8, 8),
+    # Q6_K at >= 96 pairs per used expert: the tcgen05 kernel (128-token tiles)
+    (O.Q6_K, 768, 2048, 8, 256, 4, 4),      # 128 per expert, config-2 down shape
+    (O.Q6_K, 2048, 300, 8, 512, 8, 8),      # 512 per expert, rows not a multiple of 128
+    (O.Q6_K, 1536, 256, 4, 100, 4, 1),      # 100 per expert: one full and one 28-pair tile each
     # 8 to 31 pairs per used expert: 8-token tiles (16-row warps, one 8-token MMA column)
     (O.Q8_0, 1024, 300, 16, 40, 4, 1),      # 10 per expert, partial tiles and row blocks
     (O.Q8_0, 4096, 128, 8, 12, 8, 8),       # 12 per expert, one activation row per pair
@@ -95,9 +104,9 @@ def test_uniform_routing(qwb, t, K, M, n_as, T, n_used, n_b):
     assert e <= TOL, (e, O.max_abs_rel(got, want))
 
 
-@pytest.mark.parametrize("t", [O.Q8_0, O.Q6_K])
-def test_zipf_routing_against_reference_build(qwb, t):
-    K, M, n_as, T, n_used = 1024, 256, 64, 512, 8
+@pytest.mark.parametrize("t,T", [(O.Q8_0, 512), (O.Q6_K, 512), (O.Q6_K, 1024)])
+def test_zipf_routing_against_reference_build(qwb, t, T):
+    K, M, n_as, n_used = 1024, 256, 64, 8
     w = D.weights(t, n_as, M, K, seed=31)
     b = D.acts((T, 1, K), seed=32)
     ids = D.zipf_ids(T, n_as, n_used, seed=33)
