@@ -14,13 +14,18 @@ are larger than L2, no flush is needed.
 
 Prints one JSON line (rank 0).  `value` is decode tokens/s of the whole job.  At N = 1 the
 step is the fused single-GPU layer (qwb_moe_ffn).  At N > 1 the experts are sharded over
-the ranks (expert parallelism: rank r holds experts [r*128/N, (r+1)*128/N) of every layer,
-router replicated) and every rank decodes its own token, so a step is N tokens
-("scaling": "weak"): per layer each rank routes and quantizes its token, NCCL all-gathers
-the Q8_K rows and routing, runs its experts over all N tokens and reduce-scatters the f32
-partial outputs (questwend_b200.expert_parallel).  `e2e` is the same metric through the public C ABI with
+the ranks (expert parallelism: rank r holds experts [r*128/N, (r+1)*128/N) of every layer)
+and a step decodes N tokens, one per rank ("scaling": "weak"): every rank holds all N
+tokens' hidden states, routes them (replicated router) and runs its own experts over the
+pairs routed to them (one qwb_moe_ep_layer call per layer), and one NCCL all-reduce per
+layer sums the partial outputs (questwend_b200.expert_parallel).  `ep_nrmse` compares one
+such layer with the fused single-GPU layer on the same tokens (the run fails above 1e-5).
+`ep_config4` (every N) runs the 235B-A22B layer shape (hidden 4096, expert FFN 1536) the
+same way at decode batches of 1, 8 and 64 tokens with the aggregate HBM roofline.  `e2e` is
+the same metric through the public C ABI with
 the token's hidden state copied from pinned host memory and the layer output copied back
-every step.  `roofline` is the gate/up GEMV kernel (the largest weight stream per layer).
+every step.  `roofline` is the gate/up GEMV kernel (the largest weight stream per layer)
+at N = 1 and the whole step's aggregate HBM bytes over N x peak at N > 1.
 `cpu_baseline` times the reference's own ggml CPU backend (oracle/_ref, built from the
 reference sources) on one layer of the same shapes, scaled to 48 layers.
 
@@ -727,93 +732,265 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu=None):
     return res
 
 
-def run_ep(args, world, rank, local):
-    """N > 1: the same 48-layer decode stack with the experts sharded over the ranks."""
-    import torch
-    import torch.distributed as dist
+# the 235B-A22B expert-parallel layer: hidden 4096, expert FFN 1536, 128 experts, top-8
+EP4_H, EP4_F, EP4_TOKENS, EP4_LAYERS, EP4_UNIQUE = 4096, 1536, (1, 8, 64), 8, 8
 
-    import questwend_b200 as q
-    from questwend_b200.expert_parallel import ExpertShard, moe_layer, shard_range
-    q.lib()
-    dev = torch.device("cuda", local)
-    lo, n = shard_range(E, world, rank)
-    g, u, d = quantized_experts(seed=0)
-    base = [torch.from_numpy(a).to(dev) for a in (g, u, d)]
-    n_layers = args.layers
+
+def ep_layers(q, dev, base, shapes, n_layers, n_exp, lo, n, unique):
+    """n_layers MoE layers of which this rank holds experts [lo, lo + n): global expert e of
+    layer l is distinct image ((e mod unique) - l) mod unique of `base` (one image per
+    expert and role in its own memory); router and ffn_norm weights from one seed, the
+    same on every rank."""
+    import torch
+
+    from questwend_b200.expert_parallel import ExpertShard
     gen = torch.Generator(device=dev)
-    gen.manual_seed(1234)  # router and ffn_norm weights replicated on every rank
+    gen.manual_seed(1234)
+    hid = shapes[0][2]
     layers = []
     for layer in range(n_layers):
         mats = []
-        for role, (t, rows, K) in enumerate(((Q4_K, F, H), (Q4_K, F, H), (Q6_K, H, F))):
-            # global expert e of this layer is unique expert (e - layer) mod UNIQUE, as in
-            # the single-GPU arm
-            idx = torch.tensor([((lo + i) % UNIQUE - layer) % UNIQUE for i in range(n)], device=dev)
-            sel_rows = base[role].view(UNIQUE, -1).index_select(0, idx).reshape(-1)
-            buf = torch.empty(sel_rows.numel() + 16, dtype=torch.uint8, device=dev)
-            buf[:-16].copy_(sel_rows)
+        for role, (t, rows, K) in enumerate(shapes):
+            idx = torch.tensor([((lo + i) % unique - layer) % unique for i in range(n)], device=dev)
+            rows_img = base[role].view(unique, -1).index_select(0, idx).reshape(-1)
+            buf = torch.empty(rows_img.numel() + 16, dtype=torch.uint8, device=dev)
+            buf[:-16].copy_(rows_img)
             mats.append(q.QTensor(buf[:-16], t, (K, rows, n, 1)))
-        rw = torch.randn((E, H), generator=gen, device=dev) * 0.02
-        nw = 1.0 + 0.1 * torch.randn(H, generator=gen, device=dev)
+        rw = torch.randn((n_exp, hid), generator=gen, device=dev) * 0.02
+        nw = 1.0 + 0.1 * torch.randn(hid, generator=gen, device=dev)
         layers.append((rw, nw, ExpertShard(mats[0], mats[1], mats[2], lo, n)))
-    x0 = torch.randn((1, H), generator=torch.Generator(device=dev).manual_seed(77 + rank), device=dev)
+    return layers
 
-    def step(x):
-        for rw, nw, shard in layers:
-            x = moe_layer(x, rw, shard, K_USED, E, norm_w=nw, norm_eps=1e-6)[0]
-        return x
 
-    xd = x0.clone()
-    # eager warm-up (sizes the workspace, checks the output), then the whole step (48
-    # layers, kernels and NCCL collectives) captured in one CUDA graph
-    for _ in range(2):
-        y = step(xd)
+def ep_run(layers, x, n_used, steps, warmup, world):
+    """Time the expert-parallel stack (one qwb_moe_ep_layer call and one all-reduce per
+    layer) captured in a CUDA graph.  Returns (per-step ms stats, mean ms, the selections of
+    every layer, the stack output, the graph, the collective-only ms per step)."""
+    import torch
+    import torch.distributed as dist
+
+    from questwend_b200.expert_parallel import moe_layer
+    T, hid = x.shape
+    outs = [torch.empty((T, hid), device=x.device) for _ in layers]
+
+    def step():
+        y, sels = x, []
+        for (rw, nw, shard), o in zip(layers, outs):
+            y, sel, _ = moe_layer(y, rw, shard, n_used, norm_w=nw, norm_eps=1e-6, out=o)
+            sels.append(sel)
+        return y, sels
+
+    for _ in range(2):  # eager: sizes the workspace, configures the kernels
+        y, _ = step()
     torch.cuda.synchronize()
     assert torch.isfinite(y).all()
-    dist.barrier()
+    if world > 1:
+        dist.barrier()
     graph = torch.cuda.CUDAGraph()
     cs = torch.cuda.Stream()
     cs.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(cs):
-        step(xd)
-        torch.cuda.synchronize()
         with torch.cuda.graph(graph, stream=cs):
-            y_graph = step(xd)
+            y, sels = step()
     torch.cuda.synchronize()
-    for _ in range(max(3, args.warmup)):
+    for _ in range(max(3, warmup)):
         graph.replay()
     torch.cuda.synchronize()
-    assert torch.isfinite(y_graph).all()
-    dist.barrier()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    if world > 1:
+        dist.barrier()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    evs[0].record()
+    for i in range(steps):
+        graph.replay()
+        evs[i + 1].record()
+    torch.cuda.synchronize()
+    ms = evs[0].elapsed_time(evs[-1]) / steps
+    st = stats([evs[i].elapsed_time(evs[i + 1]) for i in range(steps)])
+    coll_ms = 0.0
+    if world > 1:
+        # the collectives alone: the same all-reduces (one per layer, (T, H) f32) in a graph
+        bufs = [torch.zeros((T, hid), device=x.device) for _ in layers]
+        cgraph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cs):
+            for bf in bufs:
+                dist.all_reduce(bf)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(cgraph, stream=cs):
+                for bf in bufs:
+                    dist.all_reduce(bf)
         torch.cuda.synchronize()
-        t0.record()
-        for _ in range(args.steps):
-            graph.replay()
-        t1.record()
+        for _ in range(3):
+            cgraph.replay()
         torch.cuda.synchronize()
-    ms_step = t0.elapsed_time(t1) / args.steps
-    # end to end: the rank's token from pinned host memory, the layer output back
-    x_host = torch.randn((1, H), generator=torch.Generator().manual_seed(5 + rank)).pin_memory()
-    y_host = torch.empty((1, H)).pin_memory()
-    dist.barrier()
+        dist.barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record()
+        for _ in range(steps):
+            cgraph.replay()
+        c1.record()
+        torch.cuda.synchronize()
+        coll_ms = c0.elapsed_time(c1) / steps
+        del cgraph
+    return st, ms, sels, y, graph, coll_ms
+
+
+def ep_step_bytes(sels, n_exp, expert_bytes, router_bytes, world):
+    """Algorithmic HBM bytes of one step over all ranks: every expert some token selected
+    is read once (by its owner), and every rank reads its router replica."""
+    return sum(int(np.unique(s.cpu().numpy()).size) * expert_bytes + world * router_bytes for s in sels)
+
+
+def ep_check(q, dev, base, shapes, n_exp, unique, layer0, x, y_ep, n_used):
+    """nRMS of one expert-parallel layer's output against the fused single-GPU layer
+    (qwb_moe_ffn with all experts of the layer) on the same input."""
+    import torch
+    full = ep_layers(q, dev, base, shapes, 1, n_exp, 0, n_exp, unique)[0]
+    rw, nw, sh = full
+    assert torch.equal(rw, layer0[0]) and torch.equal(nw, layer0[1])
+    want, _, _ = q.moe_ffn(x, rw, sh.gate, sh.up, sh.down, n_used, residual=x, norm_w=nw, norm_eps=1e-6)
+    got, ref = y_ep.cpu().numpy(), want.cpu().numpy()
+    return float(np.sqrt(np.mean((got - ref) ** 2)) / max(np.sqrt(np.mean(ref ** 2)), 1e-30))
+
+
+def ep_fused_ms(q, layers, x, steps):
+    """One GPU holding every expert: the same stack through qwb_moe_ffn (the batch-1 decode
+    kernels at T = 1), ms per step, captured in a CUDA graph."""
+    import torch
+    outs = [torch.empty_like(x) for _ in layers]
+
+    def step():
+        y = x
+        for (rw, nw, sh), o in zip(layers, outs):
+            y, _, _ = q.moe_ffn(y, rw, sh.gate, sh.up, sh.down, K_USED, residual=y, out=o, norm_w=nw, norm_eps=1e-6)
+        return y
+
+    step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    cs.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cs):
+        with torch.cuda.graph(graph, stream=cs):
+            step()
+    torch.cuda.synchronize()
+    for _ in range(3):
+        graph.replay()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
     e0.record()
-    for _ in range(args.steps):
-        xd.copy_(x_host, non_blocking=True)
+    for _ in range(steps):
         graph.replay()
-        y_host.copy_(y_graph, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
     e1.record()
     torch.cuda.synchronize()
+    del graph
+    return e0.elapsed_time(e1) / steps
+
+
+def ep_config4_sweep(q, dev, world, rank, steps, warmup):
+    """The 235B-A22B layer (hidden 4096, expert FFN 1536, 128 experts, top-8; Q4_K gate/up,
+    Q6_K down) expert-parallel over `world` GPUs: EP4_LAYERS layers per step (of the
+    model's 94), decode batches of T in EP4_TOKENS tokens (total over the job), one
+    qwb_moe_ep_layer call and one all-reduce per layer."""
+    import torch
+    import torch.distributed as dist
+
+    from questwend_b200.expert_parallel import moe_layer, shard_range
+    hbm, kind = peaks()
+    shapes = ((Q4_K, EP4_F, EP4_H), (Q4_K, EP4_F, EP4_H), (Q6_K, EP4_H, EP4_F))
+    rng = np.random.default_rng(4)
+    base = [torch.from_numpy(synth_blocks(t, EP4_UNIQUE * rows, K, rng)).to(dev) for t, rows, K in shapes]
+    lo, n = shard_range(E, world, rank)
+    layers = ep_layers(q, dev, base, shapes, EP4_LAYERS, E, lo, n, EP4_UNIQUE)
+    expert_bytes = 2 * EP4_F * (EP4_H // 256) * 144 + EP4_H * (EP4_F // 256) * 210
+    router_bytes = E * EP4_H * 4
+    points = []
+    for T in EP4_TOKENS:
+        x = torch.randn((T, EP4_H), generator=torch.Generator(device=dev).manual_seed(900 + T), device=dev)
+        st, ms, sels, y, graph, coll_ms = ep_run(layers, x, K_USED, steps, warmup, world)
+        del graph
+        t = torch.tensor([ms, st["median"], coll_ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, med, coll_ms = t.tolist()
+        nbytes = ep_step_bytes(sels, E, expert_bytes, router_bytes, world)
+        # one layer's output against the fused single-GPU layer (rank 0), T = 8
+        err = None
+        if T == 8:
+            y1, _, _ = moe_layer(x, layers[0][0], layers[0][2], K_USED, norm_w=layers[0][1], norm_eps=1e-6)
+            torch.cuda.synchronize()
+            if rank == 0:
+                err = ep_check(q, dev, base, shapes, E, EP4_UNIQUE, layers[0], x, y1, K_USED)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        fused_ms = ep_fused_ms(q, layers, x, steps) if world == 1 else None
+        points.append({"tokens": T, "ms_per_step": ms, "ms_per_layer": ms / EP4_LAYERS, "step_ms_median": med,
+                       "fused_layer_ms_per_step": fused_ms,
+                       "tokens_per_s": T * 1000.0 / ms,
+                       "collective_ms_per_step": coll_ms if world > 1 else 0.0,
+                       "kernel_ms_per_step": ms - coll_ms if world > 1 else ms,
+                       "hbm_bytes_per_step": nbytes, "hbm_gbs_aggregate": gbs,
+                       "roofline": {"bound": "hbm", "achieved": gbs, "peak": world * hbm,
+                                    "peak_kind": f"{kind} x {world} GPUs", "unit": "GB/s",
+                                    "frac": gbs / (world * hbm)},
+                       "ep_nrmse": err})
+    return {"workload": "qwen3-235b-a22b MoE FFN layer, expert-parallel decode", "layers": EP4_LAYERS,
+            "hidden": EP4_H, "expert_ffn": EP4_F, "experts": E, "top_k": K_USED, "experts_per_gpu": n,
+            "n_gpus": world, "collectives_per_step": EP4_LAYERS if world > 1 else 0,
+            "note": "kernel_ms_per_step = step - the same all-reduces timed alone in a graph",
+            "points": points}
+
+
+def run_ep(args, world, rank, local):
+    """N > 1: the 48-layer decode stack with the experts sharded over the ranks; every rank
+    holds all N tokens (one per rank) and routes them; one all-reduce per layer."""
+    import torch
+    import torch.distributed as dist
+
+    import questwend_b200 as q
+    from questwend_b200.expert_parallel import moe_layer, shard_range
+    q.lib()
+    dev = torch.device("cuda", local)
+    lo, n = shard_range(E, world, rank)
+    base = [torch.from_numpy(a).to(dev) for a in quantized_experts(seed=0)]
+    shapes = ((Q4_K, F, H), (Q4_K, F, H), (Q6_K, H, F))
+    n_layers = args.layers
+    layers = ep_layers(q, dev, base, shapes, n_layers, E, lo, n, UNIQUE)
+    # the step's batch: one token per rank, the same (N, H) rows on every rank
+    x = torch.randn((world, H), generator=torch.Generator(device=dev).manual_seed(77), device=dev)
+    with ClockSampler(local) as clk:
+        st, ms_step, sels, y_graph, graph, coll_ms = ep_run(layers, x, K_USED, args.steps, args.warmup, world)
+        # end to end: the batch from pinned host memory (every rank reads all N rows), the
+        # rank's own token's output row back
+        x_host = torch.randn((world, H), generator=torch.Generator().manual_seed(5)).pin_memory()
+        y_host = torch.empty((1, H)).pin_memory()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            x.copy_(x_host, non_blocking=True)
+            graph.replay()
+            y_host.copy_(y_graph[rank:rank + 1], non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        e1.record()
+        torch.cuda.synchronize()
     ms_e2e = e0.elapsed_time(e1) / args.steps
     del graph
-    times = torch.tensor([ms_step, ms_e2e], device=dev)
+    flags, bad, cnt = q.read_status()
+    times = torch.tensor([ms_step, ms_e2e, coll_ms, st["median"], st["p10"], st["p90"], float(flags)], device=dev)
     dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    ms_step, ms_e2e = times.tolist()
+    ms_step, ms_e2e, coll_ms, med, p10, p90, flags = times.tolist()
+    expert_bytes = 2 * EXPERT_GU + EXPERT_D
+    nbytes = ep_step_bytes(sels, E, expert_bytes, E * H * 4, world)
+    # multi-GPU correctness: one layer against the fused single-GPU layer (rank 0 decides)
+    y1, _, _ = moe_layer(x, layers[0][0], layers[0][2], K_USED, norm_w=layers[0][1], norm_eps=1e-6)
+    torch.cuda.synchronize()
+    err = ep_check(q, dev, base, shapes, E, UNIQUE, layers[0], x, y1, K_USED) if rank == 0 else 0.0
+    bad_t = torch.tensor([1.0 if (err > 1e-5 or flags) else 0.0], device=dev)
+    dist.all_reduce(bad_t, op=dist.ReduceOp.MAX)
+    if bad_t.item():
+        raise RuntimeError(f"expert-parallel output differs from the fused layer: nrmse {err:.3e}, flags {flags}")
+    c4 = None if args.no_ep4 else ep_config4_sweep(q, dev, world, rank, max(20, args.steps // 10), args.warmup)
     hbm, kind = peaks()
+    gbs = nbytes / (ms_step * 1e-3) / 1e9
     if rank == 0:
         cfg = workload_config(world, n_layers)
         cfg["parallelism"] = f"ep{world}"
@@ -821,16 +998,23 @@ def run_ep(args, world, rank, local):
         print(json.dumps({
             "metric": "decode_tokens_per_s", "value": world * 1000.0 / ms_step, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "step_ms": {"median": med, "p10": p10, "p90": p90, "n": args.steps},
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "q4_K/q6_K x q8_K -> f32", "data": "synthetic (seeded quantized blocks: random codes, scales sized like quantized N(0,0.02))",
             "config": cfg,
-            "e2e": {"value": world * 1000.0 / ms_e2e, "unit": "tokens/s", "h2d_bytes_per_step": H * 4,
+            "e2e": {"value": world * 1000.0 / ms_e2e, "unit": "tokens/s", "h2d_bytes_per_step": world * H * 4,
                     "d2h_bytes_per_step": H * 4},
-            "collectives_per_step": 2 * n_layers,
-            "gpu_launches": args.steps * 11 * n_layers,
-            "roofline": {"bound": "latency", "kernel": "expert-parallel layer (collective-bound at batch 1)",
-                         "achieved": None, "peak": hbm, "peak_kind": kind, "unit": "GB/s", "frac": None,
-                         "traffic": None},
+            "collectives_per_step": n_layers,
+            "collective_ms_per_step": coll_ms,
+            "kernel_ms_per_step": ms_step - coll_ms,
+            "gpu_launches": args.steps * 7 * n_layers,
+            "ep_nrmse": err,
+            "device_errors": int(flags),
+            "roofline": {"bound": "hbm", "kernel": "whole expert-parallel step, aggregate over the GPUs",
+                         "achieved": gbs, "peak": world * hbm, "peak_kind": f"{kind} x {world} GPUs",
+                         "unit": "GB/s", "frac": gbs / (world * hbm), "traffic": None,
+                         "algorithmic_bytes": nbytes},
+            "ep_config4": c4,
             "clocks": clk.summary(),
         }))
     dist.barrier()
@@ -938,6 +1122,8 @@ def main():
                     help="internal: time the stack through ggml on the stock ggml-cuda backend and on "
                          "libggml-qwb.so, print the JSON and exit")
     ap.add_argument("--no-ggml", action="store_true", help="skip the ggml drop-in comparison")
+    ap.add_argument("--no-ep4", action="store_true",
+                    help="skip the 235B-A22B expert-parallel layer sweep (T = 1, 8, 64)")
     args = ap.parse_args()
     if args.cpu_leg:
         return run_cpu_leg(args)
@@ -1155,6 +1341,8 @@ def main():
         result["gathers"] = gathers_sweep(q, dev)
     if rank == 0 and not args.no_slabs:
         result["slab_upload"] = slab_sweep(q, dev)
+    if rank == 0 and not args.no_ep4:
+        result["ep_config4"] = ep_config4_sweep(q, dev, 1, 0, max(20, args.steps // 10), args.warmup)
     if rank == 0 and not args.no_ggml:
         # the GPU memory this process holds is released first: the leg loads 2 x 16 GB stacks
         del layers, descs, ws, base

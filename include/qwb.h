@@ -239,47 +239,38 @@ QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *desc, void *workspace, si
 /* ----------------------------------------------------- expert parallelism (EP)
  * The MoE layer split over N GPUs (no counterpart in the reference, whose multi-GPU
  * plan is a pipeline-style layer split, core/runtime.cpp:1551-1724; the arithmetic per
- * (token, slot) is build_moe's, core/runtime.cpp:2743-2816).  Tokens are data-parallel
- * and GPU g owns experts [expert_lo, expert_lo + n_local) of every layer.  Per layer:
- *   1. qwb_moe_ep_prepare on each GPU's own tokens: rms_norm * ffn_norm, router, top-k,
- *      and the normalised rows quantized to the gate/up weights' vec_dot type (Q8_K or
- *      Q8_0 CPU variant), packed as ggml blocks.
- *   2. the caller all-gathers the packed rows, selected ids and weights (NCCL);
- *      quantization is per row, so the gathered bytes equal a single-GPU run's.
- *   3. qwb_moe_ep_experts on every GPU: the SwiGLU expert FFN of ITS experts over all
- *      gathered tokens; out[t] = sum over slots j routed to a local expert of
- *      weights[t][j] * down(swiglu(gate x_t, up x_t)) (zero when none is local).
- *   4. the caller reduce-scatters out (sum, f32) back to the token owners and adds the
- *      residual: only the f32 summation order differs from qwb_moe_ffn. */
-typedef struct qwb_moe_ep_prepare_desc {
-    const float *x;          /* [T][H] this GPU's token rows */
+ * (token, slot) is build_moe's, core/runtime.cpp:2743-2816).  GPU g owns experts
+ * [expert_lo, expert_lo + n_local) of every layer, and every GPU holds the hidden states
+ * of all T tokens (identical copies).  Per layer:
+ *   1. qwb_moe_ep_layer on every GPU: rms_norm * ffn_norm, router and top-k for all T
+ *      tokens (replicated: the same ids and weights everywhere), then the SwiGLU expert
+ *      FFN of ITS experts over the pairs routed to them:
+ *        out[t] = sum over slots j with a local expert of weights[t][j] *
+ *                 down(swiglu(gate x_t, up x_t))  (+ residual[t] when residual != NULL)
+ *      (zero, or the residual, for a token with no local expert);
+ *   2. the caller all-reduces out (sum, f32) over the N GPUs, passing the residual to
+ *      exactly one of them: every GPU then holds the layer's output for all tokens.
+ * One collective per layer.  Quantization is per row, so every GPU's activation bytes
+ * equal a single-GPU run's; only the f32 summation order of the weighted expert outputs
+ * differs from qwb_moe_ffn. */
+typedef struct qwb_moe_ep_layer_desc {
+    const float *x;          /* [T][H] all tokens' rows (the same on every GPU) */
     const float *norm_w;     /* [H] ffn_norm weight, or NULL (no normalisation) */
     float norm_eps;
+    int32_t reserved;
     const float *router_w;   /* [E][H] f32 router */
     const float *mask;       /* [T][E] additive logit mask, or NULL */
-    int64_t H, E, n_used, T;
-    int32_t act_type;        /* QWB_TYPE_Q8_K (K-quant gate/up) or QWB_TYPE_Q8_0 (Q8_0 gate/up) */
-    int32_t reserved;
-    void *xq;                /* out: T packed rows of act_type, row size = H/256*292 or H/32*34 bytes */
-    int32_t *selected;       /* out: [T][n_used] expert ids, descending probability */
-    float *weights;          /* out: [T][n_used] renormalised routing weights */
-} qwb_moe_ep_prepare_desc;
-QWB_API size_t qwb_moe_ep_prepare_workspace_size(const qwb_moe_ep_prepare_desc *desc);
-QWB_API qwb_status qwb_moe_ep_prepare(const qwb_moe_ep_prepare_desc *desc, void *workspace, size_t workspace_bytes,
-                                      qwb_status_block *d_status, qwb_stream_t stream);
-
-typedef struct qwb_moe_ep_experts_desc {
-    const void *xq;          /* [T] packed Q8 rows of all GPUs' tokens (gathered) */
-    const int32_t *selected; /* [T][n_used] global expert ids in [0, E) */
-    const float *weights;    /* [T][n_used] */
     qwb_tensor gate, up, down; /* this GPU's experts: [H, F, n_local], [H, F, n_local], [F, H, n_local] */
     int64_t expert_lo;       /* global id of local expert 0 */
     int64_t H, F, E, n_used, T;
+    const float *residual;   /* [T][H] added to out, or NULL */
     float *out;              /* [T][H] f32 partial sums (overwritten) */
-} qwb_moe_ep_experts_desc;
-QWB_API size_t qwb_moe_ep_experts_workspace_size(const qwb_moe_ep_experts_desc *desc);
-QWB_API qwb_status qwb_moe_ep_experts(const qwb_moe_ep_experts_desc *desc, void *workspace, size_t workspace_bytes,
-                                      qwb_status_block *d_status, qwb_stream_t stream);
+    int32_t *selected;       /* out: [T][n_used] expert ids, descending probability, or NULL */
+    float *weights;          /* out: [T][n_used] renormalised routing weights, or NULL */
+} qwb_moe_ep_layer_desc;
+QWB_API size_t qwb_moe_ep_layer_workspace_size(const qwb_moe_ep_layer_desc *desc);
+QWB_API qwb_status qwb_moe_ep_layer(const qwb_moe_ep_layer_desc *desc, void *workspace, size_t workspace_bytes,
+                                    qwb_status_block *d_status, qwb_stream_t stream);
 
 /* ------------------------------------------------------------- expert pool writes
  * The expert cache keeps each role's experts in a pool tensor [ne0, ne1, n_slots] (one

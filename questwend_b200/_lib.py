@@ -52,18 +52,12 @@ class MoeFfnDesc(C.Structure):
                 ("norm_w", C.c_void_p), ("norm_eps", C.c_float)]
 
 
-class MoeEpPrepareDesc(C.Structure):
-    _fields_ = [("x", C.c_void_p), ("norm_w", C.c_void_p), ("norm_eps", C.c_float), ("router_w", C.c_void_p),
-                ("mask", C.c_void_p), ("H", C.c_int64), ("E", C.c_int64), ("n_used", C.c_int64), ("T", C.c_int64),
-                ("act_type", C.c_int32), ("reserved", C.c_int32), ("xq", C.c_void_p), ("selected", C.c_void_p),
-                ("weights", C.c_void_p)]
-
-
-class MoeEpExpertsDesc(C.Structure):
-    _fields_ = [("xq", C.c_void_p), ("selected", C.c_void_p), ("weights", C.c_void_p),
+class MoeEpLayerDesc(C.Structure):
+    _fields_ = [("x", C.c_void_p), ("norm_w", C.c_void_p), ("norm_eps", C.c_float), ("reserved", C.c_int32),
+                ("router_w", C.c_void_p), ("mask", C.c_void_p),
                 ("gate", Tensor), ("up", Tensor), ("down", Tensor), ("expert_lo", C.c_int64),
                 ("H", C.c_int64), ("F", C.c_int64), ("E", C.c_int64), ("n_used", C.c_int64), ("T", C.c_int64),
-                ("out", C.c_void_p)]
+                ("residual", C.c_void_p), ("out", C.c_void_p), ("selected", C.c_void_p), ("weights", C.c_void_p)]
 
 
 _lib = None
@@ -99,10 +93,8 @@ SIGNATURES = [
     ("qwb_moe_weighted_sum", C.c_int, [_P, _P, _P, C.c_int64, C.c_int64, C.c_int64, _P]),
     ("qwb_moe_ffn_workspace_size", C.c_size_t, [C.POINTER(MoeFfnDesc)]),
     ("qwb_moe_ffn", C.c_int, [C.POINTER(MoeFfnDesc), _P, C.c_size_t, _P, _P]),
-    ("qwb_moe_ep_prepare_workspace_size", C.c_size_t, [C.POINTER(MoeEpPrepareDesc)]),
-    ("qwb_moe_ep_prepare", C.c_int, [C.POINTER(MoeEpPrepareDesc), _P, C.c_size_t, _P, _P]),
-    ("qwb_moe_ep_experts_workspace_size", C.c_size_t, [C.POINTER(MoeEpExpertsDesc)]),
-    ("qwb_moe_ep_experts", C.c_int, [C.POINTER(MoeEpExpertsDesc), _P, C.c_size_t, _P, _P]),
+    ("qwb_moe_ep_layer_workspace_size", C.c_size_t, [C.POINTER(MoeEpLayerDesc)]),
+    ("qwb_moe_ep_layer", C.c_int, [C.POINTER(MoeEpLayerDesc), _P, C.c_size_t, _P, _P]),
     ("qwb_pool_write_slabs", C.c_int, [_TP, C.c_size_t, C.POINTER(SlabCopy), C.c_int, _P]),
     ("qwb_pool_audit_slabs", C.c_int, [_TP, C.POINTER(SlabCopy), C.c_int, C.c_int, _P, _P]),
     ("qwb_profile_enable", C.c_int, [C.c_int]),

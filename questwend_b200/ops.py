@@ -288,59 +288,48 @@ def moe_ffn(x, router_w, gate: QTensor, up: QTensor, down: QTensor, n_used: int,
 
 
 # ------------------------------------------------------------------ expert parallelism
-def moe_ep_prepare(x, router_w, n_used: int, norm_w=None, norm_eps: float = 1e-6, act_type: int = Q8_K,
-                   mask=None):
-    """Token-owner side of the expert-parallel MoE layer: rms_norm(x) * norm_w, router,
-    top-k, and the normalised rows quantized to act_type (Q8_K for K-quant gate/up
-    weights, Q8_0 for Q8_0) as packed ggml blocks.  x (T, H) f32, router_w (E, H) f32.
-    Returns (xq (T, row bytes) uint8, selected (T, n_used) int32, weights (T, n_used))."""
+def moe_ep_layer_desc(x, router_w, gate: QTensor, up: QTensor, down: QTensor, expert_lo: int, n_used: int, out,
+                      residual=None, selected=None, weights=None, norm_w=None, norm_eps: float = 1e-6,
+                      mask=None) -> L.MoeEpLayerDesc:
     T, H = x.shape
-    E = router_w.shape[0]
-    xq = torch.empty((T, row_size(act_type, H)), dtype=torch.uint8, device=x.device)
-    sel = torch.empty((T, n_used), dtype=torch.int32, device=x.device)
-    w = torch.empty((T, n_used), dtype=torch.float32, device=x.device)
-    d = L.MoeEpPrepareDesc()
+    d = L.MoeEpLayerDesc()
     d.x, d.router_w = x.data_ptr(), router_w.data_ptr()
     d.norm_w = norm_w.data_ptr() if norm_w is not None else None
     d.norm_eps = norm_eps
     d.mask = mask.data_ptr() if mask is not None else None
-    d.H, d.E, d.n_used, d.T = H, E, n_used, T
-    d.act_type = act_type
-    d.xq, d.selected, d.weights = xq.data_ptr(), sel.data_ptr(), w.data_ptr()
-    lib = L.lib()
-    need = lib.qwb_moe_ep_prepare_workspace_size(C.byref(d))
-    if need == 0:
-        raise L.QwbError("qwb_moe_ep_prepare_workspace_size", 3)
-    ws = workspace(need)
-    L.check("qwb_moe_ep_prepare", lib.qwb_moe_ep_prepare(C.byref(d), _ws_ptr(ws), ws.numel(),
-                                                         status_block().data_ptr(), _stream()))
-    return xq, sel, w
-
-
-def moe_ep_experts(xq, selected, weights, gate: QTensor, up: QTensor, down: QTensor, expert_lo: int,
-                   n_expert: int, out=None):
-    """Expert side of the expert-parallel MoE layer: the SwiGLU FFN of the local experts
-    (gate/up [H, F, n_local], down [F, H, n_local] = global experts [expert_lo,
-    expert_lo + n_local)) over all gathered tokens.  xq (T, row bytes) packed Q8 rows,
-    selected/weights (T, n_used).  Returns the f32 partial sums (T, H)."""
-    T, n_used = selected.shape
-    H, F = gate.ne[0], gate.ne[1]
-    if out is None:
-        out = torch.empty((T, H), dtype=torch.float32, device=xq.device)
-    d = L.MoeEpExpertsDesc()
-    d.xq, d.selected, d.weights = xq.data_ptr(), selected.data_ptr(), weights.data_ptr()
     d.gate, d.up, d.down = gate.desc(), up.desc(), down.desc()
     d.expert_lo = expert_lo
-    d.H, d.F, d.E, d.n_used, d.T = H, F, n_expert, n_used, T
+    d.H, d.F, d.E, d.n_used, d.T = H, gate.ne[1], router_w.shape[0], n_used, T
+    d.residual = residual.data_ptr() if residual is not None else None
     d.out = out.data_ptr()
+    d.selected = selected.data_ptr() if selected is not None else None
+    d.weights = weights.data_ptr() if weights is not None else None
+    return d
+
+
+def moe_ep_layer(x, router_w, gate: QTensor, up: QTensor, down: QTensor, expert_lo: int, n_used: int,
+                 residual=None, norm_w=None, norm_eps: float = 1e-6, mask=None, out=None):
+    """One GPU's share of an expert-parallel MoE layer.  x (T, H) f32: all tokens' rows (the
+    same on every GPU); gate/up [H, F, n_local], down [F, H, n_local]: global experts
+    [expert_lo, expert_lo + n_local).  Routes all tokens (replicated router) and returns
+    (out (T, H), selected (T, n_used), weights (T, n_used)): out[t] = the weighted sum of
+    this GPU's experts' outputs for token t (+ residual[t] when given).  Summing out over
+    the GPUs (all-reduce) gives the layer's output."""
+    T, H = x.shape
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.float32, device=x.device)
+    sel = torch.empty((T, n_used), dtype=torch.int32, device=x.device)
+    w = torch.empty((T, n_used), dtype=torch.float32, device=x.device)
+    d = moe_ep_layer_desc(x, router_w, gate, up, down, expert_lo, n_used, out, residual, sel, w, norm_w, norm_eps,
+                          mask)
     lib = L.lib()
-    need = lib.qwb_moe_ep_experts_workspace_size(C.byref(d))
+    need = lib.qwb_moe_ep_layer_workspace_size(C.byref(d))
     if need == 0:
-        raise L.QwbError("qwb_moe_ep_experts_workspace_size", 3)
+        raise L.QwbError("qwb_moe_ep_layer_workspace_size", 3)
     ws = workspace(need)
-    L.check("qwb_moe_ep_experts", lib.qwb_moe_ep_experts(C.byref(d), _ws_ptr(ws), ws.numel(),
-                                                         status_block().data_ptr(), _stream()))
-    return out
+    L.check("qwb_moe_ep_layer", lib.qwb_moe_ep_layer(C.byref(d), _ws_ptr(ws), ws.numel(), status_block().data_ptr(),
+                                                     _stream()))
+    return out, sel, w
 
 
 # ------------------------------------------------------------------ expert pool writes

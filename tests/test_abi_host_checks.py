@@ -64,18 +64,27 @@ def test_mul_mat_checks(lib):
 
 
 def test_expert_parallel_workspace_queries(lib):
-    p = L.MoeEpPrepareDesc()
-    p.H, p.E, p.n_used, p.T, p.act_type = 2048, 128, 8, 4, L.Q8_K
-    assert lib.qwb_moe_ep_prepare_workspace_size(C.byref(p)) > 0
-    p.act_type = L.F32
-    assert lib.qwb_moe_ep_prepare_workspace_size(C.byref(p)) == 0  # unsupported activation type
-    p.act_type, p.H = L.Q8_K, 2000
-    assert lib.qwb_moe_ep_prepare_workspace_size(C.byref(p)) == 0  # H % 256
-    p.H, p.n_used = 2048, 200
-    assert lib.qwb_moe_ep_prepare_workspace_size(C.byref(p)) == 0  # more experts used than exist
-    assert lib.qwb_moe_ep_prepare(C.byref(p), None, 0, None, None) == LIMIT
-    p.n_used, p.T = 8, 0
-    assert lib.qwb_moe_ep_prepare(C.byref(p), None, 0, None, None) == OK  # no tokens
+    H, F, E, n_loc = 2048, 768, 128, 16
+    rg, rd = H // 256 * 144, F // 256 * 210
+    p = L.MoeEpLayerDesc()
+    p.gate = _t(0x100000, L.Q4_K, (H, F, n_loc, 1), (144, rg, rg * F, rg * F * n_loc))
+    p.up = _t(0x200000, L.Q4_K, (H, F, n_loc, 1), (144, rg, rg * F, rg * F * n_loc))
+    p.down = _t(0x300000, L.Q6_K, (F, H, n_loc, 1), (210, rd, rd * H, rd * H * n_loc))
+    p.expert_lo, p.H, p.F, p.E, p.n_used, p.T = 32, H, F, E, 8, 8
+    assert lib.qwb_moe_ep_layer_workspace_size(C.byref(p)) > 0
+    p.expert_lo = E - n_loc + 1
+    assert lib.qwb_moe_ep_layer_workspace_size(C.byref(p)) == 0  # shard past the last expert
+    p.expert_lo, p.H = 0, 2000
+    assert lib.qwb_moe_ep_layer_workspace_size(C.byref(p)) == 0  # H % 1024
+    p.H, p.n_used = H, 200
+    assert lib.qwb_moe_ep_layer_workspace_size(C.byref(p)) == 0  # more experts used than exist
+    assert lib.qwb_moe_ep_layer(C.byref(p), None, 0, None, None) == LIMIT
+    p.n_used, p.up.type = 8, L.Q6_K
+    assert lib.qwb_moe_ep_layer(C.byref(p), None, 0, None, None) == UNSUPPORTED  # gate and up differ
+    p.up.type, p.T = L.Q4_K, 0
+    assert lib.qwb_moe_ep_layer(C.byref(p), None, 0, None, None) == OK  # no tokens
+    p.T = 4
+    assert lib.qwb_moe_ep_layer(C.byref(p), None, 0, None, None) == INVALID  # no x / router / out
 
 
 def test_noalloc_limit_without_gpu(lib):

@@ -1,11 +1,13 @@
 """Expert parallelism: partition and exchange logic on CPU ranks (gloo, world sizes 2 and 4).
 
 questwend_b200.expert_parallel.moe_layer runs unchanged on 2 or 4 CPU processes with a test
-backend whose compute steps are the CPU oracle (rms_norm, router top-k, mul_mat_id on the
-rank's expert range, swiglu, masked weighted sum).  The outputs of the ranks must
-equal a one-rank run of the same backend over all tokens and all experts up to f32
-summation order (1e-6 normalized RMS), and that one-rank run must match the oracle's own
-build_moe layer (1e-4).  No GPU is involved."""
+backend whose compute step is the CPU oracle (rms_norm, router top-k over all tokens,
+mul_mat_id on the rank's expert range, swiglu, masked weighted sum, residual on rank 0).
+After the layer's one all-reduce every rank must hold the same output for all tokens,
+equal to a one-rank run of the same backend over all experts up to f32 summation order
+(1e-6 normalized RMS), and that one-rank run must match the oracle's own build_moe layer
+(1e-4).  Two layers are chained, so the second routes on the all-reduced output.  No GPU
+is involved."""
 import os
 import socket
 
@@ -21,34 +23,29 @@ H, F, E, K_USED, T_RANK = 1024, 256, 8, 2, 3
 
 
 class OracleBackend:
-    """Compute steps of the expert-parallel layer on the CPU oracle.  The 'packed rows'
-    exchanged between ranks are the normalised f32 rows (the oracle quantizes inside
-    mul_mat_id, exactly as the reference CPU backend does)."""
+    """The compute step of the expert-parallel layer on the CPU oracle (which quantizes the
+    activations inside mul_mat_id, exactly as the reference CPU backend does)."""
 
-    def prepare(self, x, router_w, n_used, norm_w, norm_eps, act_type):
+    def layer(self, x, router_w, shard, n_used, norm_w, norm_eps, residual, out=None):
         xn = O.rms_norm_mul(x.numpy(), norm_w.numpy(), norm_eps)
         logits = (xn.astype(np.float64) @ router_w.numpy().astype(np.float64).T).astype(np.float32)
         sel, w = O.route(logits, n_used)
-        return torch.from_numpy(xn), torch.from_numpy(sel), torch.from_numpy(w)
-
-    def experts(self, xq, selected, weights, shard, n_expert):
-        x = xq.numpy()
-        sel = selected.numpy()
-        w = weights.numpy()
-        T = x.shape[0]
+        T = xn.shape[0]
         local = (sel >= shard.lo) & (sel < shard.lo + shard.n)
         ids = np.where(local, sel - shard.lo, 0).astype(np.int32)
-        g, rc = O.mul_mat_id(O.Q4_K, shard.gate, H, F, shard.n, x[:, None, :], ids)
+        g, rc = O.mul_mat_id(O.Q4_K, shard.gate, H, F, shard.n, xn[:, None, :], ids)
         assert rc == 0
-        u, rc = O.mul_mat_id(O.Q4_K, shard.up, H, F, shard.n, x[:, None, :], ids)
+        u, rc = O.mul_mat_id(O.Q4_K, shard.up, H, F, shard.n, xn[:, None, :], ids)
         assert rc == 0
         act = (g / (1.0 + np.exp(-g)) * u).astype(np.float32)
         dn, rc = O.mul_mat_id(O.Q6_K, shard.down, F, H, shard.n, act, ids)
         assert rc == 0
-        out = np.zeros((T, H), dtype=np.float32)
+        part = np.zeros((T, H), dtype=np.float32)
         for j in range(sel.shape[1]):
-            out += np.where(local[:, j:j + 1], w[:, j:j + 1] * dn[:, j, :], 0.0).astype(np.float32)
-        return torch.from_numpy(out)
+            part += np.where(local[:, j:j + 1], w[:, j:j + 1] * dn[:, j, :], 0.0).astype(np.float32)
+        if residual is not None:
+            part += residual.numpy()
+        return torch.from_numpy(part), torch.from_numpy(sel), torch.from_numpy(w)
 
 
 def _inputs(world):
@@ -75,10 +72,14 @@ def _rank_main(rank, world, port, q):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     x, router_w, norm_w, gate, up, down = _inputs(world)
     lo, n = shard_range(E, world, rank)
-    xs = torch.from_numpy(x[rank * T_RANK:(rank + 1) * T_RANK].copy())
-    out, sel, w = moe_layer(xs, torch.from_numpy(router_w), _shard(gate, up, down, lo, n), K_USED, E,
-                            norm_w=torch.from_numpy(norm_w), backend=OracleBackend())
-    q.put((rank, out.numpy(), sel.numpy()))
+    shard = _shard(gate, up, down, lo, n)
+    y = torch.from_numpy(x)
+    sels = []
+    for _ in range(2):
+        y, sel, _ = moe_layer(y, torch.from_numpy(router_w), shard, K_USED, norm_w=torch.from_numpy(norm_w),
+                              backend=OracleBackend())
+        sels.append(sel.numpy())
+    q.put((rank, y.numpy(), sels))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -101,26 +102,32 @@ def test_cpu_ranks_match_one_rank_and_oracle(world):
         p.start()
     res = {}
     for _ in range(world):
-        rank, out, sel = q.get(timeout=180)
-        res[rank] = (out, sel)
+        rank, out, sels = q.get(timeout=180)
+        res[rank] = (out, sels)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    ep_out = np.concatenate([res[r][0] for r in range(world)])
-    ep_sel = np.concatenate([res[r][1] for r in range(world)])
+    # every rank holds the same output (the all-reduce leaves identical sums) and routing
+    for r in range(1, world):
+        assert np.array_equal(res[r][0], res[0][0])
+        assert all(np.array_equal(a, b) for a, b in zip(res[r][1], res[0][1]))
 
-    # one rank, all experts: same backend, no exchange
+    # one rank, all experts: same backend, no exchange, two chained layers
     x, router_w, norm_w, gate, up, down = _inputs(world)
     bk = OracleBackend()
-    xn, sel, w = bk.prepare(torch.from_numpy(x), torch.from_numpy(router_w), K_USED, torch.from_numpy(norm_w), 1e-6, 0)
-    single = bk.experts(xn, sel, w, _shard(gate, up, down, 0, E), E).numpy() + x
-    assert (ep_sel == sel.numpy()).all()
-    assert O.nrmse(ep_out, single) <= 1e-6, O.nrmse(ep_out, single)
+    full = _shard(gate, up, down, 0, E)
+    y = torch.from_numpy(x)
+    layer_in = []
+    for layer in range(2):
+        layer_in.append(y.numpy())
+        y, sel, _ = bk.layer(y, torch.from_numpy(router_w), full, K_USED, torch.from_numpy(norm_w), 1e-6, y)
+        assert (res[0][1][layer] == sel.numpy()).all()
+    single = y.numpy()
+    assert O.nrmse(res[0][0], single) <= 1e-6, O.nrmse(res[0][0], single)
 
-    # and the backend itself is build_moe: the oracle's own layer
-    want = O.moe_layer(x, router_w, O.Q4_K, gate, up, O.Q6_K, down, F, E, K_USED, norm_w=norm_w)
-    assert (want["selected"] == sel.numpy()).all()
-    assert O.nrmse(single - x, want["out"]) <= 1e-4
+    # and the backend itself is build_moe: the oracle's own layer, on the last layer's input
+    want = O.moe_layer(layer_in[1], router_w, O.Q4_K, gate, up, O.Q6_K, down, F, E, K_USED, norm_w=norm_w)
+    assert O.nrmse(single - layer_in[1], want["out"]) <= 1e-4
 
 
 def test_shard_range_partitions_experts():
