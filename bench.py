@@ -762,10 +762,11 @@ def ep_layers(q, dev, base, shapes, n_layers, n_exp, lo, n, unique):
     return layers
 
 
-def ep_run(layers, x, n_used, steps, warmup, world):
+def ep_run(layers, x, n_used, steps, warmup, world, comm=None):
     """Time the expert-parallel stack (one qwb_moe_ep_layer call and one all-reduce per
-    layer) captured in a CUDA graph.  Returns (per-step ms stats, mean ms, the selections of
-    every layer, the stack output, the graph, the collective-only ms per step)."""
+    layer: the peer-memory one when `comm` is given, else NCCL's) captured in a CUDA
+    graph.  Returns (per-step ms stats, mean ms, the selections of every layer, the stack
+    output, the graph, the collective-only ms per step, NCCL's collective-only ms)."""
     import torch
     import torch.distributed as dist
 
@@ -776,7 +777,7 @@ def ep_run(layers, x, n_used, steps, warmup, world):
     def step():
         y, sels = x, []
         for (rw, nw, shard), o in zip(layers, outs):
-            y, sel, _ = moe_layer(y, rw, shard, n_used, norm_w=nw, norm_eps=1e-6, out=o)
+            y, sel, _ = moe_layer(y, rw, shard, n_used, norm_w=nw, norm_eps=1e-6, out=o, comm=comm)
             sels.append(sel)
         return y, sels
 
@@ -806,18 +807,18 @@ def ep_run(layers, x, n_used, steps, warmup, world):
     torch.cuda.synchronize()
     ms = evs[0].elapsed_time(evs[-1]) / steps
     st = stats([evs[i].elapsed_time(evs[i + 1]) for i in range(steps)])
-    coll_ms = 0.0
-    if world > 1:
+    def coll_alone(use_comm):
         # the collectives alone: the same all-reduces (one per layer, (T, H) f32) in a graph
         bufs = [torch.zeros((T, hid), device=x.device) for _ in layers]
+        red = (lambda b: comm.all_reduce(b)) if use_comm else (lambda b: dist.all_reduce(b))
         cgraph = torch.cuda.CUDAGraph()
         with torch.cuda.stream(cs):
             for bf in bufs:
-                dist.all_reduce(bf)
+                red(bf)
             torch.cuda.synchronize()
             with torch.cuda.graph(cgraph, stream=cs):
                 for bf in bufs:
-                    dist.all_reduce(bf)
+                    red(bf)
         torch.cuda.synchronize()
         for _ in range(3):
             cgraph.replay()
@@ -829,9 +830,14 @@ def ep_run(layers, x, n_used, steps, warmup, world):
             cgraph.replay()
         c1.record()
         torch.cuda.synchronize()
-        coll_ms = c0.elapsed_time(c1) / steps
         del cgraph
-    return st, ms, sels, y, graph, coll_ms
+        return c0.elapsed_time(c1) / steps
+
+    coll_ms = nccl_ms = 0.0
+    if world > 1:
+        coll_ms = coll_alone(comm is not None)
+        nccl_ms = coll_alone(False) if comm is not None else coll_ms
+    return st, ms, sels, y, graph, coll_ms, nccl_ms
 
 
 def ep_step_bytes(sels, n_exp, expert_bytes, router_bytes, world):
@@ -885,7 +891,7 @@ def ep_fused_ms(q, layers, x, steps):
     return e0.elapsed_time(e1) / steps
 
 
-def ep_config4_sweep(q, dev, world, rank, steps, warmup):
+def ep_config4_sweep(q, dev, world, rank, steps, warmup, comm=None):
     """The 235B-A22B layer (hidden 4096, expert FFN 1536, 128 experts, top-8; Q4_K gate/up,
     Q6_K down) expert-parallel over `world` GPUs: EP4_LAYERS layers per step (of the
     model's 94), decode batches of T in EP4_TOKENS tokens (total over the job), one
@@ -905,17 +911,18 @@ def ep_config4_sweep(q, dev, world, rank, steps, warmup):
     points = []
     for T in EP4_TOKENS:
         x = torch.randn((T, EP4_H), generator=torch.Generator(device=dev).manual_seed(900 + T), device=dev)
-        st, ms, sels, y, graph, coll_ms = ep_run(layers, x, K_USED, steps, warmup, world)
+        st, ms, sels, y, graph, coll_ms, nccl_ms = ep_run(layers, x, K_USED, steps, warmup, world, comm)
         del graph
-        t = torch.tensor([ms, st["median"], coll_ms], device=dev)
+        t = torch.tensor([ms, st["median"], coll_ms, nccl_ms], device=dev)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, med, coll_ms = t.tolist()
+        ms, med, coll_ms, nccl_ms = t.tolist()
         nbytes = ep_step_bytes(sels, E, expert_bytes, router_bytes, world)
         # one layer's output against the fused single-GPU layer (rank 0), T = 8
         err = None
         if T == 8:
-            y1, _, _ = moe_layer(x, layers[0][0], layers[0][2], K_USED, norm_w=layers[0][1], norm_eps=1e-6)
+            y1, _, _ = moe_layer(x, layers[0][0], layers[0][2], K_USED, norm_w=layers[0][1], norm_eps=1e-6,
+                                 comm=comm)
             torch.cuda.synchronize()
             if rank == 0:
                 err = ep_check(q, dev, base, shapes, E, EP4_UNIQUE, layers[0], x, y1, K_USED)
@@ -925,6 +932,7 @@ def ep_config4_sweep(q, dev, world, rank, steps, warmup):
                        "fused_layer_ms_per_step": fused_ms,
                        "tokens_per_s": T * 1000.0 / ms,
                        "collective_ms_per_step": coll_ms if world > 1 else 0.0,
+                       "nccl_allreduce_ms_per_step": nccl_ms if world > 1 else 0.0,
                        "kernel_ms_per_step": ms - coll_ms if world > 1 else ms,
                        "hbm_bytes_per_step": nbytes, "hbm_gbs_aggregate": gbs,
                        "roofline": {"bound": "hbm", "achieved": gbs, "peak": world * hbm,
@@ -932,6 +940,7 @@ def ep_config4_sweep(q, dev, world, rank, steps, warmup):
                                     "frac": gbs / (world * hbm)},
                        "ep_nrmse": err})
     return {"workload": "qwen3-235b-a22b MoE FFN layer, expert-parallel decode", "layers": EP4_LAYERS,
+            "collective": "peer-memory all-reduce (qwb_ep_allreduce_f32)" if comm is not None else "NCCL all-reduce",
             "hidden": EP4_H, "expert_ffn": EP4_F, "experts": E, "top_k": K_USED, "experts_per_gpu": n,
             "n_gpus": world, "collectives_per_step": EP4_LAYERS if world > 1 else 0,
             "note": "kernel_ms_per_step = step - the same all-reduces timed alone in a graph",
@@ -945,10 +954,12 @@ def run_ep(args, world, rank, local):
     import torch.distributed as dist
 
     import questwend_b200 as q
-    from questwend_b200.expert_parallel import moe_layer, shard_range
+    from questwend_b200.expert_parallel import PeerAllReduce, moe_layer, shard_range
     q.lib()
     dev = torch.device("cuda", local)
     lo, n = shard_range(E, world, rank)
+    # the per-layer all-reduce over peer memory; messages up to the 235B layer at 64 tokens
+    comm = PeerAllReduce(max_bytes=max(world * H, EP4_TOKENS[-1] * EP4_H) * 4)
     base = [torch.from_numpy(a).to(dev) for a in quantized_experts(seed=0)]
     shapes = ((Q4_K, F, H), (Q4_K, F, H), (Q6_K, H, F))
     n_layers = args.layers
@@ -956,7 +967,8 @@ def run_ep(args, world, rank, local):
     # the step's batch: one token per rank, the same (N, H) rows on every rank
     x = torch.randn((world, H), generator=torch.Generator(device=dev).manual_seed(77), device=dev)
     with ClockSampler(local) as clk:
-        st, ms_step, sels, y_graph, graph, coll_ms = ep_run(layers, x, K_USED, args.steps, args.warmup, world)
+        st, ms_step, sels, y_graph, graph, coll_ms, nccl_ms = ep_run(layers, x, K_USED, args.steps, args.warmup,
+                                                                     world, comm)
         # end to end: the batch from pinned host memory (every rank reads all N rows), the
         # rank's own token's output row back
         x_host = torch.randn((world, H), generator=torch.Generator().manual_seed(5)).pin_memory()
@@ -975,20 +987,25 @@ def run_ep(args, world, rank, local):
     ms_e2e = e0.elapsed_time(e1) / args.steps
     del graph
     flags, bad, cnt = q.read_status()
-    times = torch.tensor([ms_step, ms_e2e, coll_ms, st["median"], st["p10"], st["p90"], float(flags)], device=dev)
+    times = torch.tensor([ms_step, ms_e2e, coll_ms, nccl_ms, st["median"], st["p10"], st["p90"], float(flags)],
+                         device=dev)
     dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    ms_step, ms_e2e, coll_ms, med, p10, p90, flags = times.tolist()
+    ms_step, ms_e2e, coll_ms, nccl_ms, med, p10, p90, flags = times.tolist()
     expert_bytes = 2 * EXPERT_GU + EXPERT_D
     nbytes = ep_step_bytes(sels, E, expert_bytes, E * H * 4, world)
     # multi-GPU correctness: one layer against the fused single-GPU layer (rank 0 decides)
-    y1, _, _ = moe_layer(x, layers[0][0], layers[0][2], K_USED, norm_w=layers[0][1], norm_eps=1e-6)
+    y1, _, _ = moe_layer(x, layers[0][0], layers[0][2], K_USED, norm_w=layers[0][1], norm_eps=1e-6, comm=comm)
     torch.cuda.synchronize()
     err = ep_check(q, dev, base, shapes, E, UNIQUE, layers[0], x, y1, K_USED) if rank == 0 else 0.0
     bad_t = torch.tensor([1.0 if (err > 1e-5 or flags) else 0.0], device=dev)
     dist.all_reduce(bad_t, op=dist.ReduceOp.MAX)
     if bad_t.item():
         raise RuntimeError(f"expert-parallel output differs from the fused layer: nrmse {err:.3e}, flags {flags}")
-    c4 = None if args.no_ep4 else ep_config4_sweep(q, dev, world, rank, max(20, args.steps // 10), args.warmup)
+    c4 = None if args.no_ep4 else ep_config4_sweep(q, dev, world, rank, max(20, args.steps // 10), args.warmup,
+                                                   comm)
+    torch.cuda.synchronize()
+    dist.barrier()
+    comm.close()
     hbm, kind = peaks()
     gbs = nbytes / (ms_step * 1e-3) / 1e9
     if rank == 0:
@@ -1005,9 +1022,11 @@ def run_ep(args, world, rank, local):
             "e2e": {"value": world * 1000.0 / ms_e2e, "unit": "tokens/s", "h2d_bytes_per_step": world * H * 4,
                     "d2h_bytes_per_step": H * 4},
             "collectives_per_step": n_layers,
+            "collective": "peer-memory all-reduce (qwb_ep_allreduce_f32), one per layer",
             "collective_ms_per_step": coll_ms,
+            "nccl_allreduce_ms_per_step": nccl_ms,
             "kernel_ms_per_step": ms_step - coll_ms,
-            "gpu_launches": args.steps * 7 * n_layers,
+            "gpu_launches": args.steps * 4 * n_layers,  # router, gate/up, down, all-reduce per layer
             "ep_nrmse": err,
             "device_errors": int(flags),
             "roofline": {"bound": "hbm", "kernel": "whole expert-parallel step, aggregate over the GPUs",

@@ -230,6 +230,17 @@ typedef struct qwb_moe_ffn_desc {
                                 ffn_in of build_moe), fused into the router kernel; the
                                 residual is still added un-normalised. */
     float norm_eps;
+    /* Shared expert (core/runtime.cpp:2825-2833), present when shexp_down.data != NULL:
+     *   sh = shexp_down . (silu(shexp_gate . ffn_in) * (shexp_up . ffn_in)),
+     *   times sigmoid(shexp_gate_inp . ffn_in) when shexp_gate_inp != NULL,
+     * added to the routed experts' weighted sum before the residual.  shexp_gate / up have
+     * the routed gate / up type, shexp_down the routed down type, rows contiguous and
+     * 16-byte aligned.  With F_sh == F and up to 8 tokens it runs inside the routed
+     * experts' gate/up and down kernels (one more (token, expert) pair per token). */
+    qwb_tensor shexp_gate;   /* [H, F_sh] */
+    qwb_tensor shexp_up;     /* [H, F_sh] */
+    qwb_tensor shexp_down;   /* [F_sh, H] */
+    const float *shexp_gate_inp; /* [H] f32, or NULL */
 } qwb_moe_ffn_desc;
 
 QWB_API size_t qwb_moe_ffn_workspace_size(const qwb_moe_ffn_desc *desc);
@@ -267,10 +278,36 @@ typedef struct qwb_moe_ep_layer_desc {
     float *out;              /* [T][H] f32 partial sums (overwritten) */
     int32_t *selected;       /* out: [T][n_used] expert ids, descending probability, or NULL */
     float *weights;          /* out: [T][n_used] renormalised routing weights, or NULL */
+    /* the shared expert, as in qwb_moe_ffn_desc: give it to exactly one GPU (the one
+       adding the residual), shexp_down.data == NULL on the others */
+    qwb_tensor shexp_gate, shexp_up, shexp_down;
+    const float *shexp_gate_inp;
 } qwb_moe_ep_layer_desc;
 QWB_API size_t qwb_moe_ep_layer_workspace_size(const qwb_moe_ep_layer_desc *desc);
 QWB_API qwb_status qwb_moe_ep_layer(const qwb_moe_ep_layer_desc *desc, void *workspace, size_t workspace_bytes,
                                     qwb_status_block *d_status, qwb_stream_t stream);
+
+/* The per-layer all-reduce of the partial outputs over peer memory (NVLink / NVSwitch), an
+ * alternative to the caller's NCCL all-reduce for decode-sized messages.  One process per
+ * GPU of one node, up to 8 GPUs:
+ *   1. qwb_ep_comm_create on every GPU (current device): allocates the exchange buffer
+ *      (about 16 x max_bytes) and writes its CUDA IPC handle (qwb_ep_comm_handle_size()
+ *      bytes) to handle_out;
+ *   2. the caller gathers the handles of all GPUs in rank order (any host channel) and
+ *      passes them to qwb_ep_comm_connect;
+ *   3. qwb_ep_allreduce_f32 (stream-ordered, CUDA-graph capturable): out = the sum over
+ *      GPUs of `in` (n floats, n % 4 == 0, 16-byte aligned, n * 4 <= max_bytes; in == out
+ *      allowed), added in rank order so every GPU holds the same bits.  Every GPU must
+ *      issue the same calls in the same order with the same n.  A peer that does not
+ *      arrive within 5 s sets QWB_DEVERR_TIMEOUT in d_status and leaves out unwritten;
+ *   4. qwb_ep_comm_destroy after the last call has completed. */
+typedef struct qwb_ep_comm qwb_ep_comm;
+QWB_API size_t qwb_ep_comm_handle_size(void);
+QWB_API qwb_status qwb_ep_comm_create(int world, int rank, size_t max_bytes, qwb_ep_comm **comm, void *handle_out);
+QWB_API qwb_status qwb_ep_comm_connect(qwb_ep_comm *comm, const void *handles);
+QWB_API qwb_status qwb_ep_allreduce_f32(qwb_ep_comm *comm, const float *in, float *out, int64_t n,
+                                        qwb_status_block *d_status, qwb_stream_t stream);
+QWB_API void qwb_ep_comm_destroy(qwb_ep_comm *comm);
 
 /* ------------------------------------------------------------- expert pool writes
  * The expert cache keeps each role's experts in a pool tensor [ne0, ne1, n_slots] (one

@@ -131,6 +131,9 @@ def ref():
         lib.qref_moe_layer.restype = f64
         lib.qref_moe_layer.argtypes = [vp, i64, i64, vp, i64, i64, i32, vp, vp, i32, vp, i64, i64,
                                        vp, vp, vp, vp, vp, vp, i32, vp, f32]
+        lib.qref_moe_layer_shexp.restype = f64
+        lib.qref_moe_layer_shexp.argtypes = [vp, i64, i64, vp, i64, i64, i32, vp, vp, i32, vp, i64, i64, vp, f32,
+                                             vp, vp, vp, i64, vp, vp, vp, vp]
         lib.qref_backend_mul_mat_id.argtypes = [cp, i32, vp, i64, i64, i64, vp, i64, i64, vp, i64, i64, vp]
         lib.qref_backend_get_rows.argtypes = [cp, i32, vp, i64, i64, vp, i64, vp]
         lib.qref_mul_mat.restype = f64
@@ -337,6 +340,26 @@ def rms_norm_mul(x, w, eps):
     y = np.zeros_like(x)
     port().qo_rms_norm_mul(_p(x), _p(w), eps, x.shape[0], x.shape[1], _p(y))
     return y
+
+
+def moe_layer_shexp(x, router_w, type_gu, gate, up, type_d, down, F, n_mat, n_used, sh_gate, sh_up, sh_down, Fs,
+                    sh_gate_inp=None, norm_w=None, norm_eps: float = 1e-6):
+    """One build_moe layer plus the shared expert of core/runtime.cpp:2825-2833 (gate/up of
+    type_gu [H, Fs], down of type_d [Fs, H], optional sigmoid gate [H]) on the reference's
+    own ggml CPU backend (oracle/_ref).  Returns dict(out, selected, weights)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    router_w = np.ascontiguousarray(router_w, dtype=np.float32)
+    nw = None if norm_w is None else np.ascontiguousarray(norm_w, dtype=np.float32)
+    gi = None if sh_gate_inp is None else np.ascontiguousarray(sh_gate_inp, dtype=np.float32)
+    T, H = x.shape
+    E = router_w.shape[0]
+    out = np.zeros((T, H), dtype=np.float32)
+    sel = np.zeros((T, n_used), dtype=np.int32)
+    w = np.zeros((T, n_used), dtype=np.float32)
+    ref().qref_moe_layer_shexp(_p(x), H, T, _p(router_w), E, n_used, type_gu, _p(gate), _p(up), type_d, _p(down), F,
+                               n_mat, _p(nw), norm_eps, _p(sh_gate), _p(sh_up), _p(sh_down), Fs, _p(gi), _p(out),
+                               _p(sel), _p(w))
+    return dict(out=out, selected=sel, weights=w)
 
 
 def moe_layer(x, router_w, type_gu, gate, up, type_d, down, F, n_mat, n_used,

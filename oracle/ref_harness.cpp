@@ -240,13 +240,20 @@ double qref_route(const float * logits, int64_t E, int64_t T, int64_t n_used, in
 //   gate/up  [H, F, n_mat] (type_gu)   down [F, H, n_mat] (type_d)
 //   g2s      3 x E int32 (gate, up, down tables) or NULL
 // outputs: out [H, T], selected [n_used, T], weights [n_used, T]; optional act [F, n_used, T].
-double qref_moe_layer(const float * x, int64_t H, int64_t T,
-                      const float * router_w, int64_t E, int64_t n_used,
-                      int type_gu, const void * gate, const void * up,
-                      int type_d, const void * down, int64_t F, int64_t n_mat,
-                      const int32_t * g2s, const float * mask,
-                      float * out, int32_t * selected, float * weights, float * act_out,
-                      int iters, const float * norm_w, float norm_eps) {
+// Shared expert of a layer (core/runtime.cpp:2825-2833), or type -1 / null pointers.
+struct SharedExpert {
+    const void * gate, * up, * down;  // [H, Fs], [H, Fs], [Fs, H] of the routed gate/up, down types
+    int64_t Fs;
+    const float * gate_inp;           // [H] or null
+};
+
+static double moe_layer_graph(const float * x, int64_t H, int64_t T,
+                              const float * router_w, int64_t E, int64_t n_used,
+                              int type_gu, const void * gate, const void * up,
+                              int type_d, const void * down, int64_t F, int64_t n_mat,
+                              const int32_t * g2s, const float * mask,
+                              float * out, int32_t * selected, float * weights, float * act_out,
+                              int iters, const float * norm_w, float norm_eps, const SharedExpert * sh) {
     Graph g(1024);
     ggml_context * ctx = g.ctx;
     ggml_tensor * tx  = ggml_new_tensor_2d(ctx, GGML_TYPE_F32, H, T);
@@ -302,13 +309,30 @@ double qref_moe_layer(const float * x, int64_t H, int64_t T,
         }
         if (n_used == 1) moe = ggml_cont(ctx, moe);
     }
+    // shared expert, added to the routed sum (core/runtime.cpp:2825-2833)
+    ggml_tensor *tsg = nullptr, *tsu = nullptr, *tsd = nullptr, *tsi = nullptr;
+    if (sh) {
+        tsg = ggml_new_tensor_2d(ctx, (ggml_type) type_gu, H, sh->Fs);
+        tsu = ggml_new_tensor_2d(ctx, (ggml_type) type_gu, H, sh->Fs);
+        tsd = ggml_new_tensor_2d(ctx, (ggml_type) type_d, sh->Fs, H);
+        ggml_tensor * gs = ggml_mul_mat(ctx, tsg, xin);
+        ggml_tensor * us = ggml_mul_mat(ctx, tsu, xin);
+        ggml_tensor * shv = ggml_mul_mat(ctx, tsd, ggml_mul(ctx, ggml_silu(ctx, gs), us));
+        if (sh->gate_inp) {
+            tsi = ggml_new_tensor_1d(ctx, GGML_TYPE_F32, H);
+            shv = ggml_mul(ctx, shv, ggml_sigmoid(ctx, ggml_mul_mat(ctx, tsi, xin)));
+        }
+        moe = ggml_add(ctx, moe, shv);
+    }
     ggml_tensor * selc = ggml_cont(ctx, sel);
     ggml_build_forward_expand(g.gf, moe);
     ggml_build_forward_expand(g.gf, selc);
     if (act_out) ggml_build_forward_expand(g.gf, act);
 
     g.bind(tg, gate); g.bind(tu, up); g.bind(td, down);
+    if (sh) { g.bind(tsg, sh->gate); g.bind(tsu, sh->up); g.bind(tsd, sh->down); }
     g.alloc_rest();
+    if (tsi) ggml_backend_tensor_set(tsi, sh->gate_inp, 0, ggml_nbytes(tsi));
     ggml_backend_tensor_set(tx, x, 0, ggml_nbytes(tx));
     ggml_backend_tensor_set(trw, router_w, 0, ggml_nbytes(trw));
     if (tm) ggml_backend_tensor_set(tm, mask, 0, ggml_nbytes(tm));
@@ -320,6 +344,30 @@ double qref_moe_layer(const float * x, int64_t H, int64_t T,
     if (weights) ggml_backend_tensor_get(w, weights, 0, ggml_nbytes(w));
     if (act_out) ggml_backend_tensor_get(act, act_out, 0, ggml_nbytes(act));
     return ms;
+}
+
+double qref_moe_layer(const float * x, int64_t H, int64_t T,
+                      const float * router_w, int64_t E, int64_t n_used,
+                      int type_gu, const void * gate, const void * up,
+                      int type_d, const void * down, int64_t F, int64_t n_mat,
+                      const int32_t * g2s, const float * mask,
+                      float * out, int32_t * selected, float * weights, float * act_out,
+                      int iters, const float * norm_w, float norm_eps) {
+    return moe_layer_graph(x, H, T, router_w, E, n_used, type_gu, gate, up, type_d, down, F, n_mat, g2s, mask, out,
+                           selected, weights, act_out, iters, norm_w, norm_eps, nullptr);
+}
+
+// the layer with a shared expert (sh_gate_inp may be null)
+double qref_moe_layer_shexp(const float * x, int64_t H, int64_t T,
+                            const float * router_w, int64_t E, int64_t n_used,
+                            int type_gu, const void * gate, const void * up,
+                            int type_d, const void * down, int64_t F, int64_t n_mat,
+                            const float * norm_w, float norm_eps,
+                            const void * sh_gate, const void * sh_up, const void * sh_down, int64_t Fs,
+                            const float * sh_gate_inp, float * out, int32_t * selected, float * weights) {
+    const SharedExpert sh{sh_gate, sh_up, sh_down, Fs, sh_gate_inp};
+    return moe_layer_graph(x, H, T, router_w, E, n_used, type_gu, gate, up, type_d, down, F, n_mat, nullptr, nullptr,
+                           out, selected, weights, nullptr, 0, norm_w, norm_eps, &sh);
 }
 
 // ------------------------------------------------------------------------------------

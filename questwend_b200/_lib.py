@@ -49,7 +49,9 @@ class MoeFfnDesc(C.Structure):
                 ("H", C.c_int64), ("F", C.c_int64), ("E", C.c_int64), ("n_used", C.c_int64),
                 ("T", C.c_int64), ("residual", C.c_void_p), ("out", C.c_void_p),
                 ("selected", C.c_void_p), ("weights", C.c_void_p), ("act", C.c_void_p),
-                ("norm_w", C.c_void_p), ("norm_eps", C.c_float)]
+                ("norm_w", C.c_void_p), ("norm_eps", C.c_float),
+                ("shexp_gate", Tensor), ("shexp_up", Tensor), ("shexp_down", Tensor),
+                ("shexp_gate_inp", C.c_void_p)]
 
 
 class MoeEpLayerDesc(C.Structure):
@@ -57,7 +59,9 @@ class MoeEpLayerDesc(C.Structure):
                 ("router_w", C.c_void_p), ("mask", C.c_void_p),
                 ("gate", Tensor), ("up", Tensor), ("down", Tensor), ("expert_lo", C.c_int64),
                 ("H", C.c_int64), ("F", C.c_int64), ("E", C.c_int64), ("n_used", C.c_int64), ("T", C.c_int64),
-                ("residual", C.c_void_p), ("out", C.c_void_p), ("selected", C.c_void_p), ("weights", C.c_void_p)]
+                ("residual", C.c_void_p), ("out", C.c_void_p), ("selected", C.c_void_p), ("weights", C.c_void_p),
+                ("shexp_gate", Tensor), ("shexp_up", Tensor), ("shexp_down", Tensor),
+                ("shexp_gate_inp", C.c_void_p)]
 
 
 _lib = None
@@ -95,6 +99,11 @@ SIGNATURES = [
     ("qwb_moe_ffn", C.c_int, [C.POINTER(MoeFfnDesc), _P, C.c_size_t, _P, _P]),
     ("qwb_moe_ep_layer_workspace_size", C.c_size_t, [C.POINTER(MoeEpLayerDesc)]),
     ("qwb_moe_ep_layer", C.c_int, [C.POINTER(MoeEpLayerDesc), _P, C.c_size_t, _P, _P]),
+    ("qwb_ep_comm_handle_size", C.c_size_t, []),
+    ("qwb_ep_comm_create", C.c_int, [C.c_int, C.c_int, C.c_size_t, C.POINTER(C.c_void_p), _P]),
+    ("qwb_ep_comm_connect", C.c_int, [_P, _P]),
+    ("qwb_ep_allreduce_f32", C.c_int, [_P, _P, _P, C.c_int64, _P, _P]),
+    ("qwb_ep_comm_destroy", None, [_P]),
     ("qwb_pool_write_slabs", C.c_int, [_TP, C.c_size_t, C.POINTER(SlabCopy), C.c_int, _P]),
     ("qwb_pool_audit_slabs", C.c_int, [_TP, C.POINTER(SlabCopy), C.c_int, C.c_int, _P, _P]),
     ("qwb_profile_enable", C.c_int, [C.c_int]),

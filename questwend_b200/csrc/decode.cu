@@ -219,14 +219,15 @@ struct RouterSmemTail {
     int sel[32];
 };
 
-__device__ void route_in_cta(const RouterDecodeArgs &r, RouterSmemTail &t) {
+__device__ void route_in_cta(const RouterDecodeArgs &r, int tok, RouterSmemTail &t) {
     const int tid = threadIdx.x, nth = blockDim.x, warp = tid >> 5, lane = tid & 31, nw = nth >> 5;
     const int E = (int) r.E, k = r.n_used;
+    const float *mask = r.mask ? r.mask + (int64_t) tok * E : nullptr;
     // 1. max logit (+ mask)
     float lmax = -INFINITY;
     for (int e = tid; e < E; e += nth) {
         float v = t.logit[e];
-        if (r.mask) v = __fadd_rn(v, r.mask[e]);
+        if (mask) v = __fadd_rn(v, mask[e]);
         if (isnan(v)) v = -INFINITY;
         t.logit[e] = v;
         lmax = fmaxf(lmax, v);
@@ -283,16 +284,22 @@ __device__ void route_in_cta(const RouterDecodeArgs &r, RouterSmemTail &t) {
         for (int j = 0; j < k; ++j) tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, pj, j));
         const float ws = tot < 6.103515625e-5f ? 6.103515625e-5f : tot;
         if (lane < k) {
-            r.sel[lane] = e;
-            r.wts[lane] = __fdiv_rn(pj, ws);
+            r.sel[tok * k + lane] = e;
+            r.wts[tok * k + lane] = __fdiv_rn(pj, ws);
 #pragma unroll
             for (int role = 0; role < 3; ++role) {
-                int64_t sl = r.g2s ? (int64_t) r.g2s[role * E + e] : e;
-                if (sl < 0 || sl >= r.n_slots[role]) {
-                    report(r.st, QWB_DEVERR_ID_RANGE, (int32_t) sl);
-                    sl = -1;
+                int64_t sl;
+                if (r.own_n > 0) {
+                    // expert parallelism: another GPU's expert is skipped here, not an error
+                    sl = (e >= r.own_lo && e < r.own_lo + r.own_n) ? e - r.own_lo : -1;
+                } else {
+                    sl = r.g2s ? (int64_t) r.g2s[role * E + e] : e;
+                    if (sl < 0 || sl >= r.n_slots[role]) {
+                        report(r.st, QWB_DEVERR_ID_RANGE, (int32_t) sl);
+                        sl = -1;
+                    }
                 }
-                r.slots[role * k + lane] = (int32_t) sl;
+                r.slots[(role * r.T + tok) * k + lane] = (int32_t) sl;
             }
         }
     }
@@ -312,6 +319,8 @@ __global__ void __launch_bounds__(kRouterThreads) router_decode_kernel(const Rou
     __shared__ double dpart[kRouterThreads / 32];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rank_in_cluster = (int) cluster.block_rank();
+    const int tok = (int) blockIdx.x / kRouterCluster;  // one cluster per token
+    const float *x = r.x + (int64_t) tok * H;
     const int e0 = rank_in_cluster * rpc;
     const int ne = max(0, min(rpc, (int) r.E - e0));
 
@@ -333,7 +342,7 @@ __global__ void __launch_bounds__(kRouterThreads) router_decode_kernel(const Rou
     // x -> shared memory, sum of squares (f32 squares, f64 sum as ggml's rms_norm)
     double acc = 0.0;
     for (int64_t i = 4 * tid; i < H; i += 4 * kRouterThreads) {
-        const float4 b = *(const float4 *) (r.x + i);
+        const float4 b = *(const float4 *) (x + i);
         *(float4 *) (xs + i) = b;
         acc += (double) __fmul_rn(b.x, b.x);
         acc += (double) __fmul_rn(b.y, b.y);
@@ -402,10 +411,21 @@ __global__ void __launch_bounds__(kRouterThreads) router_decode_kernel(const Rou
         // side work of CTAs 1..: Q8 of the normed x, one 256-chunk per warp (needed by the
         // next kernel, which waits for this grid to complete)
         const int64_t c = (int64_t) (rank_in_cluster - 1) * (kRouterThreads / 32) + warp;
-        if (c < H / 256) quantize_chunk_warp(r.kq ? 0 : 1, xs + c * 256, r.xq, 0, c * 256, H);
+        if (c < H / 256) quantize_chunk_warp(r.kq ? 0 : 1, xs + c * 256, r.xq, tok, c * 256, H);
+        if (rank_in_cluster == kRouterCluster - 1 && warp == kRouterThreads / 32 - 1 && r.sh_scale) {
+            // the shared expert's gate: sigmoid(gw . ffn_in) (ggml_sigmoid_f32: 1 / (1 + e^-v))
+            float v = 1.f;
+            if (r.sh_gate_inp) {
+                float acc = 0.f;
+                for (int64_t h = lane; h < H; h += 32) acc = fmaf(r.sh_gate_inp[h], xs[h], acc);
+                acc = warp_sum(acc);
+                v = 1.f / (1.f + expf(-acc));
+            }
+            if (lane == 0) r.sh_scale[tok] = v;
+        }
         return;
     }
-    route_in_cta(r, tail);
+    route_in_cta(r, tok, tail);
 }
 
 // ---------------------------------------------------------------- gate/up
@@ -633,6 +653,279 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) down_decode_kernel(const Do
     QWB_TRACE(2, 6);
 }
 
+// ---------------------------------------------------------------- pair lists
+// The decode batch as (token, expert) pairs: every routed pair whose three slots are
+// valid (under expert parallelism: the experts this GPU owns), in (token, slot) order,
+// then one shared-expert pair per token.  Each CTA of the gate/up and down kernels builds
+// the same list from the router's slot ids (a ballot compaction, no extra kernel).
+struct PairList {
+    int tok[kPairsMax];
+    int sg[kPairsMax], su[kPairsMax], sd[kPairsMax];  // slots; -2: the shared expert
+    float w[kPairsMax];                                // routing weight / shared-expert factor
+};
+
+// all threads of the CTA (blockDim.x >= T * n_used); ends with a CTA barrier
+__device__ int build_pairs(const PairsCommon &a, PairList &pl, int *warp_cnt) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = (int) (blockDim.x >> 5);
+    const int TK = a.T * a.n_used;
+    int g = -1, u = -1, d = -1;
+    if (tid < TK) {
+        g = a.slots[tid];
+        u = a.slots[TK + tid];
+        d = a.slots[2 * TK + tid];
+    }
+    const bool valid = tid < TK && g >= 0 && u >= 0 && d >= 0;
+    const unsigned bal = __ballot_sync(0xffffffffu, valid);
+    if (lane == 0) warp_cnt[warp] = __popc(bal);
+    __syncthreads();
+    int base = 0, total = 0;
+    for (int w = 0; w < nw; ++w) {
+        const int c = warp_cnt[w];
+        if (w < warp) base += c;
+        total += c;
+    }
+    if (valid) {
+        const int c = base + __popc(bal & ((1u << lane) - 1u));
+        pl.tok[c] = tid / a.n_used;
+        pl.sg[c] = g;
+        pl.su[c] = u;
+        pl.sd[c] = d;
+        pl.w[c] = a.wts[tid];
+    }
+    if (a.shexp && tid < a.T) {
+        const int c = total + tid;
+        pl.tok[c] = tid;
+        pl.sg[c] = pl.su[c] = pl.sd[c] = -2;
+        pl.w[c] = a.sh_scale ? a.sh_scale[tid] : 1.f;
+    }
+    __syncthreads();
+    return total + (a.shexp ? a.T : 0);
+}
+
+// Gate/up of every pair: the (pair, row) space is cut into one contiguous range per CTA,
+// streamed through two buffers of batch_rows (gate, up) row pairs, bulk copies per
+// (pair, row) segment; lane = (row, superblock) as in gateup_decode_kernel, the
+// activation superblock reloaded when a lane's row belongs to another token.
+template <int NSB>
+__global__ void __launch_bounds__(kDecodeThreads, 2) gateup_pairs_kernel(const PairsGateUpArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *bar = (uint64_t *) smem;  // [2]
+    uint8_t *buf = smem + 128;
+    __shared__ PairList pl;
+    __shared__ int wcnt[kDecodeThreads / 32];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rb = (int) a.row_bytes, RB = a.batch_rows, F = (int) a.F;
+    const size_t bstride = (size_t) 2 * RB * rb;
+    if (tid == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_mbar_init();
+    }
+    pdl_wait();  // the routing and the quantized x are ready
+    const int L = build_pairs(a.pc, pl, wcnt);
+    const int64_t P = (int64_t) L * F;
+    const int64_t p0 = P * blockIdx.x / gridDim.x, p1 = P * (blockIdx.x + 1) / gridDim.x;
+    const int n = (int) (p1 - p0);
+    const int nbat = (n + RB - 1) / RB;
+    // batch b: rows [p0 + b RB, ...) into buffer b & 1 (gate rows, then up rows), on bar[b & 1]
+    auto issue = [&](int b) {
+        const int q0 = b * RB, nq = min(RB, n - q0);
+        uint8_t *gb = buf + (size_t) (b & 1) * bstride, *ub = gb + (size_t) RB * rb;
+        for (int pass = 0; pass < 2; ++pass) {  // pass 0 counts the bytes, pass 1 issues
+            uint32_t bytes = 0;
+            const int64_t q = p0 + q0;
+            int c = (int) (q / F), r = (int) (q - (int64_t) c * F);
+            for (int off = 0; off < nq;) {
+                const int len = min(nq - off, F - r);
+                const uint8_t *sg = pl.sg[c] == -2 ? a.Wg_sh : a.Wg + (size_t) pl.sg[c] * a.g_nb2;
+                const uint8_t *su = pl.su[c] == -2 ? a.Wu_sh : a.Wu + (size_t) pl.su[c] * a.u_nb2;
+                if (pass == 0) {
+                    bytes += bulk_span_bytes(sg + (size_t) r * rb, (size_t) len * rb) +
+                             bulk_span_bytes(su + (size_t) r * rb, (size_t) len * rb);
+                } else {
+                    bulk_span_issue(gb + (size_t) off * rb, sg + (size_t) r * rb, (size_t) len * rb, &bar[b & 1]);
+                    bulk_span_issue(ub + (size_t) off * rb, su + (size_t) r * rb, (size_t) len * rb, &bar[b & 1]);
+                }
+                off += len;
+                r = 0;
+                ++c;
+            }
+            if (pass == 0) mbar_arrive_expect_tx(&bar[b & 1], bytes);
+        }
+    };
+    int issued = 0;
+    if (tid == 0) {
+        if (nbat > 0) issue(0);
+        if (nbat > 1) issue(1);
+        issued = min(nbat, 2);
+    }
+    pdl_trigger();  // the down kernel may start copying its weights now
+
+    const int s = lane % NSB;
+    ActReg<false> act;
+    int cur_tok = -1;
+    constexpr int RPW = 32 / (2 * NSB);  // (gate, up) row pairs per warp step
+    const int pp_in = lane / (2 * NSB), mat = (lane / NSB) & 1;
+    const int dstride = (int) plane_d_stride(a.K, QK_K), bstride_pl = (int) plane_bsum_stride(a.K);
+    int b = 0;
+    bool alive = true;
+    for (; b < nbat; ++b) {
+        const bool ok = mbar_wait(&bar[b & 1], (uint32_t) ((b >> 1) & 1));
+        if (!__syncthreads_and(ok)) {
+            if (tid == 0) report(a.st, QWB_DEVERR_TIMEOUT, b);
+            alive = false;
+            break;
+        }
+        const int q0 = b * RB, nq = min(RB, n - q0);
+        const uint8_t *gb = buf + (size_t) (b & 1) * bstride;
+        for (int g = warp; g * RPW < nq; g += kDecodeThreads / 32) {
+            const int i = g * RPW + pp_in;  // row pair within the batch
+            const bool in = i < nq;
+            int c = 0, r = 0;
+            float v = 0.f;
+            if (in) {
+                const int64_t q = p0 + q0 + i;
+                c = (int) (q / F);
+                r = (int) (q - (int64_t) c * F);
+                const int t = pl.tok[c];
+                if (t != cur_tok) {
+                    load_act<false>(act, a.xq.qs + (int64_t) t * a.K + (int64_t) s * 256,
+                                    a.xq.bsum + (int64_t) t * bstride_pl + s * 16, a.xq.d[(int64_t) t * dstride + s]);
+                    cur_tok = t;
+                }
+                v = dot_q4K_sb(gb + (size_t) (mat * RB + i) * rb + (size_t) s * Q4K_BYTES, act);
+            }
+#pragma unroll
+            for (int o = 1; o < NSB; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            const float up = __shfl_down_sync(0xffffffffu, v, NSB);
+            if (in && mat == 0 && s == 0) a.act[(int64_t) c * F + r] = swiglu_f(v, up);
+        }
+        __syncthreads();  // buffer b & 1 is free
+        if (tid == 0 && b + 2 < nbat) {
+            issue(b + 2);
+            issued = b + 3;
+        }
+    }
+    // a timed-out wait leaves copies possibly in flight: drain them before the CTA exits
+    if (!alive && tid == 0)
+        for (int bb = b; bb < issued; ++bb) mbar_wait(&bar[bb & 1], (uint32_t) ((bb >> 1) & 1));
+}
+
+// Down of every pair for the CTA's output rows [h0, h1), weighted sum per token (routed
+// pairs in list order, then the shared expert, then the residual: the order of the
+// reference graph).  The pairs' weight spans are resident `group` at a time (the first
+// group copied before the wait on gate/up); each warp quantizes its pair's act row to
+// Q8_K in shared memory as down_decode_kernel does.
+template <int TYPE, int NSB>
+__global__ void __launch_bounds__(kDecodeThreads, 2) down_pairs_kernel(const PairsDownArgs a) {
+    constexpr bool KQ6 = TYPE == QWB_TYPE_Q6_K;
+    constexpr int SBB = KQ6 ? Q6K_BYTES : Q4K_BYTES;
+    constexpr int NW = kDecodeThreads / 32;
+    constexpr int RPS = 32 / NSB;  // rows per warp step
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *bar = (uint64_t *) smem;  // [group] (<= 32)
+    __shared__ PairList pl;
+    __shared__ int wcnt[NW];
+    __shared__ int s_off[32];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = a.group, T = a.pc.T;
+    const int64_t h0 = a.H * blockIdx.x / gridDim.x, h1 = a.H * (blockIdx.x + 1) / gridDim.x;
+    const int n = (int) (h1 - h0);
+    const size_t rb = a.row_bytes;
+    uint8_t *actq = smem + 256;
+    float *part = (float *) (actq + (size_t) NW * NSB * 320);  // [pair][n]
+    uint8_t *wbuf = (uint8_t *) part + align_up((size_t) kPairsMax * n * 4, 128);
+    const size_t span_stride = down_span_stride(n, rb);
+
+    if (tid < G) mbar_init(&bar[tid], 1);
+    fence_mbar_init();
+    // the router grid completed before the gate/up grid passed its wait: its slot ids,
+    // weights and shared-expert factors are visible here while gate/up is still running
+    const int L = build_pairs(a.pc, pl, wcnt);
+    auto issue_group = [&](int g0) {  // thread j copies pair g0 + j into span j
+        const int j = tid;
+        if (j < G && g0 + j < L) {
+            const int c = g0 + j;
+            const uint8_t *src = (pl.sd[c] == -2 ? a.W_sh : a.W + (size_t) pl.sd[c] * a.nb2) + (size_t) h0 * rb;
+            mbar_arrive_expect_tx(&bar[j], bulk_span_bytes(src, (size_t) n * rb));
+            s_off[j] = (int) bulk_span_issue(wbuf + (size_t) j * span_stride, src, (size_t) n * rb, &bar[j]);
+        }
+    };
+    issue_group(0);
+    pdl_trigger();  // the next layer's router may prefetch its rows
+    pdl_wait();     // act (gate/up output) is ready
+    __syncthreads();  // s_off visible
+
+    const int li = lane / NSB, ls = lane % NSB;
+    const int ngroups = (L + G - 1) / G;
+    bool alive = true;
+    int gi = 0;
+    for (; gi < ngroups; ++gi) {
+        const int g0 = gi * G, gn = min(G, L - g0);
+        bool ok = true;
+        for (int jj = warp; jj < gn; jj += NW) {
+            const int c = g0 + jj;
+            uint8_t *scr = actq + (size_t) warp * NSB * 320;
+            float xv[NSB][8];
+#pragma unroll
+            for (int sb = 0; sb < NSB; ++sb) load8_normed(a.act + (int64_t) c * a.F + sb * 256, 1.f, nullptr, lane, xv[sb]);
+            __syncwarp();
+#pragma unroll
+            for (int sb = 0; sb < NSB; ++sb)
+                q8K_block_vals(xv[sb], nullptr, (int8_t *) (scr + sb * 320), (float *) (scr + sb * 320 + 256),
+                               (int16_t *) (scr + sb * 320 + 272));
+            __syncwarp();
+            ActReg<KQ6> act;
+            {
+                const uint8_t *src = scr + (size_t) ls * 320;
+                load_act<KQ6>(act, (const int8_t *) src, (const int16_t *) (src + 272), *(const float *) (src + 256));
+            }
+            __syncwarp();  // the scratch is rewritten by this warp's next pair
+            if (!mbar_wait(&bar[jj], (uint32_t) (gi & 1))) {
+                if (lane == 0) report(a.st, QWB_DEVERR_TIMEOUT, c);
+                ok = false;
+                continue;
+            }
+            const uint8_t *span = wbuf + (size_t) jj * span_stride + s_off[jj];
+            for (int i0 = 0; i0 < n; i0 += RPS) {
+                const int i = i0 + li;
+                float v = 0.f;
+                if (li < RPS && i < n) {
+                    const uint8_t *sb = span + (size_t) i * rb + (size_t) ls * SBB;
+                    if constexpr (KQ6) v = dot_q6K_sb(sb, act);
+                    else v = dot_q4K_sb(sb, act);
+                }
+                float tot = 0.f;
+#pragma unroll
+                for (int q = 0; q < NSB; ++q) tot += __shfl_sync(0xffffffffu, v, (li < RPS ? li : 0) * NSB + q);
+                if (ls == 0 && li < RPS && i < n) part[(size_t) c * n + i] = tot;
+            }
+        }
+        if (!__syncthreads_and(ok)) {
+            alive = false;
+            break;
+        }
+        if (gi + 1 < ngroups) {
+            issue_group(g0 + G);  // every warp is done with the spans (barrier above)
+            __syncthreads();      // s_off of the new group visible
+        }
+    }
+    if (alive) {
+        for (int idx = tid; idx < T * n; idx += kDecodeThreads) {
+            const int t = idx / n, i = idx - t * n;
+            float acc = 0.f;
+            for (int c = 0; c < L; ++c)
+                if (pl.tok[c] == t && pl.sd[c] != -2) acc = fmaf(pl.w[c], part[(size_t) c * n + i], acc);
+            for (int c = 0; c < L; ++c)
+                if (pl.tok[c] == t && pl.sd[c] == -2) acc = __fadd_rn(acc, __fmul_rn(part[(size_t) c * n + i], pl.w[c]));
+            const int64_t o = (int64_t) t * a.H + h0 + i;
+            a.out[o] = a.residual ? acc + a.residual[o] : acc;
+        }
+    } else if (tid < G && gi * G + tid < L) {
+        mbar_wait(&bar[tid], (uint32_t) (gi & 1));  // drain copies still in flight before the CTA exits
+    }
+}
+
 // ---------------------------------------------------------------- launches
 template <typename Kern, typename Args>
 static cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const Args &args) {
@@ -680,7 +973,7 @@ cudaError_t launch_router_decode(const RouterDecodeArgs &r, cudaStream_t s) {
     cudaError_t e = set_smem(router_decode_kernel, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kRouterCluster);
+    cfg.gridDim = dim3(kRouterCluster * std::max(1, r.T));
     cfg.blockDim = dim3(kRouterThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -772,6 +1065,111 @@ cudaError_t launch_down_decode(int type, const DownDecodeArgs &a, cudaStream_t s
     cudaError_t e = set_smem(down_decode_kernel<QWB_TYPE_Q4_K, 3>, smem);
     if (e != cudaSuccess) return e;
     return launch_pdl(down_decode_kernel<QWB_TYPE_Q4_K, 3>, dim3(G), dim3(kDecodeThreads), smem, s, a);
+}
+
+// ---------------------------------------------------------------- pair path launches
+constexpr size_t kPairsGateUpSmem = 96 * 1024;  // dynamic shared memory of the two kernels:
+constexpr size_t kPairsDownSmem = 116 * 1024;   // both fit one SM together (overlap under PDL)
+
+static size_t pairs_down_fixed(int64_t H, int nsb) {
+    const int64_t n = ceil_div(H, num_sms());
+    return 256 + (size_t) (kDecodeThreads / 32) * nsb * 320 + align_up((size_t) kPairsMax * n * 4, 128);
+}
+
+bool pairs_supported(int type_gu, int type_d, int64_t H, int64_t F, int64_t E, int n_used, int T, size_t rb_gu,
+                     size_t nb1_g, size_t nb1_u, size_t rb_d, size_t nb1_d) {
+    if (type_gu != QWB_TYPE_Q4_K || (type_d != QWB_TYPE_Q4_K && type_d != QWB_TYPE_Q6_K)) return false;
+    if (nb1_g != rb_gu || nb1_u != rb_gu || nb1_d != rb_d || rb_gu % 16) return false;
+    if (H != 2048 && H != 4096) return false;
+    if (F % 256) return false;
+    const int nsb = (int) (F / 256);
+    if (nsb != 2 && nsb != 3 && nsb != 4 && nsb != 6) return false;
+    if (T < 1 || T > kPairsMaxT || n_used < 1 || n_used > kPairsMaxUsed) return false;
+    if (E > kMaxRouteE || E < kRouterCluster || E % kRouterCluster) return false;
+    if (4 * rb_gu + 128 > kPairsGateUpSmem) return false;
+    const int64_t n = ceil_div(H, num_sms());
+    return pairs_down_fixed(H, nsb) + down_span_stride((int) n, rb_d) <= kPairsDownSmem;
+}
+
+cudaError_t launch_gateup_pairs(PairsGateUpArgs a, cudaStream_t s) {
+    a.batch_rows = (int) ((kPairsGateUpSmem - 128) / (4 * a.row_bytes));
+    const size_t smem = 128 + (size_t) 4 * a.batch_rows * a.row_bytes;
+    const int G = num_sms();
+    if (a.K == 2048) {
+        cudaError_t e = set_smem(gateup_pairs_kernel<8>, smem);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(gateup_pairs_kernel<8>, dim3(G), dim3(kDecodeThreads), smem, s, a);
+    }
+    cudaError_t e = set_smem(gateup_pairs_kernel<16>, smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(gateup_pairs_kernel<16>, dim3(G), dim3(kDecodeThreads), smem, s, a);
+}
+
+template <int TYPE, int NSB>
+static cudaError_t launch_down_pairs_t(const PairsDownArgs &a, size_t smem, cudaStream_t s) {
+    cudaError_t e = set_smem(down_pairs_kernel<TYPE, NSB>, smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(down_pairs_kernel<TYPE, NSB>, dim3(num_sms()), dim3(kDecodeThreads), smem, s, a);
+}
+
+cudaError_t launch_down_pairs(int type, PairsDownArgs a, cudaStream_t s) {
+    const int nsb = (int) (a.F / 256);
+    const int64_t n = ceil_div(a.H, num_sms());
+    const size_t fixed = pairs_down_fixed(a.H, nsb), span = down_span_stride((int) n, a.row_bytes);
+    if (fixed + span > kPairsDownSmem) return cudaErrorInvalidValue;
+    a.group = (int) std::min<size_t>(16, (kPairsDownSmem - fixed) / span);
+    const size_t smem = fixed + (size_t) a.group * span;
+    const bool q6 = type == QWB_TYPE_Q6_K;
+    switch (nsb) {
+        case 2: return q6 ? launch_down_pairs_t<QWB_TYPE_Q6_K, 2>(a, smem, s) : launch_down_pairs_t<QWB_TYPE_Q4_K, 2>(a, smem, s);
+        case 3: return q6 ? launch_down_pairs_t<QWB_TYPE_Q6_K, 3>(a, smem, s) : launch_down_pairs_t<QWB_TYPE_Q4_K, 3>(a, smem, s);
+        case 4: return q6 ? launch_down_pairs_t<QWB_TYPE_Q6_K, 4>(a, smem, s) : launch_down_pairs_t<QWB_TYPE_Q4_K, 4>(a, smem, s);
+        case 6: return q6 ? launch_down_pairs_t<QWB_TYPE_Q6_K, 6>(a, smem, s) : launch_down_pairs_t<QWB_TYPE_Q4_K, 6>(a, smem, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t run_pairs_layer(const PairsLayer &p, cudaStream_t s) {
+    const bool sh = p.sh_down != nullptr;
+    RouterDecodeArgs r{};
+    r.x = p.x; r.router_w = p.router_w; r.mask = p.mask; r.norm_w = p.norm_w; r.norm_eps = p.norm_eps;
+    r.H = p.H; r.E = p.E; r.n_used = p.n_used; r.T = p.T;
+    r.g2s = p.g2s;
+    r.n_slots[0] = p.gate->ne[2]; r.n_slots[1] = p.up->ne[2]; r.n_slots[2] = p.down->ne[2];
+    r.own_lo = p.own_lo; r.own_n = p.own_n;
+    r.sel = p.sel; r.wts = p.wts; r.slots = p.slots;
+    r.xq = p.xq; r.kq = 1;
+    r.sh_gate_inp = sh ? p.sh_gate_inp : nullptr;
+    r.sh_scale = sh ? p.sh_scale : nullptr;
+    r.st = p.st;
+    cudaError_t e = launch_router_decode(r, s);
+    if (e != cudaSuccess) return e;
+    profile_mark(s, QWB_KERNEL_ROUTER);
+    PairsCommon pc{};
+    pc.T = p.T; pc.n_used = p.n_used; pc.slots = p.slots; pc.wts = p.wts;
+    pc.shexp = sh ? 1 : 0;
+    pc.sh_scale = sh ? p.sh_scale : nullptr;
+    PairsGateUpArgs g{};
+    g.pc = pc;
+    g.Wg = (const uint8_t *) p.gate->data; g.Wu = (const uint8_t *) p.up->data;
+    g.g_nb2 = p.gate->nb[2]; g.u_nb2 = p.up->nb[2]; g.row_bytes = row_bytes(p.gate->type, p.H);
+    g.Wg_sh = sh ? (const uint8_t *) p.sh_gate->data : nullptr;
+    g.Wu_sh = sh ? (const uint8_t *) p.sh_up->data : nullptr;
+    g.F = p.F; g.K = p.H; g.n_slots_g = p.gate->ne[2]; g.n_slots_u = p.up->ne[2];
+    g.xq = p.xq; g.act = p.act; g.st = p.st;
+    e = launch_gateup_pairs(g, s);
+    if (e != cudaSuccess) return e;
+    profile_mark(s, QWB_KERNEL_GATE_UP);
+    PairsDownArgs d{};
+    d.pc = pc;
+    d.W = (const uint8_t *) p.down->data; d.nb2 = p.down->nb[2]; d.row_bytes = row_bytes(p.down->type, p.F);
+    d.W_sh = sh ? (const uint8_t *) p.sh_down->data : nullptr;
+    d.F = p.F; d.H = p.H; d.n_slots = p.down->ne[2];
+    d.act = p.act; d.out = p.out; d.residual = p.residual; d.st = p.st;
+    e = launch_down_pairs(p.down->type, d, s);
+    if (e != cudaSuccess) return e;
+    profile_mark(s, QWB_KERNEL_DOWN);
+    return cudaSuccess;
 }
 
 }  // namespace qwb

@@ -16,8 +16,10 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "decode.cuh"
 #include "kernels.cuh"
 #include "mmid.cuh"
+#include "moe.cuh"
 #include "route.cuh"
 
 namespace qwb {
@@ -33,9 +35,11 @@ __global__ void local_ids_kernel(const int32_t *__restrict__ sel, int64_t P, int
     lid[i] = (e >= lo && e < lo + n_local) ? (int32_t) (e - lo) : -1;
 }
 
-// out[t] = sum over local slots j of w[t][j] * ex[t][j]  (slot order, f32) (+ residual[t])
+// out[t] = sum over local slots j of w[t][j] * ex[t][j]  (slot order, f32)
+//          (+ sh[t] * sh_scale[t], the shared expert) (+ residual[t])
 __global__ void weighted_sum_local_kernel(const float *__restrict__ ex, const float *__restrict__ w,
-                                          const int32_t *__restrict__ lid, const float *__restrict__ residual,
+                                          const int32_t *__restrict__ lid, const float *__restrict__ sh,
+                                          const float *__restrict__ sh_scale, const float *__restrict__ residual,
                                           float *__restrict__ out, int64_t H, int n_used, int64_t T) {
     const int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= H * T) return;
@@ -43,6 +47,7 @@ __global__ void weighted_sum_local_kernel(const float *__restrict__ ex, const fl
     float acc = 0.f;
     for (int j = 0; j < n_used; ++j)
         if (lid[t * n_used + j] >= 0) acc = fmaf(w[t * n_used + j], ex[(t * n_used + j) * H + h], acc);
+    if (sh) acc = __fadd_rn(acc, sh_scale ? __fmul_rn(sh[i], sh_scale[t]) : sh[i]);
     out[i] = residual ? acc + residual[i] : acc;
 }
 
@@ -58,8 +63,11 @@ struct EpPlan {
     bool kq_gu, kq_d;
     int NT;
     bool stream;  // expert GEMVs on the streaming kernel (index: one tile per expert)
+    bool pairs;   // decode batches of <= 8 tokens on the pair kernels (decode.cu)
+    Shexp sh;
     int64_t P, n_local;
-    size_t off_logits, off_sel, off_w, off_xn, off_xq, off_lid, off_index, off_act, off_actq, off_ex, total;
+    size_t off_logits, off_sel, off_w, off_xn, off_xq, off_lid, off_index, off_act, off_actq, off_ex;
+    size_t off_slots, off_shs, off_sh, total;
 };
 qwb_status plan_ep(const qwb_moe_ep_layer_desc *d, EpPlan &p) {
     if (!d) return QWB_ERR_INVALID_ARG;
@@ -73,9 +81,16 @@ qwb_status plan_ep(const qwb_moe_ep_layer_desc *d, EpPlan &p) {
     if (d->gate.ne[0] != d->H || d->gate.ne[1] != d->F || d->up.ne[0] != d->H || d->up.ne[1] != d->F ||
         d->up.ne[2] != p.n_local || d->down.ne[0] != d->F || d->down.ne[1] != d->H || d->down.ne[2] != p.n_local)
         return QWB_ERR_SHAPE;
+    qwb_status rc = shexp_check(d->shexp_gate, d->shexp_up, d->shexp_down, d->shexp_gate_inp, tg, td, d->H, p.sh);
+    if (rc != QWB_OK) return rc;
     p.kq_gu = tg != QWB_TYPE_Q8_0;
     p.kq_d = td != QWB_TYPE_Q8_0;
     p.P = d->n_used * d->T;
+    // the pair kernels when few pairs are expected here (they read an expert's rows once
+    // per pair; the streaming kernels read each selected expert once for all its tokens)
+    p.pairs = d->T * d->n_used * p.n_local <= (int64_t) kPairsDirect * d->E && (!p.sh.F || p.sh.F == d->F) &&
+              pairs_supported(tg, td, d->H, d->F, d->E, (int) d->n_used, (int) d->T, row_bytes(tg, d->H),
+                              d->gate.nb[1], d->up.nb[1], row_bytes(td, d->F), d->down.nb[1]);
     p.stream = stream_fits_ffn(tg, d->H, d->gate.nb[1], d->up.nb[1], td, d->F, d->down.nb[1]);
     p.NT = p.stream ? (int) std::max<int64_t>(1, p.P) : pick_nt(std::max<int64_t>(1, p.P * p.n_local / d->E), p.n_local);
     size_t o = kCtrlBytes;
@@ -87,9 +102,12 @@ qwb_status plan_ep(const qwb_moe_ep_layer_desc *d, EpPlan &p) {
     p.off_xq = o; o += planes_bytes(d->T, d->H, p.kq_gu);
     p.off_lid = o; o += align_up((size_t) p.P * 4, 256);
     p.off_index = o; o += mmid_index_bytes(std::max<int64_t>(p.P, 1), p.n_local, p.NT);
-    p.off_act = o; o += align_up((size_t) p.P * d->F * 4, 256);
+    p.off_act = o; o += align_up((size_t) (p.P + d->T) * d->F * 4, 256);
     p.off_actq = o; o += planes_bytes(p.P, d->F, p.kq_d);
     p.off_ex = o; o += align_up((size_t) p.P * d->H * 4, 256);
+    p.off_slots = o; o += align_up((size_t) 3 * p.P * 4, 256);
+    p.off_shs = o; o += align_up((size_t) d->T * 4, 256);
+    p.off_sh = o; o += shexp_bytes(p.sh, d->H, d->T);
     p.total = o;
     return QWB_OK;
 }
@@ -131,6 +149,22 @@ extern "C" QWB_API qwb_status qwb_moe_ep_layer(const qwb_moe_ep_layer_desc *d, v
     float *ex = (float *) (w + p.off_ex);
     cudaError_t e;
     profile_mark(s, 0);
+    if (p.pairs) {
+        // decode batches: router clusters, gate/up and down over the pairs routed to this
+        // GPU's experts (and the shared expert), PDL-chained
+        PairsLayer L{};
+        L.x = d->x; L.router_w = d->router_w; L.mask = d->mask; L.norm_w = d->norm_w; L.norm_eps = d->norm_eps;
+        L.H = H; L.F = F; L.E = E; L.n_used = (int) K; L.T = (int) T;
+        L.own_lo = d->expert_lo; L.own_n = NL;
+        L.gate = &d->gate; L.up = &d->up; L.down = &d->down;
+        if (p.sh.F) { L.sh_gate = &d->shexp_gate; L.sh_up = &d->shexp_up; L.sh_down = &d->shexp_down; }
+        L.sh_gate_inp = d->shexp_gate_inp;
+        L.residual = d->residual; L.out = d->out;
+        L.sel = sel; L.wts = wts; L.slots = (int32_t *) (w + p.off_slots);
+        L.sh_scale = (float *) (w + p.off_shs); L.act = act; L.xq = xq;
+        L.st = st;
+        return run_pairs_layer(L, s) == cudaSuccess ? QWB_OK : QWB_ERR_CUDA;
+    }
     // routing of all T tokens (the same on every GPU) and their quantized rows
     if (T <= kMaxRouterT) {
         RouterArgs r{};
@@ -156,6 +190,13 @@ extern "C" QWB_API qwb_status qwb_moe_ep_layer(const qwb_moe_ep_layer_desc *d, v
         if (e == cudaSuccess) e = launch_quantize_rows(p.kq_gu ? 0 : 1, xin, H, T, H, nullptr, xq, nullptr, s);
     }
     if (e != cudaSuccess) return QWB_ERR_CUDA;
+    float *sh_out = nullptr, *sh_scale = nullptr;
+    if (p.sh.F) {
+        sh_out = shexp_out_at(p.sh, H, T, w + p.off_sh);
+        sh_scale = d->shexp_gate_inp ? (float *) (w + p.off_shs) : nullptr;
+        e = shexp_run(p.sh, xq, d->x, d->norm_w, d->norm_eps, H, T, w + p.off_sh, sh_out, sh_scale, st, s);
+        if (e != cudaSuccess) return QWB_ERR_CUDA;
+    }
     // the pairs routed to this GPU's experts
     local_ids_kernel<<<(unsigned) ceil_div(P, 256), 256, 0, s>>>(sel, P, d->expert_lo, NL, E, lid, st);
     e = cudaGetLastError();
@@ -196,8 +237,8 @@ extern "C" QWB_API qwb_status qwb_moe_ep_layer(const qwb_moe_ep_layer_desc *d, v
         if (e != cudaSuccess) return QWB_ERR_CUDA;
         profile_mark(s, QWB_KERNEL_DOWN);
     }
-    weighted_sum_local_kernel<<<(unsigned) ceil_div(H * T, 256), 256, 0, s>>>(ex, wts, lid, d->residual, d->out, H,
-                                                                             (int) K, T);
+    weighted_sum_local_kernel<<<(unsigned) ceil_div(H * T, 256), 256, 0, s>>>(ex, wts, lid, sh_out, sh_scale,
+                                                                             d->residual, d->out, H, (int) K, T);
     e = cudaGetLastError();
     profile_mark(s, QWB_KERNEL_OTHER);
     return e == cudaSuccess ? QWB_OK : QWB_ERR_CUDA;

@@ -19,6 +19,7 @@
 #include "dot.cuh"
 #include "kernels.cuh"
 #include "mmid.cuh"
+#include "moe.cuh"
 #include "quant_dev.cuh"
 #include "route.cuh"
 
@@ -36,6 +37,7 @@ struct DownArgs {
     int64_t F, H;
     float *out;
     const float *residual;
+    const float *sh, *sh_scale;  // shared expert output [H] and its factor, or null
     int kq;
     int R, n_rb, wspan, act_stride, act_d_off, act_b_off, smem_act;
     qwb_status_block *st;
@@ -133,6 +135,7 @@ __global__ void __launch_bounds__(128) moe_down_decode_kernel(const DownArgs d) 
             acc = warp_sum(acc);
             if (lane == 0) {
                 const int64_t h = r0 + r;
+                if (d.sh) acc = __fadd_rn(acc, d.sh_scale ? __fmul_rn(d.sh[h], d.sh_scale[0]) : d.sh[h]);
                 d.out[h] = d.residual ? acc + d.residual[h] : acc;
             }
         }
@@ -182,13 +185,113 @@ static cudaError_t launch_down(int type, DownArgs d, cudaStream_t s) {
     }
 }
 
+// ------------------------------------------------------------ shared expert
+qwb_status shexp_check(const qwb_tensor &g, const qwb_tensor &u, const qwb_tensor &d, const float *gate_inp, int tg,
+                       int td, int64_t H, Shexp &sh) {
+    sh = Shexp{&g, &u, &d, gate_inp, 0};
+    if (!d.data) return QWB_OK;
+    if (!g.data || !u.data) return QWB_ERR_INVALID_ARG;
+    if (g.type != tg || u.type != tg || d.type != td) return QWB_ERR_UNSUPPORTED_TYPE;
+    const int64_t F = g.ne[1];
+    if (F <= 0 || F % 256 || g.ne[0] != H || u.ne[0] != H || u.ne[1] != F || d.ne[0] != F || d.ne[1] != H)
+        return QWB_ERR_SHAPE;
+    for (const qwb_tensor *t : {&g, &u, &d}) {
+        if (t->ne[2] != 1 || t->ne[3] != 1) return QWB_ERR_SHAPE;
+        if (t->nb[0] != row_bytes(t->type, block_elems(t->type)) || t->nb[1] != row_bytes(t->type, t->ne[0]))
+            return QWB_ERR_LAYOUT;
+        if ((uintptr_t) t->data % 16) return QWB_ERR_ALIGNMENT;
+    }
+    if ((uintptr_t) gate_inp % 16) return QWB_ERR_ALIGNMENT;
+    sh.F = F;
+    return QWB_OK;
+}
+
+namespace {
+struct ShexpPlan {
+    bool stream;
+    int NT;
+    size_t off_ids, off_index, off_act, off_actq, off_out, total;
+};
+ShexpPlan shexp_plan(const Shexp &sh, int64_t H, int64_t T) {
+    ShexpPlan q{};
+    const int tg = sh.gate->type, td = sh.down->type;
+    q.stream = stream_fits_ffn(tg, H, sh.gate->nb[1], sh.up->nb[1], td, sh.F, sh.down->nb[1]);
+    q.NT = q.stream ? (int) std::max<int64_t>(1, T) : pick_nt(std::max<int64_t>(1, T), 1);
+    size_t o = 0;
+    q.off_ids = o; o += align_up((size_t) T * 4, 256);
+    q.off_index = o; o += mmid_index_bytes(std::max<int64_t>(T, 1), 1, q.NT);
+    q.off_act = o; o += align_up((size_t) T * sh.F * 4, 256);
+    q.off_actq = o; o += planes_bytes(T, sh.F, td != QWB_TYPE_Q8_0);
+    q.off_out = o; o += align_up((size_t) T * H * 4, 256);
+    q.total = o;
+    return q;
+}
+}  // namespace
+
+size_t shexp_bytes(const Shexp &sh, int64_t H, int64_t T) { return sh.F ? shexp_plan(sh, H, T).total : 0; }
+float *shexp_out_at(const Shexp &sh, int64_t H, int64_t T, void *ws) {
+    return (float *) ((char *) ws + shexp_plan(sh, H, T).off_out);
+}
+
+cudaError_t shexp_run(const Shexp &sh, const Q8Planes &xq, const float *x, const float *norm_w, float eps, int64_t H,
+                      int64_t T, void *ws, float *sh_out, float *sh_scale, qwb_status_block *st, cudaStream_t s) {
+    const ShexpPlan q = shexp_plan(sh, H, T);
+    char *w = (char *) ws;
+    const int tg = sh.gate->type, td = sh.down->type;
+    // every token selects the one shared expert
+    int32_t *ids = (int32_t *) (w + q.off_ids);
+    cudaError_t e = cudaMemsetAsync(ids, 0, (size_t) T * 4, s);
+    MmidIndex ix = mmid_index_at(w + q.off_index, std::max<int64_t>(T, 1), 1, q.NT);
+    if (e == cudaSuccess) e = launch_index(ids, 1, 1, 1, (int) T, 1, q.NT, ix, nullptr, 0, 0, 0, st, s);
+    if (e != cudaSuccess) return e;
+    float *act = (float *) (w + q.off_act);
+    {
+        GemvArgs a{};
+        a.W = (const uint8_t *) sh.gate->data; a.nb1 = sh.gate->nb[1]; a.nb2 = sh.gate->nb[1] * (size_t) sh.F;
+        a.W2 = (const uint8_t *) sh.up->data; a.nb1_2 = sh.up->nb[1]; a.nb2_2 = sh.up->nb[1] * (size_t) sh.F;
+        a.row_bytes = row_bytes(tg, H);
+        a.M = sh.F; a.K = H;
+        a.act = xq;
+        a.tiles = ix.tiles; a.n_tiles = ix.n_tiles; a.pairs = ix.pairs;
+        a.n_used = 1; a.n_b = 1;
+        a.dst = act; a.dnb1 = (size_t) sh.F * 4; a.dnb2 = (size_t) sh.F * 4;
+        a.n_ids = 1; a.n_slots = 1;
+        a.st = st;
+        e = launch_expert_gemv(tg, true, a, q.stream, q.NT, ix.max_tiles, T, 1, ix.work, s);
+        if (e != cudaSuccess) return e;
+    }
+    const bool kq_d = td != QWB_TYPE_Q8_0;
+    Q8Planes aq = planes_at(w + q.off_actq, T, sh.F, kq_d);
+    e = launch_quantize_rows(kq_d ? 0 : 1, act, sh.F, T, sh.F, nullptr, aq, nullptr, s);
+    if (e != cudaSuccess) return e;
+    {
+        GemvArgs a{};
+        a.W = (const uint8_t *) sh.down->data; a.nb1 = sh.down->nb[1]; a.nb2 = sh.down->nb[1] * (size_t) H;
+        a.row_bytes = row_bytes(td, sh.F);
+        a.M = H; a.K = sh.F;
+        a.act = aq;
+        a.tiles = ix.tiles; a.n_tiles = ix.n_tiles; a.pairs = ix.pairs;
+        a.n_used = 1; a.n_b = 1;
+        a.dst = sh_out; a.dnb1 = (size_t) H * 4; a.dnb2 = (size_t) H * 4;
+        a.n_ids = 1; a.n_slots = 1;
+        a.st = st;
+        e = launch_expert_gemv(td, false, a, q.stream, q.NT, ix.max_tiles, T, 1, ix.work + 1, s);
+        if (e != cudaSuccess) return e;
+    }
+    if (sh.gate_inp) e = launch_shexp_gate(x, norm_w, eps, sh.gate_inp, T, H, sh_scale, s);
+    return e;
+}
+
 // ------------------------------------------------------------ workspace plan
 struct FfnPlan {
     bool kq_gu, kq_d;
     int NT;
     bool stream;  // batched expert GEMVs on the streaming kernel (index: one tile per expert)
+    bool pairs;   // decode batches / shared expert on the pair kernels (decode.cu)
+    Shexp sh;
     int64_t P;
-    size_t off_logits, off_sel, off_w, off_slots, off_xq, off_index, off_act, off_xn, off_actq, off_experts, total;
+    size_t off_logits, off_sel, off_w, off_slots, off_xq, off_index, off_act, off_xn, off_actq, off_experts;
+    size_t off_shs, off_sh, total;
 };
 
 static qwb_status plan_ffn(const qwb_moe_ffn_desc *d, FfnPlan &p) {
@@ -204,9 +307,20 @@ static qwb_status plan_ffn(const qwb_moe_ffn_desc *d, FfnPlan &p) {
         d->up.ne[2] != n_mat || d->down.ne[0] != d->F || d->down.ne[1] != d->H || d->down.ne[2] != n_mat)
         return QWB_ERR_SHAPE;
     if (!d->g2s && n_mat != d->E) return QWB_ERR_SHAPE;
+    qwb_status rc = shexp_check(d->shexp_gate, d->shexp_up, d->shexp_down, d->shexp_gate_inp, tg, td, d->H, p.sh);
+    if (rc != QWB_OK) return rc;
     p.kq_gu = tg != QWB_TYPE_Q8_0;
     p.kq_d = td != QWB_TYPE_Q8_0;
     p.P = d->n_used * d->T;
+    // the pair kernels: batch-1 decode with a shared expert of the routed experts' size
+    // (without one it keeps the kernels tuned for it) and decode batches of up to 16
+    // (token, expert) pairs; they read an expert's rows once per pair, so larger batches
+    // take the streaming kernels, which read each selected expert once for all its
+    // tokens.  The act output is in pair order there, so not when act is requested.
+    p.pairs = !d->act && ((d->T == 1 && p.sh.F) || (d->T > 1 && d->T * d->n_used <= kPairsDirect)) &&
+              (!p.sh.F || p.sh.F == d->F) &&
+              pairs_supported(tg, td, d->H, d->F, d->E, (int) d->n_used, (int) d->T, row_bytes(tg, d->H),
+                              d->gate.nb[1], d->up.nb[1], row_bytes(td, d->F), d->down.nb[1]);
     // batched (T > 1): the streaming kernel when it fits, with one index tile per expert
     p.stream = d->T > 1 && stream_fits_ffn(tg, d->H, d->gate.nb[1], d->up.nb[1], td, d->F, d->down.nb[1]);
     p.NT = p.stream ? (int) std::max<int64_t>(1, p.P) : pick_nt(p.P, d->E);
@@ -214,10 +328,13 @@ static qwb_status plan_ffn(const qwb_moe_ffn_desc *d, FfnPlan &p) {
     p.off_logits = o; o += align_up((size_t) (d->T * d->E) * 4, 256);
     p.off_sel = o; o += align_up((size_t) p.P * 4, 256);
     p.off_w = o; o += align_up((size_t) p.P * 4, 256);
-    p.off_slots = o; o += align_up((size_t) 3 * d->n_used * 4, 256);
+    p.off_slots = o; o += align_up((size_t) 3 * p.P * 4, 256);
     p.off_xq = o; o += planes_bytes(d->T, d->H, p.kq_gu);
     p.off_index = o; o += mmid_index_bytes(std::max<int64_t>(p.P, 1), d->E, p.NT);
-    p.off_act = o; o += align_up((size_t) p.P * d->F * 4, 256);
+    p.off_act = o; o += align_up((size_t) (p.P + (p.pairs && p.sh.F ? d->T : 0)) * d->F * 4, 256);
+    p.off_shs = o; o += align_up((size_t) d->T * 4, 256);
+    p.off_sh = o;
+    if (p.sh.F && !p.pairs) o += shexp_bytes(p.sh, d->H, d->T);
     p.off_xn = o;
     if (d->norm_w && d->T > kMaxRouterT) o += align_up((size_t) d->T * d->H * 4, 256);
     p.off_actq = o;
@@ -274,7 +391,21 @@ extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, s
 
     const bool decode = T == 1;
     profile_mark(s, 0);
-    if (decode && E <= kMaxRouteE && E >= kRouterCluster && (E % kRouterCluster) == 0 && K <= 32 &&
+    if (p.pairs) {
+        PairsLayer L{};
+        L.x = d->x; L.router_w = d->router_w; L.mask = d->mask; L.norm_w = d->norm_w; L.norm_eps = d->norm_eps;
+        L.H = H; L.F = F; L.E = E; L.n_used = (int) K; L.T = (int) T;
+        L.g2s = d->g2s;
+        L.gate = &d->gate; L.up = &d->up; L.down = &d->down;
+        if (p.sh.F) { L.sh_gate = &d->shexp_gate; L.sh_up = &d->shexp_up; L.sh_down = &d->shexp_down; }
+        L.sh_gate_inp = d->shexp_gate_inp;
+        L.residual = d->residual; L.out = d->out;
+        L.sel = sel; L.wts = wts; L.slots = (int32_t *) (w + p.off_slots);
+        L.sh_scale = (float *) (w + p.off_shs); L.act = act; L.xq = xq;
+        L.st = st;
+        return run_pairs_layer(L, s) == cudaSuccess ? QWB_OK : QWB_ERR_CUDA;
+    }
+    if (decode && !p.sh.F && E <= kMaxRouteE && E >= kRouterCluster && (E % kRouterCluster) == 0 && K <= 32 &&
         gateup_decode_supported(d->gate.type, H, row_bytes(d->gate.type, H), d->gate.nb[1], F, (int) K) &&
         d->up.nb[1] == d->gate.nb[1] &&
         down_decode_supported(d->down.type, F, H, row_bytes(d->down.type, F), d->down.nb[1], (int) K)) {
@@ -282,7 +413,7 @@ extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, s
         int32_t *slots = (int32_t *) (w + p.off_slots);
         RouterDecodeArgs r{};
         r.x = d->x; r.router_w = d->router_w; r.mask = d->mask; r.norm_w = d->norm_w; r.norm_eps = d->norm_eps;
-        r.H = H; r.E = E; r.n_used = (int) K;
+        r.H = H; r.E = E; r.n_used = (int) K; r.T = 1;
         r.g2s = d->g2s;
         r.n_slots[0] = d->gate.ne[2]; r.n_slots[1] = d->up.ne[2]; r.n_slots[2] = d->down.ne[2];
         r.sel = sel; r.wts = wts; r.slots = slots;
@@ -334,6 +465,14 @@ extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, s
     }
     if (e != cudaSuccess) return QWB_ERR_CUDA;
     profile_mark(s, QWB_KERNEL_ROUTER);
+    // the shared expert (its own GEMVs; the routed experts' reduction adds it)
+    float *sh_out = nullptr, *sh_scale = nullptr;
+    if (p.sh.F) {
+        sh_out = shexp_out_at(p.sh, H, T, w + p.off_sh);
+        sh_scale = d->shexp_gate_inp ? (float *) (w + p.off_shs) : nullptr;
+        e = shexp_run(p.sh, xq, d->x, d->norm_w, d->norm_eps, H, T, w + p.off_sh, sh_out, sh_scale, st, s);
+        if (e != cudaSuccess) return QWB_ERR_CUDA;
+    }
     if (!decode) {
         e = launch_index(sel, 1, K, (int) K, (int) T, (int) E, p.NT, ix, nullptr, 0, 0, 0, st, s);
         if (e != cudaSuccess) return QWB_ERR_CUDA;
@@ -365,6 +504,7 @@ extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, s
         dn.remap = g2s_d; dn.selected = sel; dn.weights = wts; dn.n_used = (int) K;
         dn.act = act; dn.F = F; dn.H = H;
         dn.out = d->out; dn.residual = d->residual;
+        dn.sh = sh_out; dn.sh_scale = sh_scale;
         dn.st = st;
         e = launch_down(d->down.type, dn, s);
         if (e != cudaSuccess) return QWB_ERR_CUDA;
@@ -391,7 +531,7 @@ extern "C" QWB_API qwb_status qwb_moe_ffn(const qwb_moe_ffn_desc *d, void *ws, s
         if (e != cudaSuccess) return QWB_ERR_CUDA;
         profile_mark(s, QWB_KERNEL_DOWN);
     }
-    e = launch_weighted_sum(experts, wts, d->residual, d->out, H, K, T, s);
+    e = launch_weighted_sum(experts, wts, d->residual, d->out, H, K, T, s, sh_out, sh_scale);
     if (e != cudaSuccess) return QWB_ERR_CUDA;
     profile_mark(s, QWB_KERNEL_OTHER);
     return QWB_OK;

@@ -336,8 +336,11 @@ __global__ void swiglu_kernel(const float *__restrict__ g, const float *__restri
 }
 
 // ------------------------------------------------- weighted expert reduction
-// out[t][h] = sum_j w[t][j] * ex[t][j][h] (+ res[t][h]), j ascending
+// out[t][h] = sum_j w[t][j] * ex[t][j][h], j ascending, then + sh[t][h] (* sh_scale[t]),
+// then + res[t][h] (the order of the reference graph: the routed sum, the shared expert's
+// ggml_add, the layer's residual add)
 __global__ void weighted_sum_kernel(const float *__restrict__ ex, const float *__restrict__ w,
+                                    const float *__restrict__ sh, const float *__restrict__ sh_scale,
                                     const float *__restrict__ res, float *__restrict__ out, int64_t H, int n_used,
                                     int64_t T) {
     const int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
@@ -347,15 +350,59 @@ __global__ void weighted_sum_kernel(const float *__restrict__ ex, const float *_
     const float *wt = w + t * n_used;
     float acc = 0.f;
     for (int j = 0; j < n_used; ++j) acc = fmaf(wt[j], e[(int64_t) j * H], acc);
+    if (sh) acc = __fadd_rn(acc, sh_scale ? __fmul_rn(sh[i], sh_scale[t]) : sh[i]);
     if (res) acc += res[i];
     out[i] = acc;
 }
 
 cudaError_t launch_weighted_sum(const float *ex, const float *w, const float *res, float *out, int64_t H,
-                                int64_t n_used, int64_t T, cudaStream_t s) {
+                                int64_t n_used, int64_t T, cudaStream_t s, const float *sh, const float *sh_scale) {
     const int64_t n = H * T;
     if (n == 0) return cudaSuccess;
-    weighted_sum_kernel<<<(unsigned) ceil_div(n, 256), 256, 0, s>>>(ex, w, res, out, H, (int) n_used, T);
+    weighted_sum_kernel<<<(unsigned) ceil_div(n, 256), 256, 0, s>>>(ex, w, sh, sh_scale, res, out, H, (int) n_used, T);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------- shared-expert gate
+// scale[t] = sigmoid(gw . ffn_in[t]), ffn_in = rms_norm(x) * norm_w (or x): the
+// ffn_gate_inp_shexp factor of core/runtime.cpp:2831-2832 (ggml_sigmoid_f32:
+// 1 / (1 + exp(-v))).  One CTA (128 threads) per token; the normalisation is
+// rmsnorm_kernel's.
+__global__ void __launch_bounds__(128) shexp_gate_kernel(const float *__restrict__ x, const float *__restrict__ nw,
+                                                         float eps, const float *__restrict__ gw, int64_t H,
+                                                         float *__restrict__ scale) {
+    __shared__ double dpart[4];
+    __shared__ float fpart[4];
+    __shared__ float s_sc;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float *xr = x + (int64_t) blockIdx.x * H;
+    if (nw) {
+        const int64_t q = H / 4;
+        const double v = warp_sumsq(xr + warp * q, q, lane);
+        if (lane == 0) dpart[warp] = v;
+        __syncthreads();
+        if (threadIdx.x == 0) s_sc = rms_scale(((dpart[0] + dpart[1]) + dpart[2]) + dpart[3], H, eps);
+        __syncthreads();
+    }
+    const float sc = nw ? s_sc : 1.f;
+    float acc = 0.f;
+    for (int64_t h = threadIdx.x; h < H; h += blockDim.x) {
+        const float xi = nw ? __fmul_rn(__fmul_rn(xr[h], sc), nw[h]) : xr[h];
+        acc = fmaf(gw[h], xi, acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) fpart[warp] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const float v = ((fpart[0] + fpart[1]) + fpart[2]) + fpart[3];
+        scale[blockIdx.x] = 1.f / (1.f + expf(-v));
+    }
+}
+
+cudaError_t launch_shexp_gate(const float *x, const float *norm_w, float eps, const float *gw, int64_t T, int64_t H,
+                              float *scale, cudaStream_t s) {
+    if (T == 0) return cudaSuccess;
+    shexp_gate_kernel<<<(unsigned) T, 128, 0, s>>>(x, norm_w, eps, gw, H, scale);
     return cudaGetLastError();
 }
 

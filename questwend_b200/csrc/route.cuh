@@ -34,7 +34,12 @@ cudaError_t launch_logits_gemm(const float *x, const float *w, float *out, int64
                                cudaStream_t s);
 // y[t] = rms_norm(x[t]) * w  (ggml-cpu/ops.cpp:4107-4162, fused RMS_NORM + MUL)
 cudaError_t launch_rmsnorm(const float *x, const float *w, float eps, int64_t T, int64_t H, float *y, cudaStream_t s);
+// out = sum_j w_j ex_j (+ sh * sh_scale, the shared expert) (+ res)
 cudaError_t launch_weighted_sum(const float *ex, const float *w, const float *res, float *out, int64_t H,
-                                int64_t n_used, int64_t T, cudaStream_t s);
+                                int64_t n_used, int64_t T, cudaStream_t s, const float *sh = nullptr,
+                                const float *sh_scale = nullptr);
+// scale[t] = sigmoid(gw . (rms_norm(x[t]) * norm_w)) (norm_w null: gw . x[t])
+cudaError_t launch_shexp_gate(const float *x, const float *norm_w, float eps, const float *gw, int64_t T, int64_t H,
+                              float *scale, cudaStream_t s);
 
 }  // namespace qwb

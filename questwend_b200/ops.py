@@ -243,9 +243,18 @@ def moe_weighted_sum(experts: torch.Tensor, weights: torch.Tensor) -> torch.Tens
     return out
 
 
+def _set_shexp(d, shexp):
+    """shexp: None or (gate QTensor [H, F_sh], up QTensor, down QTensor [F_sh, H], gate_inp (H,) f32 or None)."""
+    if shexp is None:
+        return
+    g, u, dn, gi = shexp
+    d.shexp_gate, d.shexp_up, d.shexp_down = g.desc(), u.desc(), dn.desc()
+    d.shexp_gate_inp = gi.data_ptr() if gi is not None else None
+
+
 def moe_ffn_desc(x, router_w, gate: QTensor, up: QTensor, down: QTensor, n_used: int, out,
                  g2s=None, mask=None, residual=None, selected=None, weights=None, act=None,
-                 norm_w=None, norm_eps: float = 1e-6) -> L.MoeFfnDesc:
+                 norm_w=None, norm_eps: float = 1e-6, shexp=None) -> L.MoeFfnDesc:
     T, H = x.shape
     d = L.MoeFfnDesc()
     d.x = x.data_ptr()
@@ -261,22 +270,27 @@ def moe_ffn_desc(x, router_w, gate: QTensor, up: QTensor, down: QTensor, n_used:
     d.act = act.data_ptr() if act is not None else None
     d.norm_w = norm_w.data_ptr() if norm_w is not None else None
     d.norm_eps = norm_eps
+    _set_shexp(d, shexp)
     return d
 
 
 def moe_ffn(x, router_w, gate: QTensor, up: QTensor, down: QTensor, n_used: int,
-            g2s=None, mask=None, residual=None, out=None, act=None, norm_w=None, norm_eps: float = 1e-6):
+            g2s=None, mask=None, residual=None, out=None, act=None, norm_w=None, norm_eps: float = 1e-6,
+            shexp=None):
     """One MoE FFN layer (build_moe).  x (T, H) f32, router_w (E, H) f32, gate/up ggml
     [H, F, n_mat], down [F, H, n_mat]; g2s (3, E) int32 expert->slot tables (gate, up,
     down) or None; act: optional (T, n_used, F) f32 tensor receiving swiglu(gate, up);
-    norm_w: optional ffn_norm weight (H,): the layer then runs on rms_norm(x) * norm_w.
+    norm_w: optional ffn_norm weight (H,): the layer then runs on rms_norm(x) * norm_w;
+    shexp: optional shared expert (gate [H, F_sh], up, down [F_sh, H] QTensors, gate_inp
+    (H,) f32 or None), added to the routed experts' sum (core/runtime.cpp:2825-2833).
     Returns (out (T, H), selected (T, n_used), weights (T, n_used))."""
     T, H = x.shape
     if out is None:
         out = torch.empty((T, H), dtype=torch.float32, device=x.device)
     sel = torch.empty((T, n_used), dtype=torch.int32, device=x.device)
     w = torch.empty((T, n_used), dtype=torch.float32, device=x.device)
-    d = moe_ffn_desc(x, router_w, gate, up, down, n_used, out, g2s, mask, residual, sel, w, act, norm_w, norm_eps)
+    d = moe_ffn_desc(x, router_w, gate, up, down, n_used, out, g2s, mask, residual, sel, w, act, norm_w, norm_eps,
+                     shexp)
     lib = L.lib()
     need = lib.qwb_moe_ffn_workspace_size(C.byref(d))
     if need == 0:
@@ -290,7 +304,7 @@ def moe_ffn(x, router_w, gate: QTensor, up: QTensor, down: QTensor, n_used: int,
 # ------------------------------------------------------------------ expert parallelism
 def moe_ep_layer_desc(x, router_w, gate: QTensor, up: QTensor, down: QTensor, expert_lo: int, n_used: int, out,
                       residual=None, selected=None, weights=None, norm_w=None, norm_eps: float = 1e-6,
-                      mask=None) -> L.MoeEpLayerDesc:
+                      mask=None, shexp=None) -> L.MoeEpLayerDesc:
     T, H = x.shape
     d = L.MoeEpLayerDesc()
     d.x, d.router_w = x.data_ptr(), router_w.data_ptr()
@@ -304,24 +318,26 @@ def moe_ep_layer_desc(x, router_w, gate: QTensor, up: QTensor, down: QTensor, ex
     d.out = out.data_ptr()
     d.selected = selected.data_ptr() if selected is not None else None
     d.weights = weights.data_ptr() if weights is not None else None
+    _set_shexp(d, shexp)
     return d
 
 
 def moe_ep_layer(x, router_w, gate: QTensor, up: QTensor, down: QTensor, expert_lo: int, n_used: int,
-                 residual=None, norm_w=None, norm_eps: float = 1e-6, mask=None, out=None):
+                 residual=None, norm_w=None, norm_eps: float = 1e-6, mask=None, out=None, shexp=None):
     """One GPU's share of an expert-parallel MoE layer.  x (T, H) f32: all tokens' rows (the
     same on every GPU); gate/up [H, F, n_local], down [F, H, n_local]: global experts
     [expert_lo, expert_lo + n_local).  Routes all tokens (replicated router) and returns
     (out (T, H), selected (T, n_used), weights (T, n_used)): out[t] = the weighted sum of
-    this GPU's experts' outputs for token t (+ residual[t] when given).  Summing out over
-    the GPUs (all-reduce) gives the layer's output."""
+    this GPU's experts' outputs for token t (+ the shared expert `shexp`, as in moe_ffn,
+    when given) (+ residual[t] when given).  Summing out over the GPUs (all-reduce) gives
+    the layer's output: pass residual and shexp to one GPU only."""
     T, H = x.shape
     if out is None:
         out = torch.empty((T, H), dtype=torch.float32, device=x.device)
     sel = torch.empty((T, n_used), dtype=torch.int32, device=x.device)
     w = torch.empty((T, n_used), dtype=torch.float32, device=x.device)
     d = moe_ep_layer_desc(x, router_w, gate, up, down, expert_lo, n_used, out, residual, sel, w, norm_w, norm_eps,
-                          mask)
+                          mask, shexp)
     lib = L.lib()
     need = lib.qwb_moe_ep_layer_workspace_size(C.byref(d))
     if need == 0:

@@ -102,3 +102,18 @@ def test_noalloc_limit_without_gpu(lib):
     a_bad = _t(0x100000, 2, (K, M, n_as, 1), (18, rs, rs * M, rs * M * n_as))
     assert lib.qwb_mul_mat_id_noalloc(C.byref(a_bad), C.byref(b), C.byref(ids), C.byref(dst), None,
                                       None) == UNSUPPORTED
+
+
+def test_ep_comm_argument_checks(lib):
+    # refused before any CUDA call
+    assert lib.qwb_ep_comm_handle_size() > 0
+    h = (C.c_char * lib.qwb_ep_comm_handle_size())()
+    p = C.c_void_p()
+    assert lib.qwb_ep_comm_create(2, 2, 1 << 20, C.byref(p), h) == INVALID   # rank outside the world
+    assert lib.qwb_ep_comm_create(0, 0, 1 << 20, C.byref(p), h) == INVALID
+    assert lib.qwb_ep_comm_create(2, 0, 0, C.byref(p), h) == INVALID        # no message size
+    assert lib.qwb_ep_comm_create(16, 0, 1 << 20, C.byref(p), h) == LIMIT   # more GPUs than one node's 8
+    assert lib.qwb_ep_comm_create(2, 0, 1 << 20, None, h) == INVALID
+    assert lib.qwb_ep_comm_connect(None, h) == INVALID
+    assert lib.qwb_ep_allreduce_f32(None, 0x1000, 0x1000, 16, None, None) == INVALID
+    lib.qwb_ep_comm_destroy(None)  # no-op

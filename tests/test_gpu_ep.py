@@ -139,3 +139,36 @@ def test_unselected_shard_gives_zeros_and_no_error(qwb):
                                       _shard(qwb, U, O.Q4_K, H, F, 16, 16), _shard(qwb, Dn, O.Q6_K, F, H, 16, 16),
                                       16, K, residual=x, norm_w=cu(norm_w), mask=mask)
     assert torch.equal(part, x)
+
+
+@pytest.mark.parametrize("T,world", [(1, 2), (8, 4), (24, 2)])
+def test_shared_expert_on_one_shard(qwb, T, world):
+    # the shared expert given to rank 0 only (with the residual): the shards' sum equals
+    # the fused layer with the shared expert (pair kernels up to 8 tokens, GEMVs beyond)
+    from questwend_b200.expert_parallel import shard_range
+    H, F, E, K = 2048, 768, 32, 8
+    router_w, norm_w, gate, up, down = _layer(O.Q4_K, O.Q6_K, H, F, E, seed=120 + T)
+    r = D.rng(121)
+    sh_np = (D.weights(O.Q4_K, 1, F, H, seed=122), D.weights(O.Q4_K, 1, F, H, seed=123),
+             D.weights(O.Q6_K, 1, H, F, seed=124))
+    gi = cu((r.standard_normal(H, dtype=np.float32) * 0.05).astype(np.float32))
+    sh = (qwb.QTensor.from_bytes(sh_np[0], O.Q4_K, (H, F)), qwb.QTensor.from_bytes(sh_np[1], O.Q4_K, (H, F)),
+          qwb.QTensor.from_bytes(sh_np[2], O.Q6_K, (F, H)), gi)
+    x = D.acts((T, H), seed=125 + T)
+    G = qwb.QTensor.from_bytes(gate, O.Q4_K, (H, F, E))
+    U = qwb.QTensor.from_bytes(up, O.Q4_K, (H, F, E))
+    Dn = qwb.QTensor.from_bytes(down, O.Q6_K, (F, H, E))
+    xc, rw, nw = cu(x), cu(router_w), cu(norm_w)
+    fused, _, _ = qwb.moe_ffn(xc, rw, G, U, Dn, K, residual=xc, norm_w=nw, shexp=sh)
+    fused = fused.clone()
+    total = torch.zeros((T, H), device="cuda")
+    for rk in range(world):
+        lo, n = shard_range(E, world, rk)
+        part, _, _ = qwb.ops.moe_ep_layer(xc, rw, _shard(qwb, G, O.Q4_K, H, F, lo, n),
+                                          _shard(qwb, U, O.Q4_K, H, F, lo, n), _shard(qwb, Dn, O.Q6_K, F, H, lo, n),
+                                          lo, K, residual=xc if rk == 0 else None, norm_w=nw,
+                                          shexp=sh if rk == 0 else None)
+        total += part
+    assert qwb.read_status()[0] == 0
+    e = O.nrmse(total.cpu().numpy(), fused.cpu().numpy())
+    assert e <= 1e-5, (e, O.max_abs_rel(total.cpu().numpy(), fused.cpu().numpy()))
