@@ -69,8 +69,8 @@ import numpy as np  # noqa: E402
 
 H, F, E, K_USED, LAYERS = 2048, 768, 128, 8, 48
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate/up decode launch, from an ncu
-# capture of this kernel at these shapes (48-layer stack, one token)
-GATEUP_TRAFFIC_BYTES = 14_179_840
+# capture of this kernel at these shapes (one token, 4-layer stack: the same launch shape)
+GATEUP_TRAFFIC_BYTES = 14_179_584
 Q4_K, Q6_K = 12, 14
 ROW_GU = H // 256 * 144        # bytes per gate/up row
 ROW_D = F // 256 * 210         # bytes per down row
@@ -597,8 +597,9 @@ def slab_sweep(q, dev, iters=20):
             "audit_compare_ms": audit_ms[0], "audit_checksums_ms": audit_ms[1], "audit_equal": True}
 
 
-def prefill_sweep(q, lib, dev, warmup, iters, cpu=None):
-    """cpu: the --cpu-leg JSON (reference CPU timings), or None."""
+def prefill_sweep(q, lib, dev, warmup, iters, cpu=None, tokens=PF_TOKENS, parts=("q4k", "q8_0", "q6k")):
+    """cpu: the --cpu-leg JSON (reference CPU timings), or None.  tokens / parts: a subset
+    of the sweep (profiling runs); the headline keys need the full Q4_K sweep."""
     import ctypes as C
 
     import torch
@@ -616,7 +617,7 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu=None):
     gen = torch.Generator(device=dev)
     gen.manual_seed(99)
     points = []
-    for T in PF_TOKENS:
+    for T in (tokens if "q4k" in parts else ()):
         ids = torch.from_numpy(zipf_ids(T, E, K_USED, seed=T)).to(dev)
         for name, (W, k, rows) in zip(("gate_up", "down"), pools):
             nb = 1 if name == "gate_up" else K_USED
@@ -653,7 +654,7 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu=None):
     q8buf = torch.empty(q8base.numel() * reps, dtype=torch.uint8, device=dev)
     q8buf.view(reps, -1).copy_(q8base.expand(reps, -1))
     W8 = q.QTensor(q8buf, Q8_0, (PF_H, PF_F, E, 1))
-    for T in PF_TOKENS:
+    for T in (tokens if "q8_0" in parts else ()):
         ids = torch.from_numpy(zipf_ids(T, E, K_USED, seed=T)).to(dev)
         b = torch.randn((T, 1, PF_H), generator=gen, device=dev)
         out = torch.empty((T, K_USED, PF_F), device=dev)
@@ -678,7 +679,7 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu=None):
     q6buf = torch.empty(q6base.numel() * reps, dtype=torch.uint8, device=dev)
     q6buf.view(reps, -1).copy_(q6base.expand(reps, -1))
     W6 = q.QTensor(q6buf, Q6_K, (PF_F, PF_H, E, 1))
-    for T in PF_TOKENS:
+    for T in (tokens if "q6k" in parts else ()):
         ids = torch.from_numpy(zipf_ids(T, E, K_USED, seed=T)).to(dev)
         b = torch.randn((T, K_USED, PF_F), generator=gen, device=dev)
         out = torch.empty((T, K_USED, PF_H), device=dev)
@@ -706,6 +707,8 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu=None):
             peak, pkind = json.load(f)["bf16_tflops"], "measured bf16 burst"
     except Exception:
         peak, pkind = 1590.0, "fallback"
+    if "q4k" not in parts or tuple(tokens) != PF_TOKENS:
+        return {"points": points, "int8_points": q8_points}
     top = [p for p in points if p["tokens"] == PF_TOKENS[-1] and p["shape"] == "gate_up"][0]
     res = {"config": {"workload": "C3 prefill grouped GEMM, MUL_MAT_ID Q4_K x Q8_K", "hidden": PF_H,
                       "expert_ffn": PF_F, "experts": E, "top_k": K_USED, "routing": "Zipf(1.1) + Gumbel",
@@ -733,7 +736,7 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu=None):
 
 
 # the 235B-A22B expert-parallel layer: hidden 4096, expert FFN 1536, 128 experts, top-8
-EP4_H, EP4_F, EP4_TOKENS, EP4_LAYERS, EP4_UNIQUE = 4096, 1536, (1, 8, 64), 8, 8
+EP4_H, EP4_F, EP4_TOKENS, EP4_LAYERS, EP4_UNIQUE = 4096, 1536, (1, 8, 64), 24, 8
 
 
 def ep_layers(q, dev, base, shapes, n_layers, n_exp, lo, n, unique):
@@ -1129,6 +1132,10 @@ def main():
     ap.add_argument("--no-slabs", action="store_true", help="skip the expert pool write (slab upload) measurement")
     ap.add_argument("--only-prefill", action="store_true",
                     help="run only the prefill sweep, without its CPU baseline (profiling runs)")
+    ap.add_argument("--pf-tokens", default=",".join(str(t) for t in PF_TOKENS),
+                    help="with --only-prefill: comma-separated token counts")
+    ap.add_argument("--pf-parts", default="q4k,q8_0,q6k",
+                    help="with --only-prefill: comma-separated subset of q4k, q8_0, q6k")
     ap.add_argument("--only-mmid", action="store_true",
                     help="run only the decode-batch MUL_MAT_ID sweep and print its JSON (profiling runs)")
     ap.add_argument("--mmid-tokens", default=",".join(str(t) for t in MMID_TOKENS),
@@ -1177,7 +1184,9 @@ def main():
         print(json.dumps({"decode_mmid": decode_mmid_sweep(q, lib, torch.device("cuda", local), mmid_tokens, args.mmid_pools)}))
         return
     if args.only_prefill:
-        print(json.dumps({"prefill": prefill_sweep(q, lib, torch.device("cuda", local), args.warmup, 10)}))
+        pf_tokens = tuple(int(t) for t in args.pf_tokens.split(","))
+        print(json.dumps({"prefill": prefill_sweep(q, lib, torch.device("cuda", local), args.warmup, 10,
+                                                   tokens=pf_tokens, parts=tuple(args.pf_parts.split(",")))}))
         return
 
     # ---------------------------------------------------------------- weights

@@ -294,17 +294,20 @@ __global__ void __launch_bounds__(kT8Threads, 1) pf_tc8_kernel(const I8PrefillAr
                 lds_words8_a2(sb + 64 * h + 32 * (i & 1), qa);
                 const int8_t *scp = (const int8_t *) (sb + 192) + 8 * h + 2 * i;
                 const int sc0 = scp[0], sc1 = scp[1];  // sub-blocks of l = 0..15 and 16..31
+                uint32_t p1[8], p0[8];
 #pragma unroll
                 for (int m = 0; m < 8; ++m) {
                     const uint32_t nib = i < 2 ? (qa[m] & 0x0f0f0f0fu) : ((qa[m] >> 4) & 0x0f0f0f0fu);
                     const uint32_t q = nib | (((qh[m] >> (2 * i)) & 0x03030303u) << 4);
-                    uint32_t p1, p0;
-                    q6_planes(q, m < 4 ? sc0 : sc1, p1, p0);
-                    // elements l = 4m .. 4m + 3 of sub-lane i: k = 32 i + 4 m within the half
-                    const int kk = 32 * i + 4 * m;
-                    *(uint32_t *) (A + t8_off(r, kk)) = p1;
-                    *(uint32_t *) (A + kT8M * kT8Step + t8_off(r, kk)) = p0;
+                    q6_planes(q, m < 4 ? sc0 : sc1, p1[m], p0[m]);
                 }
+                // elements l = 0..31 of sub-lane i are k = 32 i .. 32 i + 31 within the half:
+                // two 16-byte core-matrix rows per plane (a warp's 32 rows store 512
+                // contiguous bytes per instruction: no bank conflicts)
+                *(uint4 *) (A + t8_off(r, 32 * i)) = make_uint4(p1[0], p1[1], p1[2], p1[3]);
+                *(uint4 *) (A + t8_off(r, 32 * i + 16)) = make_uint4(p1[4], p1[5], p1[6], p1[7]);
+                *(uint4 *) (A + kT8M * kT8Step + t8_off(r, 32 * i)) = make_uint4(p0[0], p0[1], p0[2], p0[3]);
+                *(uint4 *) (A + kT8M * kT8Step + t8_off(r, 32 * i + 16)) = make_uint4(p0[4], p0[5], p0[6], p0[7]);
             }
             if (h == 1) {  // the superblock's scales, once both halves are in
                 ep.dw[r] = h2f(*(const uint16_t *) (sb + 208));
