@@ -144,6 +144,7 @@ def ref():
                                                vp, vp, vp, vp, i64, vp, vp, i32, C.POINTER(C.c_double),
                                                C.POINTER(C.c_uint64)]
         lib.qref_dropin_first_gpu.argtypes = [cp, C.c_char_p, i32]
+        lib.qref_stack_set_shexp.argtypes = [vp, vp, vp, i64, vp]
         _ref = lib
     return _ref
 
@@ -310,6 +311,20 @@ def backend_moe_stack(path, L, H, F, E, n_used, T, type_gu, gate_u, up_u, type_d
                                       type_gu, _p(gate_u), _p(up_u), type_d, _p(down_u), n_unique, _p(rw), _p(nw),
                                       _p(xx), _p(g), n_slots, _p(out), _p(sel), iters, C.byref(ms), st)
     return dict(rc=rc, out=out, selected=sel, ms=ms.value, stats=list(st))
+
+
+_stack_sh_keep = None
+
+
+def stack_set_shexp(gate=None, up=None, down=None, Fs=0, gate_inp=None):
+    """Give every block of backend_moe_stack the shared expert of core/runtime.cpp:2825-2833
+    (byte images gate/up [H, Fs] and down [Fs, H], the same for every layer; gate_inp
+    [L][H] f32 sigmoid gate weights or None); stack_set_shexp() removes it."""
+    global _stack_sh_keep
+    gi = None if gate_inp is None else np.ascontiguousarray(gate_inp, dtype=np.float32)
+    g, u, d = (None if a is None else np.ascontiguousarray(a) for a in (gate, up, down))
+    _stack_sh_keep = (g, u, d, gi)  # the library keeps the pointers
+    ref().qref_stack_set_shexp(_p(g), _p(u), _p(d), Fs, _p(gi))
 
 
 def dropin_first_gpu(directory: str) -> str:

@@ -579,6 +579,24 @@ int qref_backend_sched_mul_mat_id(const char * path, int type, const void * as, 
 // timing): *ms = mean ms per run.  stats (5 values,
 // may be NULL): the QWB backend's counters (fused layers, own nodes, delegated nodes,
 // delegated runs) and whether it delegates, all zero for other backends.
+// Optional shared expert for qref_backend_moe_stack (core/runtime.cpp:2825-2833): one
+// byte image per matrix (the same for every layer; gate/up of the routed gate/up type
+// [H, Fs], down of the routed down type [Fs, H]) and a sigmoid gate weight per layer
+// ([L][H], or null for none).  qref_stack_set_shexp(nullptr, ...) removes it.
+static struct {
+    const void * gate = nullptr, * up = nullptr, * down = nullptr;
+    int64_t Fs = 0;
+    const float * gate_inp = nullptr;
+} g_stack_sh;
+
+void qref_stack_set_shexp(const void * gate, const void * up, const void * down, int64_t Fs, const float * gate_inp) {
+    g_stack_sh.gate = gate;
+    g_stack_sh.up = up;
+    g_stack_sh.down = down;
+    g_stack_sh.Fs = down ? Fs : 0;
+    g_stack_sh.gate_inp = down ? gate_inp : nullptr;
+}
+
 int qref_backend_moe_stack(const char * path, const char * params, int L, int64_t H, int64_t F, int64_t E,
                            int64_t n_used, int64_t T, int type_gu, const void * gate_u, const void * up_u,
                            int type_d, const void * down_u, int64_t n_unique, const float * router_w,
@@ -601,9 +619,15 @@ int qref_backend_moe_stack(const char * path, const char * params, int L, int64_
     const size_t rb_gu = ggml_row_size((ggml_type) type_gu, H), rb_d = ggml_row_size((ggml_type) type_d, F);
     const size_t ex_gu = rb_gu * F, ex_d = rb_d * H;
 
-    ggml_init_params wp = {ggml_tensor_overhead() * (6 * (size_t) L + 4), nullptr, true};
+    ggml_init_params wp = {ggml_tensor_overhead() * (7 * (size_t) L + 8), nullptr, true};
     ggml_context * wctx = ggml_init(wp);
-    std::vector<ggml_tensor *> tg(L), tu(L), td(L), trw(L), tnw(L);
+    std::vector<ggml_tensor *> tg(L), tu(L), td(L), trw(L), tnw(L), tsi(L, nullptr);
+    const bool sh = g_stack_sh.down != nullptr;
+    ggml_tensor * tsg = sh ? ggml_new_tensor_2d(wctx, (ggml_type) type_gu, H, g_stack_sh.Fs) : nullptr;
+    ggml_tensor * tsu = sh ? ggml_new_tensor_2d(wctx, (ggml_type) type_gu, H, g_stack_sh.Fs) : nullptr;
+    ggml_tensor * tsd = sh ? ggml_new_tensor_2d(wctx, (ggml_type) type_d, g_stack_sh.Fs, H) : nullptr;
+    if (sh && g_stack_sh.gate_inp)
+        for (int l = 0; l < L; ++l) tsi[l] = ggml_new_tensor_1d(wctx, GGML_TYPE_F32, H);
     for (int l = 0; l < L; ++l) {
         tg[l] = ggml_new_tensor_3d(wctx, (ggml_type) type_gu, H, F, NE);
         tu[l] = ggml_new_tensor_3d(wctx, (ggml_type) type_gu, H, F, NE);
@@ -638,6 +662,13 @@ int qref_backend_moe_stack(const char * path, const char * params, int L, int64_
             ggml_backend_tensor_set(tnw[l], norm_w + (size_t) l * H, 0, ggml_nbytes(tnw[l]));
         }
         if (cache) ggml_backend_tensor_set(g2s_all, g2s, 0, ggml_nbytes(g2s_all));
+        if (sh) {
+            ggml_backend_tensor_set(tsg, g_stack_sh.gate, 0, ggml_nbytes(tsg));
+            ggml_backend_tensor_set(tsu, g_stack_sh.up, 0, ggml_nbytes(tsu));
+            ggml_backend_tensor_set(tsd, g_stack_sh.down, 0, ggml_nbytes(tsd));
+            for (int l = 0; l < L; ++l)
+                if (tsi[l]) ggml_backend_tensor_set(tsi[l], g_stack_sh.gate_inp + (size_t) l * H, 0, ggml_nbytes(tsi[l]));
+        }
 
         ggml_init_params ip = {ggml_tensor_overhead() * (64 * (size_t) L + 64) + ggml_graph_overhead_custom(8192, false),
                                nullptr, true};
@@ -701,6 +732,14 @@ int qref_backend_moe_stack(const char * path, const char * params, int L, int64_
                     }
                     if (n_used == 1) moe = ggml_cont(ctx, moe);
                 }
+            }
+            if (sh) {
+                // shared expert (runtime.cpp:2825-2833)
+                ggml_tensor * gs = ggml_mul_mat(ctx, tsg, ffn_in);
+                ggml_tensor * us = ggml_mul_mat(ctx, tsu, ffn_in);
+                ggml_tensor * shv = ggml_mul_mat(ctx, tsd, ggml_mul(ctx, ggml_silu(ctx, gs), us));
+                if (tsi[l]) shv = ggml_mul(ctx, shv, ggml_sigmoid(ctx, ggml_mul_mat(ctx, tsi[l], ffn_in)));
+                moe = ggml_add(ctx, moe, shv);
             }
             cur = ggml_add(ctx, moe, cur);
         }

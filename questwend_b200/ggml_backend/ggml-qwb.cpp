@@ -260,6 +260,8 @@ struct MoeRegion {
     ggml_tensor *weights = nullptr;   // [1, n_used, T] normalised routing weights
     ggml_tensor *norm_w = nullptr;    // ffn_norm weight when rms_norm * ffn_norm is absorbed (x: its input)
     ggml_tensor *residual = nullptr;  // the residual add's other operand when the add is absorbed
+    ggml_tensor *sh_g = nullptr, *sh_u = nullptr, *sh_d = nullptr;  // shared expert when absorbed
+    ggml_tensor *sh_gate_inp = nullptr;                               // its sigmoid gate weight, or none
     float norm_eps = 0.f;
     const int32_t *g2s = nullptr;     // gate, up, down tables, consecutive (slot-remap branch)
     int64_t H = 0, F = 0, E = 0, n_used = 0, T = 0;
@@ -434,6 +436,46 @@ bool match_moe(const Uses &u, ggml_tensor *D, MoeRegion &r) {
     }
     if (!f32_contig(r.out) || r.out->ne[0] != r.H || r.out->ne[1] != r.T) return false;
 
+    // the shared expert (runtime.cpp:2825-2833): moe_out + down_sh(silu(gate_sh x) * up_sh x),
+    // the down output optionally times sigmoid(gate_inp_sh x), x the experts' input
+    if (ggml_tensor *sa = u.only(r.out)) {
+        ggml_tensor *sh = is_op(sa, GGML_OP_ADD) ? (sa->src[0] == r.out ? sa->src[1] : sa->src[0]) : nullptr;
+        std::vector<ggml_tensor *> SN;
+        ggml_tensor *gw = nullptr;
+        if (sh && sh != r.out && is_op(sh, GGML_OP_MUL) && is_op(sh->src[1], GGML_OP_UNARY) &&
+            ggml_get_unary_op(sh->src[1]) == GGML_UNARY_OP_SIGMOID) {
+            ggml_tensor *sg = sh->src[1], *gi = sg->src[0];
+            if (is_op(gi, GGML_OP_MUL_MAT) && gi->src[1] == r.x && f32_contig(gi->src[0]) &&
+                ggml_nelements(gi->src[0]) == r.H && u.only(gi) == sg && u.only(sg) == sh) {
+                gw = gi->src[0];
+                SN.insert(SN.end(), {gi, sg, sh});
+                sh = sh->src[0];
+            } else {
+                sh = nullptr;
+            }
+        }
+        ggml_tensor *md = sh && is_op(sh, GGML_OP_MUL_MAT) ? sh : nullptr;
+        ggml_tensor *mu = md ? md->src[1] : nullptr;
+        ggml_tensor *sl = is_op(mu, GGML_OP_MUL) ? mu->src[0] : nullptr;
+        ggml_tensor *mg = is_op(sl, GGML_OP_UNARY) && ggml_get_unary_op(sl) == GGML_UNARY_OP_SILU ? sl->src[0] : nullptr;
+        ggml_tensor *mup = mu ? mu->src[1] : nullptr;
+        if (is_op(mg, GGML_OP_MUL_MAT) && is_op(mup, GGML_OP_MUL_MAT) && mg->src[1] == r.x && mup->src[1] == r.x &&
+            mg->src[0]->type == r.wg->type && mup->src[0]->type == r.wg->type && md->src[0]->type == r.wd->type &&
+            ggml_n_dims(mg->src[0]) == 2 && ggml_n_dims(mup->src[0]) == 2 && ggml_n_dims(md->src[0]) == 2 &&
+            u.only(mg) == sl && u.only(sl) == mu && u.only(mup) == mu && u.only(mu) == md &&
+            (SN.empty() ? u.only(md) == sa : u.only(md) == SN.back()) && f32_contig(sa) &&
+            ggml_are_same_shape(sa, r.out) && !(r.out->flags & GGML_TENSOR_FLAG_OUTPUT)) {
+            r.sh_g = mg->src[0];
+            r.sh_u = mup->src[0];
+            r.sh_d = md->src[0];
+            r.sh_gate_inp = gw;
+            N.insert(N.end(), {mg, mup, sl, mu, md});
+            N.insert(N.end(), SN.begin(), SN.end());
+            N.push_back(sa);
+            r.out = sa;
+        }
+    }
+
     ggml_tensor *head = logits;  // the layer's first node: it reads only inputs from outside
     // ffn_in = rms_norm(cur) * ffn_norm (runtime.cpp:2979) when nothing else reads it (a
     // shared expert does), and l_out = moe_out + cur (:2993): one qwb_moe_ffn call then
@@ -497,6 +539,11 @@ bool match_moe(const Uses &u, ggml_tensor *D, MoeRegion &r) {
     d.up = view_of(r.wu);
     d.down = view_of(r.wd);
     d.H = r.H; d.F = r.F; d.E = r.E; d.n_used = r.n_used; d.T = r.T;
+    if (r.sh_d) {
+        d.shexp_gate = view_of(r.sh_g);
+        d.shexp_up = view_of(r.sh_u);
+        d.shexp_down = view_of(r.sh_d);
+    }
     return qwb_moe_ffn_workspace_size(&d) > 0;
 }
 
@@ -886,6 +933,12 @@ qwb_moe_ffn_desc fused_desc(const MoeRegion &r) {
     d.up = view_of(r.wu);
     d.down = view_of(r.wd);
     d.H = r.H; d.F = r.F; d.E = r.E; d.n_used = r.n_used; d.T = r.T;
+    if (r.sh_d) {
+        d.shexp_gate = view_of(r.sh_g);
+        d.shexp_up = view_of(r.sh_u);
+        d.shexp_down = view_of(r.sh_d);
+        d.shexp_gate_inp = r.sh_gate_inp ? (const float *) r.sh_gate_inp->data : nullptr;
+    }
     return d;
 }
 

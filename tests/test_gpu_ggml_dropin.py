@@ -182,3 +182,24 @@ def test_stock_ggml_cuda_baseline_runs(model):
     e = O.nrmse(got["out"], want["out"])
     print(f"stock ggml-cuda, one layer: nrmse {e:.3e} (Q8_1 activations)")
     assert e <= 2e-2, e
+
+
+@needs
+@pytest.mark.parametrize("T,gate", [(1, True), (4, False)])
+def test_stack_shared_expert_fused_layerwise(install, model, T, gate):
+    # blocks with a shared expert (runtime.cpp:2825-2833): the shared expert's nodes join
+    # the fused qwb_moe_ffn call (its shexp operands), still one call per block
+    H, F, L = model["H"], model["F"], model["L"]
+    r = D.rng(60)
+    sg = D.weights(O.Q4_K, 1, F, H, seed=61)
+    su = D.weights(O.Q4_K, 1, F, H, seed=62)
+    sd = D.weights(O.Q6_K, 1, H, F, seed=63)
+    gi = (r.standard_normal((L, H), dtype=np.float32) * 0.05).astype(np.float32) if gate else None
+    O.stack_set_shexp(sg, su, sd, F, gi)
+    try:
+        x = D.acts((T, H), seed=64 + T)
+        got = layerwise(os.path.join(install, "libggml-cuda-qwb.so"), model, T, x, TOL)
+        fused, own, _, _, _ = got["stats"]
+        assert fused == L and own == 0, got["stats"]
+    finally:
+        O.stack_set_shexp()
