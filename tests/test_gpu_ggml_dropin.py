@@ -194,7 +194,8 @@ def test_stack_shared_expert_fused_layerwise(install, model, T, gate):
     sg = D.weights(O.Q4_K, 1, F, H, seed=61)
     su = D.weights(O.Q4_K, 1, F, H, seed=62)
     sd = D.weights(O.Q6_K, 1, H, F, seed=63)
-    gi = (r.standard_normal((L, H), dtype=np.float32) * 0.05).astype(np.float32) if gate else None
+    # one gate row for every layer: the CPU check of layer l runs a 1-layer stack
+    gi = np.tile((r.standard_normal(H, dtype=np.float32) * 0.05).astype(np.float32), (L, 1)) if gate else None
     O.stack_set_shexp(sg, su, sd, F, gi)
     try:
         x = D.acts((T, H), seed=64 + T)
