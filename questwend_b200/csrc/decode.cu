@@ -529,6 +529,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) gateup_decode_kernel(const 
 }
 
 // ---------------------------------------------------------------- down
+// output rows per down CTA: H / #SMs, at most ceil(8192 / 148)
+constexpr int kDownMaxRows = 56;
+
 // bytes reserved per expert weight span: the CTA's rows plus the 16-byte widening,
 // rounded to 16 mod 128 so consecutive experts start on different shared-memory banks
 __host__ __device__ inline size_t down_span_stride(int n, size_t rb) {
@@ -553,6 +556,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) down_decode_kernel(const Do
     __shared__ int s_slot[32];
     __shared__ float s_w[32];
     __shared__ int s_off[32];  // misalignment of each expert's span
+    __shared__ float s_res[kDownMaxRows];  // the CTA's residual rows, read before the wait
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nu = a.n_used;
     const int64_t h0 = a.H * blockIdx.x / gridDim.x, h1 = a.H * (blockIdx.x + 1) / gridDim.x;
@@ -587,11 +591,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) down_decode_kernel(const Do
             mbar_arrive_expect_tx(&bar[j], 0);
         }
     }
+    // the residual (this layer's input) was complete before the router ran: load it
+    // before waiting on gate/up, off the critical path
+    if (a.residual)
+        for (int r = tid; r < n; r += kDecodeThreads) s_res[r] = a.residual[h0 + r];
     QWB_TRACE(2, 1);
     pdl_trigger();  // the next layer's router may prefetch its rows
     pdl_wait();     // act (gate/up output) is ready
     QWB_TRACE(2, 2);
-    __syncthreads();  // s_off visible
+    __syncthreads();  // s_off, s_res visible
 
     const int li = lane / NSB, ls = lane % NSB;
     bool alive = true;
@@ -645,7 +653,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) down_decode_kernel(const Do
             for (int j = 0; j < nu; ++j)
                 if (s_slot[j] >= 0) acc = fmaf(s_w[j], part[(size_t) j * n + r], acc);
             const int64_t h = h0 + r;
-            a.out[h] = a.residual ? acc + a.residual[h] : acc;
+            a.out[h] = a.residual ? acc + s_res[r] : acc;
         }
     } else if (tid < nu) {
         mbar_wait(&bar[tid], 0);  // drain copies still in flight before the CTA exits
@@ -714,8 +722,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) gateup_pairs_kernel(const P
     __shared__ PairList pl;
     __shared__ int wcnt[kDecodeThreads / 32];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int rb = (int) a.row_bytes, RB = a.batch_rows, F = (int) a.F;
-    const size_t bstride = (size_t) 2 * RB * rb;
+    const int rb = (int) a.row_bytes, F = (int) a.F;
     if (tid == 0) {
         mbar_init(&bar[0], 1);
         mbar_init(&bar[1], 1);
@@ -726,6 +733,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) gateup_pairs_kernel(const P
     const int64_t P = (int64_t) L * F;
     const int64_t p0 = P * blockIdx.x / gridDim.x, p1 = P * (blockIdx.x + 1) / gridDim.x;
     const int n = (int) (p1 - p0);
+    // rows that fit both buffers go out as one batch (fewer, larger bulk copies); more
+    // stream through the two buffers batch_rows at a time
+    const int RB = n <= 2 * a.batch_rows ? max(n, 1) : a.batch_rows;
+    const size_t bstride = (size_t) 2 * RB * rb;
     const int nbat = (n + RB - 1) / RB;
     // batch b: rows [p0 + b RB, ...) into buffer b & 1 (gate rows, then up rows), on bar[b & 1]
     auto issue = [&](int b) {
@@ -827,6 +838,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) down_pairs_kernel(const Pai
     __shared__ PairList pl;
     __shared__ int wcnt[NW];
     __shared__ int s_off[32];
+    __shared__ float s_res[kPairsMaxT * kDownMaxRows];  // residual rows, read before the wait
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = a.group, T = a.pc.T;
     const int64_t h0 = a.H * blockIdx.x / gridDim.x, h1 = a.H * (blockIdx.x + 1) / gridDim.x;
@@ -852,9 +864,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) down_pairs_kernel(const Pai
         }
     };
     issue_group(0);
+    // the residual (this layer's input) was complete before the router ran
+    if (a.residual)
+        for (int idx = tid; idx < T * n; idx += kDecodeThreads)
+            s_res[idx] = a.residual[(int64_t) (idx / n) * a.H + h0 + idx % n];
     pdl_trigger();  // the next layer's router may prefetch its rows
     pdl_wait();     // act (gate/up output) is ready
-    __syncthreads();  // s_off visible
+    __syncthreads();  // s_off, s_res visible
 
     const int li = lane / NSB, ls = lane % NSB;
     const int ngroups = (L + G - 1) / G;
@@ -919,7 +935,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) down_pairs_kernel(const Pai
             for (int c = 0; c < L; ++c)
                 if (pl.tok[c] == t && pl.sd[c] == -2) acc = __fadd_rn(acc, __fmul_rn(part[(size_t) c * n + i], pl.w[c]));
             const int64_t o = (int64_t) t * a.H + h0 + i;
-            a.out[o] = a.residual ? acc + a.residual[o] : acc;
+            a.out[o] = a.residual ? acc + s_res[idx] : acc;
         }
     } else if (tid < G && gi * G + tid < L) {
         mbar_wait(&bar[tid], (uint32_t) (gi & 1));  // drain copies still in flight before the CTA exits
@@ -1049,6 +1065,7 @@ size_t down_decode_smem_bytes(int64_t H, int n_used, size_t row_bytes) {
 
 bool down_decode_supported(int type, int64_t F, int64_t H, size_t row_bytes, size_t nb1, int n_used) {
     if ((type != QWB_TYPE_Q4_K && type != QWB_TYPE_Q6_K) || nb1 != row_bytes) return false;
+    if (ceil_div(H, num_sms()) > kDownMaxRows) return false;
     const int nsb = (int) (F / 256);
     if (nsb != 3 || n_used * nsb > 32) return false;
     return down_decode_smem(H, n_used, nsb, row_bytes) <= 220 * 1024;
