@@ -11,8 +11,12 @@
 // allocates: there is no cudaMalloc, cudaFree or allocating library routine.
 //
 // Contract (also in include/qwb.h):
-//   - the scratch holds at most QWB_NOALLOC_SCRATCH_BYTES; a problem whose workspace
-//     (qwb_mul_mat_id_workspace_size) is larger is rejected with QWB_ERR_LIMIT;
+//   - it always takes the GEMV / weight-streaming kernels, and the scratch holds at most
+//     QWB_NOALLOC_SCRATCH_BYTES: a problem whose workspace for that plan is larger is
+//     rejected with QWB_ERR_LIMIT (qwb_mul_mat_id_workspace_size also plans for the
+//     tensor-core GEMMs, so it can report more for a problem this entry point accepts);
+//   - the address lookup below is cached per device for the life of the process: do not
+//     use this entry point on a device across a cudaDeviceReset of it;
 //   - every call on a device shares the one array and it keeps the previous call's
 //     contents; the kernels write every byte they later read, so nothing needs
 //     clearing between calls, but calls whose executions overlap on the GPU (different
