@@ -671,8 +671,11 @@ def prefill_sweep(q, lib, dev, warmup, iters, cpu=None, tokens=PF_TOKENS, parts=
         assert torch.isfinite(out).all()
         fl = 2.0 * T * K_USED * PF_H * PF_F
         t_ms = float(np.median(tot))
+        # the library's rule: 128-token tcgen05 tiles at >= 256 routed pairs per expert
+        path = ("tcgen05 kind::i8 grouped GEMM" if T * K_USED >= 256 * min(T * K_USED, E)
+                else "int8 tensor cores (mma.sync)")
         q8_points.append({"tokens": T, "shape": "gate_up", "type": "Q8_0", "ms": t_ms,
-                          "tflops": fl / (t_ms * 1e-3) / 1e12, "path": "int8 tensor cores (mma.sync)"})
+                          "tflops": fl / (t_ms * 1e-3) / 1e12, "path": path})
     del W8, q8buf, q8base
     # Q6_K experts, down shape [PF_F -> PF_H] (the Q4_K_M mix's down projections)
     q6base = torch.from_numpy(synth_blocks(Q6_K, PF_UNIQUE * PF_H, PF_F, rng)).to(dev)

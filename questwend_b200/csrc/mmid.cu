@@ -434,7 +434,7 @@ qwb_status plan_mmid(const qwb_tensor *as, const qwb_tensor *b, const qwb_tensor
     } else if (p.pf8 && p.NT == kTc8TileTokens) {
         const int64_t max_tiles = mmid_max_tiles(p.P, p.n_as, p.NT);
         p.btiles = align_up((size_t) max_tiles * tc8_btile_stride(p.K), 256);
-        p.da = align_up((size_t) max_tiles * tc8_da_stride(p.K), 256);
+        p.da = align_up((size_t) max_tiles * tc8_da_stride(p.type, p.K), 256);
     }
     // [0, 256) is the control block of the fused kernels
     p.total = kCtrlBytes + p.planes + p.index + p.btiles + p.da;
@@ -547,7 +547,7 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
         if (p.NT == kTc8TileTokens) {
             uint8_t *bt = (uint8_t *) ws + kCtrlBytes + p.planes + p.index;
             float *bda = (float *) (bt + p.btiles);
-            e = launch_tc8_gather(pl, q.act_dstride, p.K, ix.tiles, ix.n_tiles, ix.max_tiles, ix.pairs,
+            e = launch_tc8_gather(p.type, pl, q.act_dstride, p.K, ix.tiles, ix.n_tiles, ix.max_tiles, ix.pairs,
                                   (int) p.n_used, (int) p.n_b, bt, bda, s);
             if (e != cudaSuccess) return QWB_ERR_CUDA;
             profile_mark(s, QWB_KERNEL_OTHER);

@@ -69,17 +69,17 @@ struct I8PrefillArgs {
 bool pf_i8_eligible(int type, int64_t K, int64_t M, int64_t P, int64_t n_as, const void *W, size_t nb1, size_t nb2);
 int pf_i8_tile_tokens(int type, int64_t P, int64_t n_as);
 cudaError_t launch_pf_i8(int type, int tile_tokens, const I8PrefillArgs &a, cudaStream_t s);
-// Q6_K experts with >= 96 pairs per expert: tcgen05 kind::i8 grouped GEMM (prefill_tc8.cu)
-// over index tiles of up to kTc8TileTokens pairs
+// Q6_K / Q8_0 experts with many pairs per expert: tcgen05 kind::i8 grouped GEMM
+// (prefill_tc8.cu) over index tiles of up to kTc8TileTokens pairs
 constexpr int kTc8TileTokens = 128;
-cudaError_t launch_pf_tc8(const I8PrefillArgs &a, cudaStream_t s);
+cudaError_t launch_pf_tc8(int type, const I8PrefillArgs &a, cudaStream_t s);
 // Bytes per index tile of the gathered activation codes / scales that kernel reads, and
 // the gather (one pass over the tiles after the index is built).
 size_t tc8_btile_stride(int64_t K);
-size_t tc8_da_stride(int64_t K);
-cudaError_t launch_tc8_gather(Q8Planes act, int act_dstride, int64_t K, const int4 *tiles, const int *n_tiles,
-                              int max_tiles, const int *pairs, int n_used, int n_b, uint8_t *btiles, float *bda,
-                              cudaStream_t s);
+size_t tc8_da_stride(int type, int64_t K);
+cudaError_t launch_tc8_gather(int type, Q8Planes act, int act_dstride, int64_t K, const int4 *tiles,
+                              const int *n_tiles, int max_tiles, const int *pairs, int n_used, int n_b,
+                              uint8_t *btiles, float *bda, cudaStream_t s);
 
 void gemv_geometry(GemvArgs &a, int NT, bool glu);
 cudaError_t launch_gemv(int type, bool glu, GemvArgs a, int NT, int max_tiles, cudaStream_t s);

@@ -455,21 +455,20 @@ bool pf_i8_eligible(int type, int64_t K, int64_t M, int64_t P, int64_t n_as, con
     return used > 0 && P >= kI8TNSmall * used;
 }
 
-// Tile size by routed pairs per used expert on average.  Q6_K with >= 96: 128-token tiles
-// on the tcgen05 kernel (prefill_tc8.cu), whose epilogue runs once per 256-element
-// superblock because the sub-block scales ride in the A operand.  Otherwise >= 32: 64-token
-// tiles here, 8 to 31: 8-token tiles here.  Q8_0 stays on this kernel at every size: its
-// rank-1 block scale d_w * d_a changes every 32 K, so a TMEM accumulator needs an epilogue
-// pass (load, scale, add, refill) per 32 K, which costs more than the register
-// accumulators of mma.sync.
+// Tile size by routed pairs per used expert on average: 128-token tiles on the tcgen05
+// kernels (prefill_tc8.cu) for Q6_K from 96 (the sub-block scales ride in the A operand,
+// one epilogue pass per superblock) and for Q8_0 from 256 (one accumulator region per
+// 32-element block; measured on the config-3 gate/up shape, Zipf routing: 190 against 175
+// TOP/s for this file's mma.sync kernel at 512 pairs per expert, 137 against 146 at 128).
+// Otherwise >= 32: 64-token tiles here, 8 to 31: 8-token tiles here.
 int pf_i8_tile_tokens(int type, int64_t P, int64_t n_as) {
     const int64_t used = std::max<int64_t>(1, std::min<int64_t>(P, n_as));
-    if (type == QWB_TYPE_Q6_K && P >= 96 * used) return kTc8TileTokens;
+    if (P >= (type == QWB_TYPE_Q8_0 ? 256 : 96) * used) return kTc8TileTokens;
     return P >= 32 * used ? kI8TNBig : kI8TNSmall;
 }
 
 cudaError_t launch_pf_i8(int type, int tile_tokens, const I8PrefillArgs &a, cudaStream_t s) {
-    if (tile_tokens == kTc8TileTokens) return type == QWB_TYPE_Q6_K ? launch_pf_tc8(a, s) : cudaErrorInvalidValue;
+    if (tile_tokens == kTc8TileTokens) return launch_pf_tc8(type, a, s);
     if (tile_tokens == kI8TNBig)
         return type == QWB_TYPE_Q6_K ? launch_i8_t<QWB_TYPE_Q6_K, kI8TNBig>(a, s)
                                      : launch_i8_t<QWB_TYPE_Q8_0, kI8TNBig>(a, s);

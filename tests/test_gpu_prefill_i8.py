@@ -1,11 +1,12 @@
 """GPU parity: MUL_MAT_ID on Q8_0 and Q6_K experts with many tokens per expert, the
 integer tensor-core kernels:
-  * mma.sync s8 x s8 -> s32 (prefill_i8.cu): one m16n8k32 per Q8_0 block with fp32 block
-    scaling in block order; one m16n8k16 per Q6_K sub-block with its int8 scale in int32
-    and fp32 scaling per superblock (Q8_0 at every size, Q6_K below 96 pairs per expert);
-  * tcgen05.mma kind::i8 (prefill_tc8.cu, Q6_K at >= 96 pairs per expert): the sub-block
-    scales folded into two int8 weight planes, s32 accumulators in tensor memory, fp32
-    scaling per superblock;
+  * mma.sync s8 x s8 -> s32 (prefill_i8.cu, fewer pairs per expert): one m16n8k32 per
+    Q8_0 block with fp32 block scaling in block order; one m16n8k16 per Q6_K sub-block with
+    its int8 scale in int32 and fp32 scaling per superblock;
+  * tcgen05.mma kind::i8 (prefill_tc8.cu, Q6_K from 96 and Q8_0 from 256 pairs per
+    expert): Q6_K with the sub-block scales folded into two int8 weight planes and fp32
+    scaling per superblock; Q8_0 with one s32 tensor-memory accumulator region per
+    32-element block and fp32 scaling per block;
 against the oracle's dots (activations quantized as the CPU backend does: Q8_0 CPU
 variant / Q8_K), against the reference's own ggml CPU backend under skewed routing, and
 against the weight-streaming path on the same inputs.  Bar: nRMS <= 1e-4 (max abs-rel
@@ -79,6 +80,10 @@ CASES = [
     (O.Q6_K, 768, 2048, 8, 256, 4, 4),      # 128 per expert, config-2 down shape
     (O.Q6_K, 2048, 300, 8, 512, 8, 8),      # 512 per expert, rows not a multiple of 128
     (O.Q6_K, 1536, 256, 4, 100, 4, 1),      # 100 per expert: one full and one 28-pair tile each
+    # Q8_0 at >= 256 pairs per used expert: the tcgen05 kernel (one TMEM region per 32-block)
+    (O.Q8_0, 4096, 256, 8, 256, 8, 8),      # 256 per expert, one activation row per (token, slot)
+    (O.Q8_0, 1536, 300, 4, 300, 4, 1),      # 300 per expert: two full and one 44-pair tile each,
+                                            # rows not a multiple of 128
     # 8 to 31 pairs per used expert: 8-token tiles (16-row warps, one 8-token MMA column)
     (O.Q8_0, 1024, 300, 16, 40, 4, 1),      # 10 per expert, partial tiles and row blocks
     (O.Q8_0, 4096, 128, 8, 12, 8, 8),       # 12 per expert, one activation row per pair
@@ -104,7 +109,7 @@ def test_uniform_routing(qwb, t, K, M, n_as, T, n_used, n_b):
     assert e <= TOL, (e, O.max_abs_rel(got, want))
 
 
-@pytest.mark.parametrize("t,T", [(O.Q8_0, 512), (O.Q6_K, 512), (O.Q6_K, 1024)])
+@pytest.mark.parametrize("t,T", [(O.Q8_0, 512), (O.Q8_0, 2048), (O.Q6_K, 512), (O.Q6_K, 1024)])
 def test_zipf_routing_against_reference_build(qwb, t, T):
     K, M, n_as, n_used = 1024, 256, 64, 8
     w = D.weights(t, n_as, M, K, seed=31)
@@ -121,7 +126,7 @@ def test_zipf_routing_against_reference_build(qwb, t, T):
     assert e <= TOL, (e, O.max_abs_rel(got, want))
 
 
-@pytest.mark.parametrize("t,T", [(O.Q8_0, 160), (O.Q6_K, 160), (O.Q8_0, 12), (O.Q6_K, 12)])
+@pytest.mark.parametrize("t,T", [(O.Q8_0, 160), (O.Q8_0, 320), (O.Q6_K, 160), (O.Q8_0, 12), (O.Q6_K, 12)])
 def test_matches_streaming_path(qwb, t, T):
     K, M, n_as, n_used = 1024, 384, 8, 8
     w = D.weights(t, n_as, M, K, seed=51)
