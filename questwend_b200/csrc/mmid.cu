@@ -13,6 +13,9 @@
 //      shared memory behind an mbarrier, two stages deep, and computes R x NT dots from
 //      shared memory (dp4a integer sub-block sums, fp32 scale combine).  Weights are
 //      streamed from HBM once per tile; the grid is persistent (<= SMs x resident CTAs).
+// One token (T == 1, Q4_K / Q6_K): one kernel instead (mmid_one.cu) that reads the ids,
+// copies its rows and quantizes the activation rows it uses meanwhile.  Many tokens per expert take the tensor-core grouped
+// GEMMs (prefill*.cu) after step 2.
 #include <algorithm>
 
 #include "common.cuh"
@@ -485,6 +488,17 @@ qwb_status qwb::mul_mat_id_impl(const qwb_tensor *as, const qwb_tensor *b, const
     profile_mark(s, 0);
     Q8Planes pl = planes_at((char *) ws + kCtrlBytes, p.n_b * p.T, p.K, kq);
     MmidIndex ix = mmid_index_at((char *) ws + kCtrlBytes + p.planes, p.P, p.n_as, p.NT);
+    if (p.T == 1 && !p.pf && !p.pf8 && (uintptr_t) as->data % 16 == 0 && as->nb[2] % 16 == 0 &&
+        mmid_one_supported(p.type, p.K, p.M, (int) p.n_used, (int) p.n_b, as->nb[1])) {
+        // one token: one launch over the rows of its selected experts (no expert index, the
+        // activation rows quantized inside)
+        const cudaError_t e1 = launch_mmid_one(p.type, (const uint8_t *) as->data, as->nb[2], p.M, p.K, p.n_as,
+                                               (const int32_t *) ids->data, (int64_t) (ids->nb[0] / 4), (int) p.n_used,
+                                               (int) p.n_b, (const float *) b->data, (int64_t) (b->nb[1] / 4),
+                                               (float *) dst->data, (int64_t) (dst->nb[1] / 4), st, s);
+        profile_mark(s, QWB_KERNEL_EXPERT_GEMV);
+        return e1 == cudaSuccess ? QWB_OK : QWB_ERR_CUDA;
+    }
     cudaError_t e = launch_quantize_rows(kq ? 0 : 1, (const float *) b->data, (int64_t) (b->nb[1] / 4),
                                          p.n_b * p.T, p.K, nullptr, pl, nullptr, s);
     if (e != cudaSuccess) return QWB_ERR_CUDA;

@@ -81,6 +81,14 @@ cudaError_t launch_tc8_gather(int type, Q8Planes act, int act_dstride, int64_t K
                               const int *n_tiles, int max_tiles, const int *pairs, int n_used, int n_b,
                               uint8_t *btiles, float *bda, cudaStream_t s);
 
+// MUL_MAT_ID of one token (T == 1) on Q4_K / Q6_K experts in one launch (mmid_one.cu): no
+// expert index, no quantizer kernel; each CTA quantizes the activation rows it uses while
+// its slice of the selected experts' rows is copied.  x: f32 activation rows at stride x_s1.
+bool mmid_one_supported(int type, int64_t K, int64_t M, int n_used, int n_b, size_t nb1);
+cudaError_t launch_mmid_one(int type, const uint8_t *W, size_t nb2, int64_t M, int64_t K, int64_t n_as,
+                            const int32_t *ids, int64_t ids_s0, int n_used, int n_b, const float *x, int64_t x_s1,
+                            float *dst, int64_t dst_s1, qwb_status_block *st, cudaStream_t s);
+
 void gemv_geometry(GemvArgs &a, int NT, bool glu);
 cudaError_t launch_gemv(int type, bool glu, GemvArgs a, int NT, int max_tiles, cudaStream_t s);
 int pick_nt(int64_t pairs, int64_t n_as);

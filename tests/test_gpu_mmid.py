@@ -114,3 +114,55 @@ def test_repeat_calls_identical(qwb):
     a1 = qwb.mul_mat_id(W, b, ids).clone()
     a2 = qwb.mul_mat_id(W, b, ids)
     assert torch.equal(a1, a2)
+
+
+# One token (T == 1, Q4_K / Q6_K, K / 256 in {3, 6, 8, 16}): the kernel without an expert
+# index (mmid_one.cu), each CTA's slice of the selected experts' rows copied while the
+# activation row is quantized.  Shapes: the large-model decode MUL_MAT_IDs (hidden 4096,
+# expert FFN 1536: gate/up [4096 -> 1536] with one activation row, down [1536 -> 4096]
+# with one per slot), Q6_K rows (2-byte aligned segments), ranges that split experts.
+ONE_TOKEN = [
+    # type, K, M, n_as, n_used, n_b
+    (O.Q4_K, 4096, 1536, 128, 8, 1),
+    (O.Q4_K, 1536, 4096, 64, 8, 8),
+    (O.Q6_K, 1536, 512, 16, 4, 4),
+    (O.Q6_K, 2048, 300, 8, 6, 2),
+    (O.Q4_K, 4096, 100, 8, 8, 1),
+]
+
+
+@pytest.mark.parametrize("t,K,M,n_as,n_used,n_b", ONE_TOKEN)
+def test_one_token(qwb, t, K, M, n_as, n_used, n_b):
+    qwb.read_status()
+    w = D.weights(t, n_as, M, K, seed=K + M + 3)
+    b = D.acts((1, n_b, K), seed=K + 4)
+    ids = D.rng(K + 5).choice(n_as, n_used, replace=False).astype(np.int32)[None, :]
+    W = qwb.QTensor.from_bytes(w, t, (K, M, n_as))
+    got = qwb.mul_mat_id(W, cu(b), cu(ids)).cpu().numpy()
+    want, rc = O.mul_mat_id(t, w, K, M, n_as, b, ids)
+    assert rc == 0
+    e = O.nrmse(got, want)
+    assert e <= TOL, (e, O.max_abs_rel(got, want))
+    assert qwb.read_status()[0] == 0
+
+
+def test_one_token_bad_id_and_strided_view(qwb):
+    """An id outside the pool gives a zero output row and a QWB_DEVERR_ID_RANGE record; the
+    ids may be a strided view (the argsort row of all experts)."""
+    qwb.read_status()
+    t, K, M, n_as, n_used, E = O.Q4_K, 2048, 384, 16, 4, 16
+    w = D.weights(t, n_as, M, K, seed=71)
+    b = D.acts((1, 1, K), seed=72)
+    full = D.rng(73).permutation(E).astype(np.int32)[None, :]
+    full[0, 2] = n_as + 7
+    view = cu(full)[:, :n_used]
+    W = qwb.QTensor.from_bytes(w, t, (K, M, n_as))
+    got = qwb.mul_mat_id(W, cu(b), view).cpu().numpy()
+    flags, bad, count = qwb.read_status()
+    assert flags & 1 and bad == n_as + 7 and count == 1
+    assert not got[0, 2].any()
+    ok = np.ascontiguousarray(full[:, :n_used]).copy()
+    ok[0, 2] = 0
+    want, _ = O.mul_mat_id(t, w, K, M, n_as, b, ok)
+    for j in (0, 1, 3):
+        assert O.nrmse(got[0, j], want[0, j]) <= TOL
